@@ -1,0 +1,93 @@
+/*
+ * r4q — B200 (sm_100a) decode hot path of rdna4-quant, C ABI.
+ *
+ * Plain pointers and sizes only.  Every pointer argument is a CUDA device
+ * pointer unless stated otherwise; `stream` is a cudaStream_t (NULL = legacy
+ * default stream).  Every call only enqueues work on `stream` and returns a
+ * status: 0 on success, a negative R4Q_ERR_* code otherwise (the message is
+ * available from r4q_last_error()).  No call synchronises the device.
+ *
+ * Data layouts (the reference's runtime layouts, int4_engine_v5.py:95-102):
+ *   INT4 weight   uint8 [N, K/2]   two nibbles per byte, low nibble = even k
+ *   INT4 scales   fp16  [N, K/16]  (scale, zero-as-fp16) pair per 32-block
+ *   INT8 weight   int8  [N, K]     scales fp16 [N, K/32]
+ *   FP16 weight   fp16  [N, K]
+ *   activations   fp16  [B, K] with row stride ldx (elements), outputs [B, N]
+ *   KV cache      uint8 [Hk, max_seq, D] per batch row, FP8 E4M3 bytes of the
+ *                 reference codec (int4_decode_step.hip:47-81)
+ */
+#ifndef R4Q_H
+#define R4Q_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  R4Q_OK = 0,
+  R4Q_ERR_ARG = -1,        /* bad shape / null pointer / unsupported option */
+  R4Q_ERR_ALIGN = -2,      /* pointer or stride misaligned for vector access */
+  R4Q_ERR_CAPACITY = -3,   /* workspace / scratch too small */
+  R4Q_ERR_CUDA = -4,       /* a CUDA runtime call failed */
+  R4Q_ERR_TIMEOUT = -5,    /* a bounded device-side wait gave up */
+};
+
+/* Activation prologue applied inside the GEMV before the dot products. */
+enum {
+  R4Q_PRO_NONE = 0,        /* x as given */
+  R4Q_PRO_FWHT = 1,        /* x <- fp16(H32 x) per 32-block */
+  R4Q_PRO_SILU_FWHT = 2,   /* x <- fp16(H32 (silu(g) * u)); g = x[:, :K], u = x[:, K:2K] */
+};
+
+/* Message of the last failing call on this host thread ("" if none). */
+const char* r4q_last_error(void);
+/* Library version (major*10000 + minor*100 + patch). */
+int r4q_version(void);
+
+/* ---------------------------------------------------------------- GEMV --- */
+/* Bytes of workspace the GEMV entry points need for (B, N, K).  The
+ * workspace must be zero-filled once before its first use; the kernels leave
+ * it zeroed again on exit, so it can be reused by later calls on the same
+ * stream.  Calls that run concurrently need distinct workspaces. */
+size_t r4q_gemv_workspace_bytes(int B, int N, int K);
+
+/* y[b, n] = fp16( sum_k fp16((q[n,k] - z[n,k/32]) * s[n,k/32]) * x'[b, k] )
+ * with fp32 accumulation, x' = prologue(x).  B in 1..16, K % 32 == 0,
+ * N % 16 == 0.  Replaces `gemv_warp<4>`/`launch_gemv`
+ * (int4_decode_step.hip:116-170,230-235) and `dbg_gemv`/`dbg_gemm`
+ * (:3541-3563); the prologue replaces the separate FWHT / SiLU-FWHT kernels
+ * (:1031-1051, :505-557).  ldx, ldy in elements. */
+int r4q_gemv_int4(const void* x, long ldx, const void* w, const void* sz, void* y, long ldy,
+                  int B, int N, int K, int prologue, void* workspace, size_t ws_bytes,
+                  void* stream);
+
+/* INT8 symmetric weights, y = x' @ fp16(q * s)^T.  No kernel in the reference;
+ * its dequant is int8_quant.py:52-69 (dequantize_int8). */
+int r4q_gemv_int8(const void* x, long ldx, const void* w, const void* s, void* y, long ldy,
+                  int B, int N, int K, int prologue, void* workspace, size_t ws_bytes,
+                  void* stream);
+
+/* FP16 weights (fp16 lm_head option). */
+int r4q_gemv_fp16(const void* x, long ldx, const void* w, void* y, long ldy, int B, int N,
+                  int K, int prologue, void* workspace, size_t ws_bytes, void* stream);
+
+/* --------------------------------------------------------- conversions --- */
+/* out[N, K] fp16 = fp16((q - z) * s); bit-exact to `dequant_int4_kernel`
+ * (int4_decode_step.hip:3568-3603) and dequantize_int4_asym
+ * (int4_quant_v2.py:105-127). */
+int r4q_dequant_int4(const void* packed, const void* sz, void* out, int N, int K, void* stream);
+
+/* n fp16 -> n FP8 bytes with the reference encoder; `fp16_to_fp8`
+ * (int4_decode_step.hip:3606-3618). */
+int r4q_fp16_to_fp8(const void* src, void* dst, long n, void* stream);
+
+/* n FP8 bytes -> n fp32 with the reference decoder (int4_decode_step.hip:71-81). */
+int r4q_fp8_to_fp32(const void* src, void* dst, long n, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* R4Q_H */

@@ -1,0 +1,594 @@
+// Dequant-GEMV for the decode path: y[b, n] = sum_k W[n, k] * x'[b, k].
+//
+// Design (B200, HBM-bound matvec):
+//  * every weight byte is read exactly once with 128-bit streaming loads
+//    (ld.global.nc.L1::no_allocate); each thread owns a 16-byte chunk of two
+//    rows (g and g+8 of a 16-row tile), so the dequantised values land directly
+//    in the A-fragment registers of an m16n8k16 tensor-core MMA — no shared
+//    memory round trip for weights;
+//  * nibbles / int8 bytes become fp16 with integer bit tricks (lop3/prmt into
+//    the 0x6400 exponent), then (q - z) and * s in fp16 give exactly the
+//    reference dequant value fp16((q - z) * s); the MMA multiplies those by the
+//    fp16 activations and accumulates in fp32;
+//  * activations are staged once per CTA in shared memory, already permuted
+//    into the order the B fragments need, and the prologue (H32 FWHT, SiLU*up)
+//    is applied while staging — no separate activation kernel;
+//  * the grid is planned to fill all SMs in one wave: 16-row tiles x K splits;
+//    split partials go to an fp32 workspace and the last CTA of a tile sums
+//    them in split order (deterministic), then resets the tile counter.
+//
+// Replaces gemv_warp<4>/launch_gemv (int4_decode_step.hip:116-170,230-235);
+// the reference maps one warp to 4 rows with scalar FMAs.
+#include <cstdarg>
+#include <cstdio>
+#include <mutex>
+#include <unordered_map>
+
+#include "r4q_common.cuh"
+#include "gemv.cuh"
+
+namespace r4q {
+
+constexpr int kWarps = 8;
+constexpr int kThreads = kWarps * 32;
+constexpr int kMaxSplit = 16;
+constexpr int kMaxXSmem = 96 * 1024;
+
+template <int FMT> struct Fmt;
+// INT4: a chunk is 16 bytes of one row = 32 k = one quantisation block.
+template <> struct Fmt<W_INT4> { static constexpr int CK = 32, NSUB = 4, U = 1; };
+// INT8: a chunk is 16 bytes = 16 k (half a block); two chunks per thread-step.
+template <> struct Fmt<W_INT8> { static constexpr int CK = 16, NSUB = 2, U = 2; };
+// FP16: a chunk is 16 bytes = 8 k.
+template <> struct Fmt<W_FP16> { static constexpr int CK = 8, NSUB = 1, U = 2; };
+
+struct GemvParams {
+  const __half* x;
+  long ldx;
+  const uint8_t* w;
+  const __half* s;
+  __half* y;
+  long ldy;
+  int B, N, K;
+  int mt;        // 16-row m-tiles per CTA (1, 2 or 4)
+  int ksplit;    // K splits (gridDim.y)
+  int prologue;
+  unsigned* cnt; // per-row-tile arrival counters (zero between launches)
+  float* part;   // [ksplit][B][N] fp32 partial sums
+};
+
+__host__ __device__ inline int steps_total(int K, int ck, int u) {
+  const int nch = K / ck;
+  return (nch + 4 * u - 1) / (4 * u);
+}
+
+// shared-memory bytes per activation column for a CTA covering `nsteps` steps
+__host__ __device__ inline int x_colstride(int nsteps, int nsub, int u) {
+  int b = nsub * nsteps * 4 * u * 16;
+  b = (b + 127) / 128 * 128 + 64;  // odd multiple of 64: columns g, g+1 hit disjoint banks
+  return b;
+}
+
+// ------------------------------------------------------------ prologue ----
+// Loads 32 activations of column `col` starting at k0, applies the prologue
+// and returns them as fp16 in v[0..31].
+__device__ __forceinline__ void load_block32(const GemvParams& p, int col, int k0, __half (&v)[32]) {
+  const __half* xr = p.x + (long)col * p.ldx;
+  if (k0 >= p.K) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __float2half(0.0f);
+    return;
+  }
+  if (p.prologue == R4Q_PRO_NONE) {
+    const uint4* src = reinterpret_cast<const uint4*>(xr + k0);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      uint4 q = src[i];
+      *reinterpret_cast<uint4*>(&v[8 * i]) = q;
+    }
+    return;
+  }
+  float f[32];
+  if (p.prologue == R4Q_PRO_FWHT) {
+    const uint4* src = reinterpret_cast<const uint4*>(xr + k0);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      uint4 q = src[i];
+      const __half* h = reinterpret_cast<const __half*>(&q);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) f[8 * i + j] = __half2float(h[j]);
+    }
+  } else {  // R4Q_PRO_SILU_FWHT: g = x[:, k], u = x[:, K + k]   (hip:1031-1051)
+    const uint4* sg = reinterpret_cast<const uint4*>(xr + k0);
+    const uint4* su = reinterpret_cast<const uint4*>(xr + p.K + k0);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      uint4 qg = sg[i], qu = su[i];
+      const __half* hg = reinterpret_cast<const __half*>(&qg);
+      const __half* hu = reinterpret_cast<const __half*>(&qu);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        float g = __half2float(hg[j]);
+        f[8 * i + j] = g / (1.0f + expf(-g)) * __half2float(hu[j]);
+      }
+    }
+  }
+  fwht32_regs(f);
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __float2half(f[i]);
+}
+
+// Writes one 32-block of activations into the permuted shared layout.
+// Layout per column: [sub][chunk][16 bytes]; chunk = local chunk index.
+template <int FMT>
+__device__ __forceinline__ void store_block32(uint8_t* xs_col, int nch_pad, int blk_local,
+                                              const __half (&v)[32]) {
+  using F = Fmt<FMT>;
+  auto put = [&](int sub, int chunk, __half a0, __half a1, __half a2, __half a3, __half a4,
+                 __half a5, __half a6, __half a7) {
+    __half t[8] = {a0, a1, a2, a3, a4, a5, a6, a7};
+    *reinterpret_cast<uint4*>(xs_col + ((long)sub * nch_pad + chunk) * 16) =
+        *reinterpret_cast<uint4*>(t);
+  };
+  if constexpr (FMT == W_INT4) {
+    // word m (k = 8m..8m+7) pairs (0,4),(1,5),(2,6),(3,7)
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+      const int b = 8 * m;
+      put(m, blk_local, v[b], v[b + 4], v[b + 1], v[b + 5], v[b + 2], v[b + 6], v[b + 3], v[b + 7]);
+    }
+  } else if constexpr (FMT == W_INT8) {
+    // chunk of 16 k: word m (k = 4m..4m+3) pairs (0,2),(1,3); sub = m / 2
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+#pragma unroll
+      for (int sub = 0; sub < 2; ++sub) {
+        const int b = 16 * c + 8 * sub;
+        put(sub, 2 * blk_local + c, v[b], v[b + 2], v[b + 1], v[b + 3], v[b + 4], v[b + 6],
+            v[b + 5], v[b + 7]);
+      }
+    }
+  } else {
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      const int b = 8 * c;
+      put(0, 4 * blk_local + c, v[b], v[b + 1], v[b + 2], v[b + 3], v[b + 4], v[b + 5], v[b + 6],
+          v[b + 7]);
+    }
+  }
+  (void)F::CK;
+}
+
+// --------------------------------------------------------- dequant math ---
+struct RowChunk {
+  uint4 w;      // 16 weight bytes
+  uint32_t s;   // INT4: (scale, zero) half2;  INT8: scale in the low half
+};
+
+// INT4 word -> 4 half2 of fp16((q - z) * s), pairs (k0,k4),(k1,k5),(k2,k6),(k3,k7)
+__device__ __forceinline__ void deq_int4_word(uint32_t w, __half2 z1024, __half2 nz64, __half2 s2,
+                                              uint32_t (&o)[4]) {
+  const __half2 sixteenth = __float2half2_rn(0.0625f);
+  const uint32_t w8 = w >> 8;
+  __half2 p0 = u32_as_h2(lop3_and_or(w, 0x000F000Fu, 0x64006400u));
+  __half2 p1 = u32_as_h2(lop3_and_or(w, 0x00F000F0u, 0x64006400u));
+  __half2 p2 = u32_as_h2(lop3_and_or(w8, 0x000F000Fu, 0x64006400u));
+  __half2 p3 = u32_as_h2(lop3_and_or(w8, 0x00F000F0u, 0x64006400u));
+  o[0] = h2_as_u32(__hmul2(__hsub2(p0, z1024), s2));
+  o[1] = h2_as_u32(__hmul2(__hfma2(p1, sixteenth, nz64), s2));
+  o[2] = h2_as_u32(__hmul2(__hsub2(p2, z1024), s2));
+  o[3] = h2_as_u32(__hmul2(__hfma2(p3, sixteenth, nz64), s2));
+}
+
+// INT8 word (4 signed bytes k0..k3) -> (k0,k2),(k1,k3) as fp16(q * s)
+__device__ __forceinline__ void deq_int8_word(uint32_t w, __half2 s2, uint32_t& o0, uint32_t& o1) {
+  const __half2 off = __float2half2_rn(1152.0f);
+  const uint32_t wx = w ^ 0x80808080u;
+  __half2 p0 = u32_as_h2(prmt(wx, 0x64646464u, 0x4240u));
+  __half2 p1 = u32_as_h2(prmt(wx, 0x64646464u, 0x4341u));
+  o0 = h2_as_u32(__hmul2(__hsub2(p0, off), s2));
+  o1 = h2_as_u32(__hmul2(__hsub2(p1, off), s2));
+}
+
+template <int FMT, int NG>
+__device__ __forceinline__ void chunk_mma(const RowChunk& ra, const RowChunk& rb,
+                                          const uint8_t* xs, int colstride, int nch_pad,
+                                          int lchunk, const int (&colx)[NG], float (&acc)[NG][4]) {
+  using F = Fmt<FMT>;
+  // activation fragments for this chunk, per column group
+  uint4 xf[NG][F::NSUB];
+#pragma unroll
+  for (int cg = 0; cg < NG; ++cg)
+#pragma unroll
+    for (int sub = 0; sub < F::NSUB; ++sub)
+      xf[cg][sub] = *reinterpret_cast<const uint4*>(xs + (long)colx[cg] * colstride +
+                                                    ((long)sub * nch_pad + lchunk) * 16);
+  if constexpr (FMT == W_INT4) {
+    const __half2 sza = u32_as_h2(ra.s), szb = u32_as_h2(rb.s);
+    const __half2 c1024 = __float2half2_rn(1024.0f), c64 = __float2half2_rn(64.0f);
+    const __half2 za = __high2half2(sza), zb = __high2half2(szb);
+    const __half2 za1024 = __hadd2(za, c1024), zb1024 = __hadd2(zb, c1024);
+    const __half2 nza64 = __hneg2(__hadd2(za, c64)), nzb64 = __hneg2(__hadd2(zb, c64));
+    const __half2 sa = __low2half2(sza), sb = __low2half2(szb);
+    const uint32_t wa[4] = {ra.w.x, ra.w.y, ra.w.z, ra.w.w};
+    const uint32_t wb[4] = {rb.w.x, rb.w.y, rb.w.z, rb.w.w};
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+      uint32_t A[4], Bq[4];
+      deq_int4_word(wa[m], za1024, nza64, sa, A);
+      deq_int4_word(wb[m], zb1024, nzb64, sb, Bq);
+#pragma unroll
+      for (int cg = 0; cg < NG; ++cg) {
+        mma16816(acc[cg], A[0], Bq[0], A[1], Bq[1], xf[cg][m].x, xf[cg][m].y);
+        mma16816(acc[cg], A[2], Bq[2], A[3], Bq[3], xf[cg][m].z, xf[cg][m].w);
+      }
+    }
+  } else if constexpr (FMT == W_INT8) {
+    const __half2 sa = __low2half2(u32_as_h2(ra.s)), sb = __low2half2(u32_as_h2(rb.s));
+    const uint32_t wa[4] = {ra.w.x, ra.w.y, ra.w.z, ra.w.w};
+    const uint32_t wb[4] = {rb.w.x, rb.w.y, rb.w.z, rb.w.w};
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+      uint32_t a0, a1, b0, b1;
+      deq_int8_word(wa[m], sa, a0, a1);
+      deq_int8_word(wb[m], sb, b0, b1);
+#pragma unroll
+      for (int cg = 0; cg < NG; ++cg) {
+        const uint4& q = xf[cg][m >> 1];
+        const uint32_t x0 = (m & 1) ? q.z : q.x;
+        const uint32_t x1 = (m & 1) ? q.w : q.y;
+        mma16816(acc[cg], a0, b0, a1, b1, x0, x1);
+      }
+    }
+  } else {
+#pragma unroll
+    for (int cg = 0; cg < NG; ++cg) {
+      mma16816(acc[cg], ra.w.x, rb.w.x, ra.w.y, rb.w.y, xf[cg][0].x, xf[cg][0].y);
+      mma16816(acc[cg], ra.w.z, rb.w.z, ra.w.w, rb.w.w, xf[cg][0].z, xf[cg][0].w);
+    }
+  }
+}
+
+template <int FMT>
+__device__ __forceinline__ void load_chunk(const GemvParams& p, int row, int chunk, bool valid,
+                                           RowChunk& r) {
+  using F = Fmt<FMT>;
+  if (!valid) {
+    r.w = make_uint4(0, 0, 0, 0);
+    r.s = 0;
+    return;
+  }
+  const long rowbytes = (FMT == W_INT4) ? (p.K >> 1) : (FMT == W_INT8 ? p.K : 2L * p.K);
+  r.w = ldg_stream128(p.w + (long)row * rowbytes + (long)chunk * 16);
+  if constexpr (FMT == W_INT4) {
+    r.s = ldg_stream32(p.s + ((long)row * (p.K >> 5) + chunk) * 2);
+  } else if constexpr (FMT == W_INT8) {
+    const uint16_t sv = __ldg(reinterpret_cast<const unsigned short*>(p.s) +
+                              (long)row * (p.K >> 5) + (chunk >> 1));
+    r.s = sv;
+  } else {
+    r.s = 0;
+  }
+  (void)F::CK;
+}
+
+// --------------------------------------------------------------- kernel ---
+template <int FMT, int NG>
+__global__ void __launch_bounds__(kThreads) gemv_kernel(const GemvParams p) {
+  using F = Fmt<FMT>;
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, t = lane & 3;
+
+  const int nsteps = steps_total(p.K, F::CK, F::U);
+  const int ks = blockIdx.y;
+  const int s0 = (int)((long)ks * nsteps / p.ksplit);
+  const int s1 = (int)((long)(ks + 1) * nsteps / p.ksplit);
+  const int nst = s1 - s0;
+  const int nch_pad = nst * 4 * F::U;           // chunks covered by this CTA (padded)
+  const int chunk0 = s0 * 4 * F::U;             // first global chunk
+  const int nchunks = p.K / F::CK;
+  const int colstride = x_colstride(nst, F::NSUB, F::U);
+  const int ncolx = p.B;
+
+  // ---- main loop: warp -> (m-tile, interleaved steps) ----
+  const int wpm = kWarps / p.mt;
+  const int mt = warp % p.mt, wi = warp / p.mt;
+  const int row0 = blockIdx.x * p.mt * 16 + mt * 16;
+  const bool tile_ok = row0 < p.N;
+  const int row_a = row0 + g, row_b = row0 + g + 8;
+  int colx[NG];
+#pragma unroll
+  for (int cg = 0; cg < NG; ++cg) colx[cg] = min(cg * 8 + g, p.B - 1);
+
+  float acc[NG][4];
+#pragma unroll
+  for (int cg = 0; cg < NG; ++cg)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) acc[cg][i] = 0.0f;
+
+  // first weight chunks are requested before the activations are staged, so
+  // the HBM latency overlaps the prologue
+  RowChunk cur_a[F::U], cur_b[F::U], nxt_a[F::U], nxt_b[F::U];
+  const bool active = tile_ok && wi < nst;
+  if (active) {
+#pragma unroll
+    for (int u = 0; u < F::U; ++u) {
+      const int lc = wi * 4 * F::U + u * 4 + t;
+      const bool v = chunk0 + lc < nchunks;
+      load_chunk<FMT>(p, row_a, chunk0 + lc, v, cur_a[u]);
+      load_chunk<FMT>(p, row_b, chunk0 + lc, v, cur_b[u]);
+    }
+  }
+
+  // ---- stage activations (with prologue) into shared memory ----
+  {
+    const int nblk = nch_pad * F::CK / 32;
+    const int k_base = chunk0 * F::CK;
+    for (int item = tid; item < ncolx * nblk; item += kThreads) {
+      const int col = item / nblk, blk = item - col * nblk;
+      __half v[32];
+      load_block32(p, col, k_base + blk * 32, v);
+      store_block32<FMT>(smem + (long)col * colstride, nch_pad, blk, v);
+    }
+  }
+  __syncthreads();
+
+  if (active) {
+    for (int s = wi; s < nst; s += wpm) {
+      const int sn = s + wpm;
+      if (sn < nst) {
+#pragma unroll
+        for (int u = 0; u < F::U; ++u) {
+          const int lc = sn * 4 * F::U + u * 4 + t;
+          const bool v = chunk0 + lc < nchunks;
+          load_chunk<FMT>(p, row_a, chunk0 + lc, v, nxt_a[u]);
+          load_chunk<FMT>(p, row_b, chunk0 + lc, v, nxt_b[u]);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < F::U; ++u) {
+        const int lc = s * 4 * F::U + u * 4 + t;
+        chunk_mma<FMT, NG>(cur_a[u], cur_b[u], smem, colstride, nch_pad, lc, colx, acc);
+      }
+#pragma unroll
+      for (int u = 0; u < F::U; ++u) {
+        cur_a[u] = nxt_a[u];
+        cur_b[u] = nxt_b[u];
+      }
+    }
+  }
+
+  // ---- reduce the warps that share an m-tile ----
+  __syncthreads();  // activation smem no longer needed: reuse it
+  float* red = reinterpret_cast<float*>(smem);  // [warp][NG*4][32]
+#pragma unroll
+  for (int cg = 0; cg < NG; ++cg)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) red[(warp * NG * 4 + cg * 4 + i) * 32 + lane] = acc[cg][i];
+  __syncthreads();
+
+  __shared__ unsigned s_last;
+  if (wi == 0 && tile_ok) {
+#pragma unroll
+    for (int cg = 0; cg < NG; ++cg)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        float v = 0.0f;
+        for (int j = 0; j < wpm; ++j) v += red[((mt + j * p.mt) * NG * 4 + cg * 4 + i) * 32 + lane];
+        acc[cg][i] = v;
+      }
+    if (p.ksplit == 1) {
+#pragma unroll
+      for (int cg = 0; cg < NG; ++cg) {
+        const int c0 = cg * 8 + 2 * t, c1 = c0 + 1;
+        if (c0 < p.B) {
+          p.y[(long)c0 * p.ldy + row_a] = __float2half(acc[cg][0]);
+          p.y[(long)c0 * p.ldy + row_b] = __float2half(acc[cg][2]);
+        }
+        if (c1 < p.B) {
+          p.y[(long)c1 * p.ldy + row_a] = __float2half(acc[cg][1]);
+          p.y[(long)c1 * p.ldy + row_b] = __float2half(acc[cg][3]);
+        }
+      }
+    } else {
+      float* part = p.part + (long)ks * p.B * p.N;
+#pragma unroll
+      for (int cg = 0; cg < NG; ++cg) {
+        const int c0 = cg * 8 + 2 * t, c1 = c0 + 1;
+        if (c0 < p.B) {
+          part[(long)c0 * p.N + row_a] = acc[cg][0];
+          part[(long)c0 * p.N + row_b] = acc[cg][2];
+        }
+        if (c1 < p.B) {
+          part[(long)c1 * p.N + row_a] = acc[cg][1];
+          part[(long)c1 * p.N + row_b] = acc[cg][3];
+        }
+      }
+    }
+  }
+  if (p.ksplit == 1) return;
+
+  // ---- split-K fixup: the last CTA of this row tile sums partials in order ----
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) {
+    const unsigned old = atomicAdd(&p.cnt[blockIdx.x], 1u);
+    s_last = (old == (unsigned)p.ksplit - 1) ? 1u : 0u;
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  const int trow0 = blockIdx.x * p.mt * 16;
+  const int trows = min(p.mt * 16, p.N - trow0);
+  for (int e = tid; e < trows * p.B; e += kThreads) {
+    const int col = e / trows, r = trow0 + (e - col * trows);
+    float v = 0.0f;
+    for (int k2 = 0; k2 < p.ksplit; ++k2) v += __ldcg(p.part + ((long)k2 * p.B + col) * p.N + r);
+    p.y[(long)col * p.ldy + r] = __float2half(v);
+  }
+  if (tid == 0) p.cnt[blockIdx.x] = 0u;  // leave the workspace zeroed for the next launch
+}
+
+// ------------------------------------------------------------- planning ---
+struct Plan {
+  int mt, ksplit;
+  size_t smem;
+};
+
+template <int FMT, int NG>
+static int occupancy_for(size_t smem) {
+  static std::mutex mu;
+  static std::unordered_map<size_t, int> cache;
+  std::lock_guard<std::mutex> lk(mu);
+  auto it = cache.find(smem);
+  if (it != cache.end()) return it->second;
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaFuncSetAttribute(gemv_kernel<FMT, NG>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         kMaxXSmem + 16384);
+    attr_set = true;
+  }
+  int nb = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, gemv_kernel<FMT, NG>, kThreads, smem) !=
+      cudaSuccess)
+    nb = 1;
+  cache[smem] = nb < 1 ? 1 : nb;
+  return cache[smem];
+}
+
+template <int FMT, int NG>
+static Plan make_plan(int B, int N, int K, size_t ws_bytes) {
+  using F = Fmt<FMT>;
+  const int nsm = num_sms();
+  const int nsteps = steps_total(K, F::CK, F::U);
+  Plan best{1, 1, 0};
+  double best_score = -1.0;
+  for (int mt : {4, 2, 1}) {
+    const int tiles = (N + 16 * mt - 1) / (16 * mt);
+    const int wpm = kWarps / mt;
+    for (int ks = 1; ks <= kMaxSplit && ks <= nsteps; ++ks) {
+      if (ks > 1) {
+        const size_t need = gemv_ws_bytes_for(B, N, ks);
+        if (need > ws_bytes) break;
+      }
+      const int nst = (nsteps + ks - 1) / ks;
+      const size_t xs = (size_t)x_colstride(nst, F::NSUB, F::U) * B;
+      const size_t red = (size_t)kWarps * NG * 4 * 32 * sizeof(float);
+      const size_t smem = xs > red ? xs : red;
+      if (xs > (size_t)kMaxXSmem) continue;
+      const int occ = occupancy_for<FMT, NG>(smem);
+      const long slots = (long)occ * nsm;
+      const long ctas = (long)tiles * ks;
+      const long waves = (ctas + slots - 1) / slots;
+      double eff = (double)ctas / (double)(waves * slots);
+      const double busy = (double)(nsteps / ks) / wpm;  // warps with work
+      if (busy < 1.0) eff *= busy;
+      // prefer fewer splits / bigger tiles on (near) ties
+      const double score = eff - 0.002 * ks - 0.001 * (4 - mt);
+      if (score > best_score) {
+        best_score = score;
+        best = Plan{mt, ks, smem};
+      }
+    }
+  }
+  return best;
+}
+
+template <int FMT, int NG>
+static int launch_gemv_t(const GemvArgs& a) {
+  const Plan pl = make_plan<FMT, NG>(a.B, a.N, a.K, a.ws_bytes);
+  GemvParams p;
+  p.x = reinterpret_cast<const __half*>(a.x);
+  p.ldx = a.ldx;
+  p.w = reinterpret_cast<const uint8_t*>(a.w);
+  p.s = reinterpret_cast<const __half*>(a.s);
+  p.y = reinterpret_cast<__half*>(a.y);
+  p.ldy = a.ldy;
+  p.B = a.B;
+  p.N = a.N;
+  p.K = a.K;
+  p.mt = pl.mt;
+  p.ksplit = pl.ksplit;
+  p.prologue = a.prologue;
+  p.cnt = reinterpret_cast<unsigned*>(a.ws);
+  p.part = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(a.ws) + gemv_cnt_bytes(a.N));
+  if (pl.ksplit > 1 && a.ws == nullptr)
+    return set_error(R4Q_ERR_CAPACITY, "gemv: workspace required for N=%d K=%d", a.N, a.K);
+  dim3 grid((a.N + 16 * pl.mt - 1) / (16 * pl.mt), pl.ksplit);
+  gemv_kernel<FMT, NG><<<grid, kThreads, pl.smem, a.stream>>>(p);
+  return check_launch("gemv_kernel");
+}
+
+size_t gemv_cnt_bytes(int N) { return ((size_t)(N + 15) / 16 * 4 + 255) / 256 * 256; }
+size_t gemv_ws_bytes_for(int B, int N, int ksplit) {
+  return gemv_cnt_bytes(N) + (size_t)ksplit * B * N * sizeof(float);
+}
+
+int gemv_validate(const GemvArgs& a, int fmt) {
+  if (!a.x || !a.w || !a.y || (fmt != W_FP16 && !a.s))
+    return set_error(R4Q_ERR_ARG, "gemv: null pointer");
+  if (a.B < 1 || a.B > 16) return set_error(R4Q_ERR_ARG, "gemv: B=%d outside 1..16", a.B);
+  if (a.N <= 0 || a.N % 16) return set_error(R4Q_ERR_ARG, "gemv: N=%d must be a positive multiple of 16", a.N);
+  if (a.K <= 0 || a.K % 32) return set_error(R4Q_ERR_ARG, "gemv: K=%d must be a positive multiple of 32", a.K);
+  if (a.prologue < R4Q_PRO_NONE || a.prologue > R4Q_PRO_SILU_FWHT)
+    return set_error(R4Q_ERR_ARG, "gemv: unknown prologue %d", a.prologue);
+  const long kin = (a.prologue == R4Q_PRO_SILU_FWHT) ? 2L * a.K : a.K;
+  if (a.B > 1 && a.ldx < kin) return set_error(R4Q_ERR_ARG, "gemv: ldx=%ld < %ld", a.ldx, kin);
+  if (a.B > 1 && a.ldy < a.N) return set_error(R4Q_ERR_ARG, "gemv: ldy=%ld < N", a.ldy);
+  if (!aligned(a.x, 16) || (a.ldx % 8)) return set_error(R4Q_ERR_ALIGN, "gemv: x must be 16-byte aligned with ldx % 8 == 0");
+  if (!aligned(a.w, 16)) return set_error(R4Q_ERR_ALIGN, "gemv: weights must be 16-byte aligned");
+  if (fmt == W_INT4 && !aligned(a.s, 4)) return set_error(R4Q_ERR_ALIGN, "gemv: scales must be 4-byte aligned");
+  if (fmt == W_INT8 && !aligned(a.s, 2)) return set_error(R4Q_ERR_ALIGN, "gemv: scales must be 2-byte aligned");
+  if (!aligned(a.y, 2)) return set_error(R4Q_ERR_ALIGN, "gemv: y misaligned");
+  return R4Q_OK;
+}
+
+int launch_gemv(const GemvArgs& a, int fmt) {
+  int st = gemv_validate(a, fmt);
+  if (st) return st;
+  const bool two = a.B > 8;
+  switch (fmt) {
+    case W_INT4: return two ? launch_gemv_t<W_INT4, 2>(a) : launch_gemv_t<W_INT4, 1>(a);
+    case W_INT8: return two ? launch_gemv_t<W_INT8, 2>(a) : launch_gemv_t<W_INT8, 1>(a);
+    case W_FP16: return two ? launch_gemv_t<W_FP16, 2>(a) : launch_gemv_t<W_FP16, 1>(a);
+  }
+  return set_error(R4Q_ERR_ARG, "gemv: unknown weight format %d", fmt);
+}
+
+}  // namespace r4q
+
+// ------------------------------------------------------------------ C ABI --
+using namespace r4q;
+
+extern "C" size_t r4q_gemv_workspace_bytes(int B, int N, int K) {
+  (void)K;
+  if (B < 1) B = 1;
+  if (N < 16) N = 16;
+  return gemv_ws_bytes_for(B, N, kMaxSplit);
+}
+
+static GemvArgs mk(const void* x, long ldx, const void* w, const void* s, void* y, long ldy, int B,
+                   int N, int K, int prologue, void* ws, size_t wsb, void* stream) {
+  GemvArgs a;
+  a.x = x; a.ldx = ldx; a.w = w; a.s = s; a.y = y; a.ldy = ldy;
+  a.B = B; a.N = N; a.K = K; a.prologue = prologue;
+  a.ws = ws; a.ws_bytes = ws ? wsb : 0;
+  a.stream = reinterpret_cast<cudaStream_t>(stream);
+  return a;
+}
+
+extern "C" int r4q_gemv_int4(const void* x, long ldx, const void* w, const void* sz, void* y,
+                             long ldy, int B, int N, int K, int prologue, void* ws, size_t wsb,
+                             void* stream) {
+  return launch_gemv(mk(x, ldx, w, sz, y, ldy, B, N, K, prologue, ws, wsb, stream), W_INT4);
+}
+extern "C" int r4q_gemv_int8(const void* x, long ldx, const void* w, const void* s, void* y,
+                             long ldy, int B, int N, int K, int prologue, void* ws, size_t wsb,
+                             void* stream) {
+  return launch_gemv(mk(x, ldx, w, s, y, ldy, B, N, K, prologue, ws, wsb, stream), W_INT8);
+}
+extern "C" int r4q_gemv_fp16(const void* x, long ldx, const void* w, void* y, long ldy, int B,
+                             int N, int K, int prologue, void* ws, size_t wsb, void* stream) {
+  return launch_gemv(mk(x, ldx, w, nullptr, y, ldy, B, N, K, prologue, ws, wsb, stream), W_FP16);
+}

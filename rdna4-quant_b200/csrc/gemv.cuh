@@ -1,0 +1,29 @@
+// Internal GEMV launcher interface shared by the C ABI and the decode step.
+#pragma once
+#include <cuda_runtime.h>
+#include <stddef.h>
+
+namespace r4q {
+
+enum WFmt { W_INT4 = 0, W_INT8 = 1, W_FP16 = 2 };
+
+struct GemvArgs {
+  const void* x;
+  long ldx;
+  const void* w;
+  const void* s;
+  void* y;
+  long ldy;
+  int B, N, K;
+  int prologue;
+  void* ws;
+  size_t ws_bytes;
+  cudaStream_t stream;
+};
+
+size_t gemv_cnt_bytes(int N);
+size_t gemv_ws_bytes_for(int B, int N, int ksplit);
+int gemv_validate(const GemvArgs& a, int fmt);
+int launch_gemv(const GemvArgs& a, int fmt);
+
+}  // namespace r4q

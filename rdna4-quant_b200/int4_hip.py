@@ -1,0 +1,41 @@
+"""Drop-in for the reference's native module ``int4_hip``
+(hip_int4/int4_decode_step.hip:3620-3636), running on B200 through libr4q.so.
+
+Same function names, argument order, tensor layouts and return shapes as the
+reference pybind module; the reference engine (int4_engine_v5.py) imports it
+with ``import int4_hip`` after putting this folder on ``sys.path``.  Unlike the
+reference, failures raise ``r4q.lib.R4QError`` instead of returning silently.
+"""
+from __future__ import annotations
+
+import torch
+
+from r4q import ops as _ops
+
+
+def dbg_gemv(X: torch.Tensor, W: torch.Tensor, S: torch.Tensor, N: int, K: int) -> torch.Tensor:
+    """INT4 asym GEMV, X fp16 [K] -> Y fp16 [N] (int4_decode_step.hip:3541-3550)."""
+    return _ops.gemv('int4', X.reshape(1, K), W, S, int(N), int(K)).reshape(int(N))
+
+
+def dbg_gemm(X: torch.Tensor, W: torch.Tensor, S: torch.Tensor, M: int, N: int, K: int) -> torch.Tensor:
+    """Batched INT4 GEMV, X fp16 [M, K] -> Y fp16 [M, N] (int4_decode_step.hip:3552-3563).
+    Batches above 16 rows are processed 16 rows per launch."""
+    M, N, K = int(M), int(N), int(K)
+    X2 = X.reshape(M, K)
+    Y = torch.empty(M, N, dtype=torch.float16, device=X.device)
+    for r in range(0, M, 16):
+        _ops.gemv('int4', X2[r:r + 16], W, S, N, K, out=Y[r:r + 16])
+    return Y
+
+
+def dequant_int4(packed: torch.Tensor, scales: torch.Tensor, N: int, K: int) -> torch.Tensor:
+    """[N, K/2] u8 + [N, K/16] interleaved (scale, zero) fp16 -> [N, K] fp16,
+    bit-exact (int4_decode_step.hip:3568-3603)."""
+    return _ops.dequant_int4(packed, scales, int(N), int(K))
+
+
+def fp16_to_fp8(src: torch.Tensor) -> torch.Tensor:
+    """fp16 tensor -> uint8 tensor of the same shape, reference E4M3 encoder
+    (int4_decode_step.hip:3606-3618)."""
+    return _ops.fp16_to_fp8(src)

@@ -1,0 +1,70 @@
+"""ctypes binding of libr4q.so (the C ABI in include/r4q.h).
+
+Every wrapper raises ``R4QError`` on a non-zero status, with the library's
+message.  There is deliberately no fallback path: a missing library is an
+import error.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+from pathlib import Path
+
+_PKG = Path(__file__).resolve().parent.parent
+_SO = Path(os.environ.get("R4Q_LIB", _PKG / "libr4q.so"))
+
+
+class R4QError(RuntimeError):
+    def __init__(self, code: int, what: str, msg: str):
+        super().__init__(f"{what} failed with r4q status {code}: {msg}")
+        self.code = code
+
+
+def _load():
+    if not _SO.exists():
+        raise ImportError(
+            f"libr4q.so not found at {_SO}: build it with `python -m r4q.build` "
+            "(or __graft_entry__.build()); r4q has no CPU fallback")
+    try:  # make sure torch's CUDA runtime is loaded first so both share it
+        import torch  # noqa: F401
+    except Exception:
+        pass
+    return C.CDLL(str(_SO))
+
+
+LIB = _load()
+vp, i32, i64, sz_t, f32 = C.c_void_p, C.c_int, C.c_long, C.c_size_t, C.c_float
+
+_SIGS = {
+    "r4q_last_error": (C.c_char_p, []),
+    "r4q_version": (i32, []),
+    "r4q_gemv_workspace_bytes": (sz_t, [i32, i32, i32]),
+    "r4q_gemv_int4": (i32, [vp, i64, vp, vp, vp, i64, i32, i32, i32, i32, vp, sz_t, vp]),
+    "r4q_gemv_int8": (i32, [vp, i64, vp, vp, vp, i64, i32, i32, i32, i32, vp, sz_t, vp]),
+    "r4q_gemv_fp16": (i32, [vp, i64, vp, vp, i64, i32, i32, i32, i32, vp, sz_t, vp]),
+    "r4q_dequant_int4": (i32, [vp, vp, vp, i32, i32, vp]),
+    "r4q_fp16_to_fp8": (i32, [vp, vp, i64, vp]),
+    "r4q_fp8_to_fp32": (i32, [vp, vp, i64, vp]),
+}
+
+EXPORTS = []
+for _name, (_res, _args) in _SIGS.items():
+    if hasattr(LIB, _name):
+        _f = getattr(LIB, _name)
+        _f.restype = _res
+        _f.argtypes = _args
+        EXPORTS.append(_name)
+
+
+def last_error() -> str:
+    return LIB.r4q_last_error().decode(errors="replace")
+
+
+def call(name: str, *args) -> None:
+    st = getattr(LIB, name)(*args)
+    if st != 0:
+        raise R4QError(st, name, last_error())
+
+
+# activation prologues (enum in include/r4q.h)
+PRO_NONE, PRO_FWHT, PRO_SILU_FWHT = 0, 1, 2

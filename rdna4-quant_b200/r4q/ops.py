@@ -1,0 +1,101 @@
+"""Torch-tensor front end over the C ABI: shape checks, output allocation,
+per-(device, stream) GEMV workspaces.  Device memory and streams come from
+PyTorch; all arithmetic runs in libr4q.so."""
+from __future__ import annotations
+
+import threading
+
+import torch
+
+from . import lib as L
+
+_ws_lock = threading.Lock()
+_ws: dict = {}
+
+
+def stream_handle(dev: torch.device) -> int:
+    return torch.cuda.current_stream(dev).cuda_stream
+
+
+def _require_cuda(*ts: torch.Tensor) -> torch.device:
+    dev = ts[0].device
+    for t in ts:
+        if not t.is_cuda:
+            raise ValueError("r4q ops take CUDA tensors only (no CPU fallback)")
+        if t.device != dev:
+            raise ValueError("all tensors must be on the same device")
+    return dev
+
+
+def gemv_workspace(dev: torch.device, B: int, N: int, K: int) -> torch.Tensor:
+    """Zero-filled workspace for GEMV split-K partials, cached per
+    (device, stream).  The kernels leave it zeroed after every call."""
+    need = int(L.LIB.r4q_gemv_workspace_bytes(B, N, K))
+    key = (dev.index, stream_handle(dev))
+    with _ws_lock:
+        cur = _ws.get(key)
+        if cur is None or cur.numel() < need:
+            cur = torch.zeros(max(need, 1 << 20), dtype=torch.uint8, device=dev)
+            _ws[key] = cur
+    return cur
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def gemv(fmt: str, x: torch.Tensor, w: torch.Tensor, s: torch.Tensor | None, N: int, K: int,
+         prologue: int = L.PRO_NONE, out: torch.Tensor | None = None) -> torch.Tensor:
+    """y[B, N] = prologue(x)[B, K] @ dequant(W)^T for fmt in {'int4','int8','fp16'}."""
+    dev = _require_cuda(x, w)
+    if x.dtype != torch.float16:
+        raise TypeError("x must be float16")
+    x2 = x.reshape(-1, x.shape[-1])
+    if x2.stride(-1) != 1:
+        x2 = x2.contiguous()
+    B = x2.shape[0]
+    kin = 2 * K if prologue == L.PRO_SILU_FWHT else K
+    if x2.shape[1] < kin:
+        raise ValueError(f"x has {x2.shape[1]} columns, need {kin}")
+    if out is None:
+        out = torch.empty(B, N, dtype=torch.float16, device=dev)
+    ws = gemv_workspace(dev, B, N, K)
+    st = stream_handle(dev)
+    ldx = x2.stride(0) if B > 1 else kin
+    ldy = out.stride(0) if B > 1 else N
+    if fmt == 'int4':
+        L.call("r4q_gemv_int4", x2.data_ptr(), ldx, w.data_ptr(), s.data_ptr(), out.data_ptr(),
+               ldy, B, N, K, prologue, ws.data_ptr(), ws.numel(), st)
+    elif fmt == 'int8':
+        L.call("r4q_gemv_int8", x2.data_ptr(), ldx, w.data_ptr(), s.data_ptr(), out.data_ptr(),
+               ldy, B, N, K, prologue, ws.data_ptr(), ws.numel(), st)
+    elif fmt == 'fp16':
+        L.call("r4q_gemv_fp16", x2.data_ptr(), ldx, w.data_ptr(), out.data_ptr(), ldy, B, N, K,
+               prologue, ws.data_ptr(), ws.numel(), st)
+    else:
+        raise ValueError(fmt)
+    return out
+
+
+def dequant_int4(packed: torch.Tensor, sz: torch.Tensor, N: int, K: int) -> torch.Tensor:
+    dev = _require_cuda(packed, sz)
+    out = torch.empty(N, K, dtype=torch.float16, device=dev)
+    L.call("r4q_dequant_int4", packed.data_ptr(), sz.data_ptr(), out.data_ptr(), N, K,
+           stream_handle(dev))
+    return out
+
+
+def fp16_to_fp8(src: torch.Tensor) -> torch.Tensor:
+    dev = _require_cuda(src)
+    s = src.contiguous()
+    out = torch.empty(s.shape, dtype=torch.uint8, device=dev)
+    L.call("r4q_fp16_to_fp8", s.data_ptr(), out.data_ptr(), s.numel(), stream_handle(dev))
+    return out
+
+
+def fp8_to_fp32(src: torch.Tensor) -> torch.Tensor:
+    dev = _require_cuda(src)
+    s = src.contiguous()
+    out = torch.empty(s.shape, dtype=torch.float32, device=dev)
+    L.call("r4q_fp8_to_fp32", s.data_ptr(), out.data_ptr(), s.numel(), stream_handle(dev))
+    return out

@@ -1,0 +1,198 @@
+"""GPU parity of the GEMV family and the format conversions against the CPU
+oracle.  Tolerance (written here, from the north-star spec): outputs within
+1e-3 relative — max |y - y_ref| <= 1e-3 * max |y_ref| and
+||y - y_ref||_2 <= 1e-3 * ||y_ref||_2.  Dequant and FP8 are bit-exact."""
+import numpy as np
+import pytest
+import torch
+
+import r4q_oracle as O
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-3
+
+
+def close(y, ref, tol=TOL):
+    y = np.asarray(y, np.float64)
+    ref = np.asarray(ref, np.float64)
+    assert np.isfinite(y).all()
+    err = np.abs(y - ref)
+    assert err.max() <= tol * np.abs(ref).max() + 1e-6, (err.max(), np.abs(ref).max())
+    assert np.linalg.norm(y - ref) <= tol * np.linalg.norm(ref) + 1e-6
+
+
+def make_int4(rng, N, K, outliers=True):
+    W = rng.standard_normal((N, K)).astype(np.float32) * 0.02
+    if outliers:
+        m = rng.random((N, K)) < 0.001
+        W[m] *= 20
+    W = O.rotate_blocks(W).astype(np.float32)
+    q, s, z = O.quantize_int4_asym(W.reshape(N, K // 32, 32))
+    return O.pack_int4(q.reshape(N, K)), O.interleave_scale_zero(s, z)
+
+
+def cuda(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+@pytest.fixture(scope="module")
+def ops():
+    from r4q import ops
+    return ops
+
+
+SHAPES = [(5120, 5120), (1024, 5120), (7168, 5120), (5120, 17408), (256, 96), (48, 64), (160, 2176)]
+
+
+@pytest.mark.parametrize("N,K", SHAPES)
+@pytest.mark.parametrize("B", [1, 4, 16])
+def test_gemv_int4(ops, N, K, B):
+    rng = np.random.default_rng(N * 7 + K + B)
+    packed, sz = make_int4(rng, N, K)
+    x = rng.standard_normal((B, K)).astype(np.float16)
+    y = ops.gemv('int4', cuda(x), cuda(packed), cuda(sz), N, K).cpu().numpy()
+    close(y, O.gemv_int4(x, packed, sz))
+    # also within tolerance of the reference kernel's blockwise arithmetic
+    close(y, O.gemv_int4_blockwise(x, packed, sz), 2e-3)
+
+
+@pytest.mark.parametrize("B", [1, 3, 8, 9])
+def test_gemv_int4_odd_batches(ops, B):
+    rng = np.random.default_rng(B)
+    N, K = 512, 1024
+    packed, sz = make_int4(rng, N, K)
+    x = rng.standard_normal((B, K)).astype(np.float16)
+    y = ops.gemv('int4', cuda(x), cuda(packed), cuda(sz), N, K).cpu().numpy()
+    close(y, O.gemv_int4(x, packed, sz))
+
+
+@pytest.mark.parametrize("B", [1, 4])
+def test_gemv_prologue_fwht(ops, B):
+    from r4q import lib as L
+    rng = np.random.default_rng(11)
+    N, K = 1024, 5120
+    packed, sz = make_int4(rng, N, K)
+    x = rng.standard_normal((B, K)).astype(np.float16)
+    y = ops.gemv('int4', cuda(x), cuda(packed), cuda(sz), N, K, prologue=L.PRO_FWHT).cpu().numpy()
+    xr = O.fwht32(x.astype(np.float32)).astype(np.float16)
+    close(y, O.gemv_int4(xr, packed, sz))
+
+
+@pytest.mark.parametrize("B", [1, 16])
+def test_gemv_prologue_silu_fwht(ops, B):
+    from r4q import lib as L
+    rng = np.random.default_rng(12)
+    N, K = 512, 2176
+    packed, sz = make_int4(rng, N, K)
+    gu = (rng.standard_normal((B, 2 * K)) * 2).astype(np.float16)
+    y = ops.gemv('int4', cuda(gu), cuda(packed), cuda(sz), N, K,
+                 prologue=L.PRO_SILU_FWHT).cpu().numpy()
+    xr = O.silu_fwht(gu[:, :K], gu[:, K:])
+    close(y, O.gemv_int4(xr, packed, sz))
+
+
+@pytest.mark.parametrize("N,K", [(5120, 5120), (1024, 17408), (96, 64)])
+@pytest.mark.parametrize("B", [1, 16])
+def test_gemv_int8(ops, N, K, B):
+    rng = np.random.default_rng(N + K + B + 1)
+    W = O.rotate_blocks(rng.standard_normal((N, K)) * 0.02).astype(np.float32)
+    q, s = O.quantize_int8_sym(W.reshape(N, K // 32, 32))
+    q = q.reshape(N, K)
+    x = rng.standard_normal((B, K)).astype(np.float16)
+    y = ops.gemv('int8', cuda(x), cuda(q), cuda(s), N, K).cpu().numpy()
+    close(y, O.gemv_int8(x, q, s))
+
+
+@pytest.mark.parametrize("N,K", [(4096, 5120), (64, 96)])
+@pytest.mark.parametrize("B", [1, 5])
+def test_gemv_fp16(ops, N, K, B):
+    rng = np.random.default_rng(N + K + B + 2)
+    W = (rng.standard_normal((N, K)) * 0.02).astype(np.float16)
+    x = rng.standard_normal((B, K)).astype(np.float16)
+    y = ops.gemv('fp16', cuda(x), cuda(W), None, N, K).cpu().numpy()
+    close(y, O.gemv_fp16(x, W))
+
+
+def test_gemv_workspace_left_zero_and_repeatable(ops):
+    rng = np.random.default_rng(5)
+    N, K = 1024, 5120                       # small N -> split-K path
+    packed, sz = make_int4(rng, N, K)
+    x = cuda(rng.standard_normal((1, K)).astype(np.float16))
+    w, s = cuda(packed), cuda(sz)
+    y1 = ops.gemv('int4', x, w, s, N, K)
+    y2 = ops.gemv('int4', x, w, s, N, K)
+    torch.cuda.synchronize()
+    assert torch.equal(y1, y2)              # deterministic split-K merge
+    ws = ops.gemv_workspace(x.device, 1, N, K)
+    cnt_bytes = ((N + 15) // 16 * 4 + 255) // 256 * 256
+    assert int(ws[:cnt_bytes].count_nonzero()) == 0
+
+
+def test_dequant_bit_exact(ops):
+    import int4_hip
+    rng = np.random.default_rng(3)
+    for N, K in [(5120, 5120), (64, 32), (17, 96)]:
+        packed, sz = make_int4(rng, N, K)
+        out = int4_hip.dequant_int4(cuda(packed), cuda(sz), N, K).cpu().numpy()
+        ref = O.dequant_int4_runtime(packed, sz)
+        assert np.array_equal(out.view(np.uint16), ref.view(np.uint16))
+
+
+def test_fp8_encoder_exhaustive_fp16(ops):
+    import int4_hip
+    allh = np.arange(65536, dtype=np.uint16).view(np.float16)
+    got = int4_hip.fp16_to_fp8(cuda(allh)).cpu().numpy()
+    ref = O.fp8_encode(allh.astype(np.float32))
+    assert np.array_equal(got, ref)
+    # odd length / unaligned tail path
+    got2 = int4_hip.fp16_to_fp8(cuda(allh[1:1000])).cpu().numpy()
+    assert np.array_equal(got2, ref[1:1000])
+
+
+def test_fp8_encoder_float32_sweep(ops):
+    """Device encoder on fp32 inputs around every rounding boundary."""
+    from r4q import ops as P
+    rng = np.random.default_rng(9)
+    v = np.concatenate([rng.standard_normal(1 << 16) * s for s in (1e-3, 1e-1, 1, 30, 300)])
+    v = v.astype(np.float16)
+    got = P.fp16_to_fp8(cuda(v)).cpu().numpy()
+    assert np.array_equal(got, O.fp8_encode(v.astype(np.float32)))
+
+
+def test_fp8_decoder_all_bytes(ops):
+    allb = np.arange(256, dtype=np.uint8)
+    got = ops.fp8_to_fp32(cuda(allb)).cpu().numpy()
+    ref = O.fp8_decode(allb)
+    assert np.array_equal(got.view(np.uint32), ref.view(np.uint32))
+
+
+def test_reference_test_gemv_vs_pytorch(ops):
+    """The reference's own GEMV test (tests/test_kernels.py:129-171): N=K=5120,
+    seed 42, unrotated W ~ N(0,1), asym INT4; its bar is cos > 0.99 against
+    dequant-then-matmul.  Here the same data must also meet the 1e-3 bar."""
+    import int4_hip
+    torch.manual_seed(42)
+    N = K = 5120
+    W = torch.randn(N, K, dtype=torch.float32).numpy()
+    q, s, z = O.quantize_int4_asym(W.reshape(N, K // 32, 32))
+    packed = O.pack_int4(q.reshape(N, K))
+    sz = O.interleave_scale_zero(s, z)
+    x = torch.randn(1, K, dtype=torch.float16).numpy()
+    y = int4_hip.dbg_gemv(cuda(x[0]), cuda(packed), cuda(sz), N, K).cpu().numpy()
+    ref = O.gemv_int4(x, packed, sz)[0]
+    cos = float(np.dot(y.astype(np.float64), ref) / (np.linalg.norm(y) * np.linalg.norm(ref)))
+    assert cos > 0.99
+    close(y, ref)
+    # dbg_gemm with M > 16 rows
+    X = torch.randn(20, K, dtype=torch.float16).numpy()
+    Y = int4_hip.dbg_gemm(cuda(X), cuda(packed), cuda(sz), 20, N, K).cpu().numpy()
+    close(Y, O.gemv_int4(X, packed, sz))
+
+
+def test_bad_arguments_raise(ops):
+    from r4q.lib import R4QError
+    x = torch.zeros(1, 48, dtype=torch.float16, device='cuda')
+    w = torch.zeros(64, 24, dtype=torch.uint8, device='cuda')
+    s = torch.zeros(64, 3, dtype=torch.float16, device='cuda')
+    with pytest.raises(R4QError):
+        ops.gemv('int4', x, w, s, 64, 48)
