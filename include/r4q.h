@@ -40,7 +40,29 @@ enum {
   R4Q_PRO_NONE = 0,        /* x as given */
   R4Q_PRO_FWHT = 1,        /* x <- fp16(H32 x) per 32-block */
   R4Q_PRO_SILU_FWHT = 2,   /* x <- fp16(H32 (silu(g) * u)); g = x[:, :K], u = x[:, K:2K] */
+  R4Q_PRO_RMSNORM_FWHT = 3,/* x <- fp16(H32 (x * rrms * norm_w)), rrms = rsqrt(ss/K + eps) */
 };
+
+/* Weight formats for r4q_gemv(). */
+enum { R4Q_W_INT4 = 0, R4Q_W_INT8 = 1, R4Q_W_FP16 = 2 };
+
+/* Optional fusions of r4q_gemv().  RMSNorm prologue: ss = sum of squares per
+ * activation row, taken from `ss_in` ([ss_in_parts][B] partial sums, summed in
+ * order) when given, else computed from the fp16 x.  Residual epilogue:
+ * y = fp16(fp16(acc) + residual); when `ss_out` is given it receives, per
+ * 16-row output tile and row b, the sum of squares of the unrounded sums
+ * ([N/16][B]) — exactly the `ss_in` of a following RMSNorm prologue.  This is
+ * fused_res_norm_fwht (int4_decode_step.hip:1143-1192) split across the two
+ * GEMVs around it. */
+typedef struct r4q_gemv_fused {
+  const void* norm_w;     /* fp16 [K] */
+  float eps;
+  const float* ss_in;
+  int ss_in_parts;
+  const void* residual;   /* fp16 [B, ldres] or NULL; may alias y */
+  long ldres;
+  float* ss_out;          /* fp32 [N/16][B] or NULL */
+} r4q_gemv_fused;
 
 /* Message of the last failing call on this host thread ("" if none). */
 const char* r4q_last_error(void);
@@ -73,6 +95,12 @@ int r4q_gemv_int8(const void* x, long ldx, const void* w, const void* s, void* y
 /* FP16 weights (fp16 lm_head option). */
 int r4q_gemv_fp16(const void* x, long ldx, const void* w, void* y, long ldy, int B, int N,
                   int K, int prologue, void* workspace, size_t ws_bytes, void* stream);
+
+/* Generic form: weight format R4Q_W_*, `s` = scales (NULL for FP16), any
+ * prologue, optional fusions (may be NULL unless the prologue is RMSNorm). */
+int r4q_gemv(int wfmt, const void* x, long ldx, const void* w, const void* s, void* y, long ldy,
+             int B, int N, int K, int prologue, const r4q_gemv_fused* fused, void* workspace,
+             size_t ws_bytes, void* stream);
 
 /* --------------------------------------------------------- conversions --- */
 /* out[N, K] fp16 = fp16((q - z) * s); bit-exact to `dequant_int4_kernel`

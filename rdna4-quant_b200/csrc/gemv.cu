@@ -55,6 +55,15 @@ struct GemvParams {
   int prologue;
   unsigned* cnt; // per-row-tile arrival counters (zero between launches)
   float* part;   // [ksplit][B][N] fp32 partial sums
+  // fused RMSNorm prologue
+  const __half* norm_w;  // [K]
+  float eps;
+  const float* ss_in;    // [ss_in_parts][B] or null (then computed from x)
+  int ss_in_parts;
+  // fused residual epilogue
+  const __half* res;     // [B][ldres] or null
+  long ldres;
+  float* ss_out;         // [N/16][B] or null
 };
 
 __host__ __device__ inline int steps_total(int K, int ck, int u) {
@@ -72,7 +81,8 @@ __host__ __device__ inline int x_colstride(int nsteps, int nsub, int u) {
 // ------------------------------------------------------------ prologue ----
 // Loads 32 activations of column `col` starting at k0, applies the prologue
 // and returns them as fp16 in v[0..31].
-__device__ __forceinline__ void load_block32(const GemvParams& p, int col, int k0, __half (&v)[32]) {
+__device__ __forceinline__ void load_block32(const GemvParams& p, int col, int k0, float rrms,
+                                             __half (&v)[32]) {
   const __half* xr = p.x + (long)col * p.ldx;
   if (k0 >= p.K) {
 #pragma unroll
@@ -89,7 +99,19 @@ __device__ __forceinline__ void load_block32(const GemvParams& p, int col, int k
     return;
   }
   float f[32];
-  if (p.prologue == R4Q_PRO_FWHT) {
+  if (p.prologue == R4Q_PRO_RMSNORM_FWHT) {
+    // fp16(x) * rrms * w, then H32 (fused_res_norm_fwht phase 2, hip:1178-1190)
+    const uint4* src = reinterpret_cast<const uint4*>(xr + k0);
+    const uint4* ws = reinterpret_cast<const uint4*>(p.norm_w + k0);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      uint4 q = src[i], wq = __ldg(ws + i);
+      const __half* h = reinterpret_cast<const __half*>(&q);
+      const __half* wh = reinterpret_cast<const __half*>(&wq);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) f[8 * i + j] = __half2float(h[j]) * rrms * __half2float(wh[j]);
+    }
+  } else if (p.prologue == R4Q_PRO_FWHT) {
     const uint4* src = reinterpret_cast<const uint4*>(xr + k0);
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
@@ -321,6 +343,40 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const GemvParams p) {
     }
   }
 
+  // ---- RMSNorm prologue: one rrms per activation column ----
+  __shared__ float s_rrms[16];
+  if (p.prologue == R4Q_PRO_RMSNORM_FWHT) {
+    if (p.ss_in) {
+      // sum of the producer's per-tile partials in tile order (deterministic)
+      if (warp < ncolx) {
+        float ss = 0.0f;
+        for (int i = lane; i < p.ss_in_parts; i += 32) ss += p.ss_in[(long)i * ncolx + warp];
+        ss = warp_sum(ss);
+        if (lane == 0) s_rrms[warp] = rsqrtf(ss / (float)p.K + p.eps);
+      }
+      if (ncolx > kWarps && warp + kWarps < ncolx) {
+        const int c = warp + kWarps;
+        float ss = 0.0f;
+        for (int i = lane; i < p.ss_in_parts; i += 32) ss += p.ss_in[(long)i * ncolx + c];
+        ss = warp_sum(ss);
+        if (lane == 0) s_rrms[c] = rsqrtf(ss / (float)p.K + p.eps);
+      }
+    } else {
+      // sum of squares of the fp16 input itself (fused_rmsnorm_fwht, hip:1195-1215)
+      for (int c = warp; c < ncolx; c += kWarps) {
+        const __half2* xr = reinterpret_cast<const __half2*>(p.x + (long)c * p.ldx);
+        float ss = 0.0f;
+        for (int i = lane; i < (p.K >> 1); i += 32) {
+          const float2 f = __half22float2(xr[i]);
+          ss += f.x * f.x + f.y * f.y;
+        }
+        ss = warp_sum(ss);
+        if (lane == 0) s_rrms[c] = rsqrtf(ss / (float)p.K + p.eps);
+      }
+    }
+    __syncthreads();
+  }
+
   // ---- stage activations (with prologue) into shared memory ----
   {
     const int nblk = nch_pad * F::CK / 32;
@@ -328,7 +384,8 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const GemvParams p) {
     for (int item = tid; item < ncolx * nblk; item += kThreads) {
       const int col = item / nblk, blk = item - col * nblk;
       __half v[32];
-      load_block32(p, col, k_base + blk * 32, v);
+      load_block32(p, col, k_base + blk * 32,
+                   p.prologue == R4Q_PRO_RMSNORM_FWHT ? s_rrms[col] : 1.0f, v);
       store_block32<FMT>(smem + (long)col * colstride, nch_pad, blk, v);
     }
   }
@@ -379,16 +436,36 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const GemvParams p) {
         acc[cg][i] = v;
       }
     if (p.ksplit == 1) {
+      // fp16 output, optionally + residual (fp16(fp16(acc) + res)) and the
+      // per-16-row sum of squares of the unrounded sum
 #pragma unroll
       for (int cg = 0; cg < NG; ++cg) {
-        const int c0 = cg * 8 + 2 * t, c1 = c0 + 1;
-        if (c0 < p.B) {
-          p.y[(long)c0 * p.ldy + row_a] = __float2half(acc[cg][0]);
-          p.y[(long)c0 * p.ldy + row_b] = __float2half(acc[cg][2]);
+        float sq[2] = {0.0f, 0.0f};
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int c = cg * 8 + 2 * t + h;
+          if (c < p.B) {
+            float va = __half2float(__float2half(acc[cg][h]));
+            float vb = __half2float(__float2half(acc[cg][2 + h]));
+            if (p.res) {
+              va += __half2float(p.res[(long)c * p.ldres + row_a]);
+              vb += __half2float(p.res[(long)c * p.ldres + row_b]);
+            }
+            sq[h] = va * va + vb * vb;
+            p.y[(long)c * p.ldy + row_a] = __float2half(va);
+            p.y[(long)c * p.ldy + row_b] = __float2half(vb);
+          }
         }
-        if (c1 < p.B) {
-          p.y[(long)c1 * p.ldy + row_a] = __float2half(acc[cg][1]);
-          p.y[(long)c1 * p.ldy + row_b] = __float2half(acc[cg][3]);
+        if (p.ss_out) {
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            float v = sq[h];
+            v += __shfl_xor_sync(0xffffffffu, v, 4);
+            v += __shfl_xor_sync(0xffffffffu, v, 8);
+            v += __shfl_xor_sync(0xffffffffu, v, 16);
+            const int c = cg * 8 + 2 * t + h;
+            if (g == 0 && c < p.B) p.ss_out[(long)(row0 >> 4) * p.B + c] = v;
+          }
         }
       }
     } else {
@@ -420,12 +497,19 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const GemvParams p) {
   if (!s_last) return;
   __threadfence();
   const int trow0 = blockIdx.x * p.mt * 16;
-  const int trows = min(p.mt * 16, p.N - trow0);
-  for (int e = tid; e < trows * p.B; e += kThreads) {
-    const int col = e / trows, r = trow0 + (e - col * trows);
+  const int tiles16 = min(p.mt, (p.N - trow0) >> 4);
+  // one warp per (16-row tile, column): lanes 0..15 own one row each
+  for (int task = warp; task < tiles16 * p.B; task += kWarps) {
+    const int ti = task / p.B, col = task - ti * p.B;
+    const int r = trow0 + ti * 16 + (lane & 15);
     float v = 0.0f;
     for (int k2 = 0; k2 < p.ksplit; ++k2) v += __ldcg(p.part + ((long)k2 * p.B + col) * p.N + r);
-    p.y[(long)col * p.ldy + r] = __float2half(v);
+    v = __half2float(__float2half(v));
+    if (p.res) v += __half2float(p.res[(long)col * p.ldres + r]);
+    if (lane < 16) p.y[(long)col * p.ldy + r] = __float2half(v);
+    float sq = (lane < 16) ? v * v : 0.0f;
+    sq = warp_sum(sq);
+    if (p.ss_out && lane == 0) p.ss_out[(long)((trow0 >> 4) + ti) * p.B + col] = sq;
   }
   if (tid == 0) p.cnt[blockIdx.x] = 0u;  // leave the workspace zeroed for the next launch
 }
@@ -511,6 +595,13 @@ static int launch_gemv_t(const GemvArgs& a) {
   p.mt = pl.mt;
   p.ksplit = pl.ksplit;
   p.prologue = a.prologue;
+  p.norm_w = reinterpret_cast<const __half*>(a.norm_w);
+  p.eps = a.eps;
+  p.ss_in = a.ss_in;
+  p.ss_in_parts = a.ss_in_parts;
+  p.res = reinterpret_cast<const __half*>(a.res);
+  p.ldres = a.ldres;
+  p.ss_out = a.ss_out;
   p.cnt = reinterpret_cast<unsigned*>(a.ws);
   p.part = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(a.ws) + gemv_cnt_bytes(a.N));
   if (pl.ksplit > 1 && a.ws == nullptr)
@@ -520,7 +611,10 @@ static int launch_gemv_t(const GemvArgs& a) {
   return check_launch("gemv_kernel");
 }
 
-size_t gemv_cnt_bytes(int N) { return ((size_t)(N + 15) / 16 * 4 + 255) / 256 * 256; }
+// The counter region has a fixed size so that it never overlaps the partials
+// of a call with a different N (partials are left behind, counters are not).
+constexpr int kMaxTiles16 = 16384;
+size_t gemv_cnt_bytes(int N) { (void)N; return (size_t)kMaxTiles16 * 4; }
 size_t gemv_ws_bytes_for(int B, int N, int ksplit) {
   return gemv_cnt_bytes(N) + (size_t)ksplit * B * N * sizeof(float);
 }
@@ -530,9 +624,16 @@ int gemv_validate(const GemvArgs& a, int fmt) {
     return set_error(R4Q_ERR_ARG, "gemv: null pointer");
   if (a.B < 1 || a.B > 16) return set_error(R4Q_ERR_ARG, "gemv: B=%d outside 1..16", a.B);
   if (a.N <= 0 || a.N % 16) return set_error(R4Q_ERR_ARG, "gemv: N=%d must be a positive multiple of 16", a.N);
+  if (a.N / 16 > kMaxTiles16) return set_error(R4Q_ERR_ARG, "gemv: N=%d above %d", a.N, kMaxTiles16 * 16);
   if (a.K <= 0 || a.K % 32) return set_error(R4Q_ERR_ARG, "gemv: K=%d must be a positive multiple of 32", a.K);
-  if (a.prologue < R4Q_PRO_NONE || a.prologue > R4Q_PRO_SILU_FWHT)
+  if (a.prologue < R4Q_PRO_NONE || a.prologue > R4Q_PRO_RMSNORM_FWHT)
     return set_error(R4Q_ERR_ARG, "gemv: unknown prologue %d", a.prologue);
+  if (a.prologue == R4Q_PRO_RMSNORM_FWHT) {
+    if (!a.norm_w || !aligned(a.norm_w, 16))
+      return set_error(R4Q_ERR_ARG, "gemv: RMSNorm prologue needs a 16-byte aligned norm weight");
+    if (a.ss_in && a.ss_in_parts <= 0) return set_error(R4Q_ERR_ARG, "gemv: ss_in_parts must be > 0");
+  }
+  if (a.res && (a.B > 1 && a.ldres < a.N)) return set_error(R4Q_ERR_ARG, "gemv: ldres < N");
   const long kin = (a.prologue == R4Q_PRO_SILU_FWHT) ? 2L * a.K : a.K;
   if (a.B > 1 && a.ldx < kin) return set_error(R4Q_ERR_ARG, "gemv: ldx=%ld < %ld", a.ldx, kin);
   if (a.B > 1 && a.ldy < a.N) return set_error(R4Q_ERR_ARG, "gemv: ldy=%ld < N", a.ldy);
@@ -570,7 +671,7 @@ extern "C" size_t r4q_gemv_workspace_bytes(int B, int N, int K) {
 
 static GemvArgs mk(const void* x, long ldx, const void* w, const void* s, void* y, long ldy, int B,
                    int N, int K, int prologue, void* ws, size_t wsb, void* stream) {
-  GemvArgs a;
+  GemvArgs a{};
   a.x = x; a.ldx = ldx; a.w = w; a.s = s; a.y = y; a.ldy = ldy;
   a.B = B; a.N = N; a.K = K; a.prologue = prologue;
   a.ws = ws; a.ws_bytes = ws ? wsb : 0;
@@ -591,4 +692,22 @@ extern "C" int r4q_gemv_int8(const void* x, long ldx, const void* w, const void*
 extern "C" int r4q_gemv_fp16(const void* x, long ldx, const void* w, void* y, long ldy, int B,
                              int N, int K, int prologue, void* ws, size_t wsb, void* stream) {
   return launch_gemv(mk(x, ldx, w, nullptr, y, ldy, B, N, K, prologue, ws, wsb, stream), W_FP16);
+}
+
+extern "C" int r4q_gemv(int wfmt, const void* x, long ldx, const void* w, const void* s, void* y,
+                        long ldy, int B, int N, int K, int prologue, const r4q_gemv_fused* f,
+                        void* ws, size_t wsb, void* stream) {
+  GemvArgs a = mk(x, ldx, w, s, y, ldy, B, N, K, prologue, ws, wsb, stream);
+  if (f) {
+    a.norm_w = f->norm_w;
+    a.eps = f->eps;
+    a.ss_in = f->ss_in;
+    a.ss_in_parts = f->ss_in_parts;
+    a.res = f->residual;
+    a.ldres = (B > 1) ? f->ldres : N;
+    a.ss_out = f->ss_out;
+  }
+  if (a.prologue == R4Q_PRO_RMSNORM_FWHT && !f)
+    return set_error(R4Q_ERR_ARG, "gemv: RMSNorm prologue needs fused parameters");
+  return launch_gemv(a, wfmt);
 }

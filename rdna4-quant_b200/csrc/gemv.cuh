@@ -19,6 +19,14 @@ struct GemvArgs {
   void* ws;
   size_t ws_bytes;
   cudaStream_t stream;
+  // fused RMSNorm prologue / residual epilogue (all optional)
+  const void* norm_w;
+  float eps;
+  const float* ss_in;
+  int ss_in_parts;
+  const void* res;
+  long ldres;
+  float* ss_out;
 };
 
 size_t gemv_cnt_bytes(int N);

@@ -33,6 +33,14 @@ def _load():
 
 
 LIB = _load()
+
+
+class GemvFused(C.Structure):
+    """r4q_gemv_fused (include/r4q.h)."""
+    _fields_ = [("norm_w", C.c_void_p), ("eps", C.c_float), ("ss_in", C.c_void_p),
+                ("ss_in_parts", C.c_int), ("residual", C.c_void_p), ("ldres", C.c_long),
+                ("ss_out", C.c_void_p)]
+
 vp, i32, i64, sz_t, f32 = C.c_void_p, C.c_int, C.c_long, C.c_size_t, C.c_float
 
 _SIGS = {
@@ -42,6 +50,8 @@ _SIGS = {
     "r4q_gemv_int4": (i32, [vp, i64, vp, vp, vp, i64, i32, i32, i32, i32, vp, sz_t, vp]),
     "r4q_gemv_int8": (i32, [vp, i64, vp, vp, vp, i64, i32, i32, i32, i32, vp, sz_t, vp]),
     "r4q_gemv_fp16": (i32, [vp, i64, vp, vp, i64, i32, i32, i32, i32, vp, sz_t, vp]),
+    "r4q_gemv": (i32, [i32, vp, i64, vp, vp, vp, i64, i32, i32, i32, i32, C.POINTER(GemvFused),
+                       vp, sz_t, vp]),
     "r4q_dequant_int4": (i32, [vp, vp, vp, i32, i32, vp]),
     "r4q_fp16_to_fp8": (i32, [vp, vp, i64, vp]),
     "r4q_fp8_to_fp32": (i32, [vp, vp, i64, vp]),
@@ -67,4 +77,5 @@ def call(name: str, *args) -> None:
 
 
 # activation prologues (enum in include/r4q.h)
-PRO_NONE, PRO_FWHT, PRO_SILU_FWHT = 0, 1, 2
+PRO_NONE, PRO_FWHT, PRO_SILU_FWHT, PRO_RMSNORM_FWHT = 0, 1, 2, 3
+W_INT4, W_INT8, W_FP16 = 0, 1, 2

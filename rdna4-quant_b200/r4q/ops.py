@@ -3,6 +3,7 @@ per-(device, stream) GEMV workspaces.  Device memory and streams come from
 PyTorch; all arithmetic runs in libr4q.so."""
 from __future__ import annotations
 
+import ctypes as C
 import threading
 
 import torch
@@ -44,9 +45,20 @@ def _ptr(t: torch.Tensor | None) -> int | None:
     return None if t is None else t.data_ptr()
 
 
+_FMT = {'int4': L.W_INT4, 'int8': L.W_INT8, 'fp16': L.W_FP16}
+
+
 def gemv(fmt: str, x: torch.Tensor, w: torch.Tensor, s: torch.Tensor | None, N: int, K: int,
-         prologue: int = L.PRO_NONE, out: torch.Tensor | None = None) -> torch.Tensor:
-    """y[B, N] = prologue(x)[B, K] @ dequant(W)^T for fmt in {'int4','int8','fp16'}."""
+         prologue: int = L.PRO_NONE, out: torch.Tensor | None = None, *,
+         norm_w: torch.Tensor | None = None, eps: float = 1e-6,
+         ss_in: torch.Tensor | None = None, residual: torch.Tensor | None = None,
+         ss_out: torch.Tensor | None = None) -> torch.Tensor:
+    """y[B, N] = prologue(x)[B, K] @ dequant(W)^T for fmt in {'int4','int8','fp16'}.
+
+    Optional fusions: RMSNorm prologue (``prologue=PRO_RMSNORM_FWHT`` with
+    ``norm_w`` and, optionally, ``ss_in`` partial sums of squares [P, B]);
+    residual epilogue y = fp16(fp16(acc) + residual) with ``ss_out`` [N/16, B]
+    receiving the sums of squares of the unrounded sums."""
     dev = _require_cuda(x, w)
     if x.dtype != torch.float16:
         raise TypeError("x must be float16")
@@ -63,17 +75,18 @@ def gemv(fmt: str, x: torch.Tensor, w: torch.Tensor, s: torch.Tensor | None, N: 
     st = stream_handle(dev)
     ldx = x2.stride(0) if B > 1 else kin
     ldy = out.stride(0) if B > 1 else N
-    if fmt == 'int4':
-        L.call("r4q_gemv_int4", x2.data_ptr(), ldx, w.data_ptr(), s.data_ptr(), out.data_ptr(),
-               ldy, B, N, K, prologue, ws.data_ptr(), ws.numel(), st)
-    elif fmt == 'int8':
-        L.call("r4q_gemv_int8", x2.data_ptr(), ldx, w.data_ptr(), s.data_ptr(), out.data_ptr(),
-               ldy, B, N, K, prologue, ws.data_ptr(), ws.numel(), st)
-    elif fmt == 'fp16':
-        L.call("r4q_gemv_fp16", x2.data_ptr(), ldx, w.data_ptr(), out.data_ptr(), ldy, B, N, K,
-               prologue, ws.data_ptr(), ws.numel(), st)
-    else:
-        raise ValueError(fmt)
+    fused = None
+    if norm_w is not None or residual is not None or ss_out is not None or ss_in is not None:
+        if residual is not None:
+            residual = residual.reshape(B, -1)
+        fused = L.GemvFused(
+            norm_w=_ptr(norm_w), eps=float(eps), ss_in=_ptr(ss_in),
+            ss_in_parts=0 if ss_in is None else int(ss_in.shape[0]),
+            residual=_ptr(residual), ldres=N if residual is None else residual.stride(0),
+            ss_out=_ptr(ss_out))
+    L.call("r4q_gemv", _FMT[fmt], x2.data_ptr(), ldx, w.data_ptr(), _ptr(s), out.data_ptr(), ldy,
+           B, N, K, prologue, None if fused is None else C.byref(fused), ws.data_ptr(), ws.numel(),
+           st)
     return out
 
 
