@@ -33,5 +33,7 @@ size_t gemv_cnt_bytes(int N);
 size_t gemv_ws_bytes_for(int B, int N, int ksplit);
 int gemv_validate(const GemvArgs& a, int fmt);
 int launch_gemv(const GemvArgs& a, int fmt);
+bool gemv_tma_supported(const GemvArgs& a, int fmt);
+int launch_gemv_tma(const GemvArgs& a, int fmt);
 
 }  // namespace r4q

@@ -180,7 +180,8 @@ def test_reference_test_gemv_vs_pytorch(ops):
     x = torch.randn(1, K, dtype=torch.float16).numpy()
     y = int4_hip.dbg_gemv(cuda(x[0]), cuda(packed), cuda(sz), N, K).cpu().numpy()
     ref = O.gemv_int4(x, packed, sz)[0]
-    cos = float(np.dot(y.astype(np.float64), ref) / (np.linalg.norm(y) * np.linalg.norm(ref)))
+    y64, r64 = y.astype(np.float64), ref.astype(np.float64)
+    cos = float(np.dot(y64, r64) / (np.linalg.norm(y64) * np.linalg.norm(r64)))
     assert cos > 0.99
     close(y, ref)
     # dbg_gemm with M > 16 rows
@@ -196,3 +197,34 @@ def test_bad_arguments_raise(ops):
     s = torch.zeros(64, 3, dtype=torch.float16, device='cuda')
     with pytest.raises(R4QError):
         ops.gemv('int4', x, w, s, 64, 48)
+
+
+@pytest.mark.parametrize("fmt", ["int4", "int8", "fp16"])
+def test_ldg_and_tma_paths_agree(fmt, tmp_path):
+    """Both GEMV kernels (TMA default, LDG for shapes TMA cannot take) meet the
+    bar on the same data; the LDG one is forced in a subprocess."""
+    import subprocess, sys, os
+    code = f"""
+import sys, numpy as np, torch
+sys.path[:0] = {[str(p) for p in __import__('sys').path[:4]]!r}
+import r4q_oracle as O
+from test_gpu_gemv import close, cuda, make_int4
+from r4q import ops
+rng = np.random.default_rng(4)
+N, K, B = 1024, 5120, 3
+x = rng.standard_normal((B, K)).astype(np.float16)
+if '{fmt}' == 'int4':
+    p, s = make_int4(rng, N, K); ref = O.gemv_int4(x, p, s)
+elif '{fmt}' == 'int8':
+    W = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
+    q, s = O.quantize_int8_sym(W.reshape(N, K // 32, 32)); p = q.reshape(N, K); ref = O.gemv_int8(x, p, s)
+else:
+    p = (rng.standard_normal((N, K)) * 0.02).astype(np.float16); s = None; ref = O.gemv_fp16(x, p)
+y = ops.gemv('{fmt}', cuda(x), cuda(p), None if s is None else cuda(s), N, K).cpu().numpy()
+close(y, ref)
+print('ok')
+"""
+    env = dict(os.environ, R4Q_GEMV_PATH="ldg")
+    r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True,
+                       cwd=str(__import__('pathlib').Path(__file__).parent))
+    assert r.returncode == 0 and "ok" in r.stdout, r.stdout + r.stderr
