@@ -415,7 +415,10 @@ int launch_gemv(const GemvArgs& a, int fmt) {
     const char* e = getenv("R4Q_GEMV_PATH");
     return (e && e[0] == 'l') ? 1 : 0;
   }();
-  if (!force_ldg && gemv_tma_supported(a, fmt)) return launch_gemv_tma(a, fmt);
+  if (!force_ldg && gemv_tma_supported(a, fmt)) {
+    st = launch_gemv_tma(a, fmt);
+    if (st != R4Q_ERR_CAPACITY) return st;  // no TMA plan fits: take the LDG kernel
+  }
   const bool two = a.B > 8;
   switch (fmt) {
     case W_INT4: return two ? launch_gemv_t<W_INT4, 2>(a) : launch_gemv_t<W_INT4, 1>(a);

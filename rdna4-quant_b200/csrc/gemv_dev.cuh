@@ -243,4 +243,66 @@ __device__ __forceinline__ void chunk_mma(const RowChunk& ra, const RowChunk& rb
 }
 
 
+// MMAs per 16-byte chunk: INT4 8 (32 k), INT8 4 (16 k), FP16 2 (8 k).
+template <int FMT> struct ChunkMma { static constexpr int N = FMT == W_INT4 ? 8 : (FMT == W_INT8 ? 4 : 2); };
+
+// Dequantises one chunk of rows a and b into the A operands of its MMAs:
+// frag[j] = {row a lo-k, row b lo-k, row a hi-k, row b hi-k} of MMA j.
+template <int FMT>
+__device__ __forceinline__ void chunk_dequant(const RowChunk& ra, const RowChunk& rb,
+                                              uint32_t (&frag)[ChunkMma<FMT>::N][4]) {
+  if constexpr (FMT == W_INT4) {
+    const __half2 sza = u32_as_h2(ra.s), szb = u32_as_h2(rb.s);
+    const __half2 c1024 = __float2half2_rn(1024.0f), c64 = __float2half2_rn(64.0f);
+    const __half2 za = __high2half2(sza), zb = __high2half2(szb);
+    const __half2 za1024 = __hadd2(za, c1024), zb1024 = __hadd2(zb, c1024);
+    const __half2 nza64 = __hneg2(__hadd2(za, c64)), nzb64 = __hneg2(__hadd2(zb, c64));
+    const __half2 sa = __low2half2(sza), sb = __low2half2(szb);
+    const uint32_t wa[4] = {ra.w.x, ra.w.y, ra.w.z, ra.w.w};
+    const uint32_t wb[4] = {rb.w.x, rb.w.y, rb.w.z, rb.w.w};
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+      uint32_t A[4], Bq[4];
+      deq_int4_word(wa[m], za1024, nza64, sa, A);
+      deq_int4_word(wb[m], zb1024, nzb64, sb, Bq);
+      frag[2 * m][0] = A[0]; frag[2 * m][1] = Bq[0]; frag[2 * m][2] = A[1]; frag[2 * m][3] = Bq[1];
+      frag[2 * m + 1][0] = A[2]; frag[2 * m + 1][1] = Bq[2]; frag[2 * m + 1][2] = A[3]; frag[2 * m + 1][3] = Bq[3];
+    }
+  } else if constexpr (FMT == W_INT8) {
+    const __half2 sa = __low2half2(u32_as_h2(ra.s)), sb = __low2half2(u32_as_h2(rb.s));
+    const uint32_t wa[4] = {ra.w.x, ra.w.y, ra.w.z, ra.w.w};
+    const uint32_t wb[4] = {rb.w.x, rb.w.y, rb.w.z, rb.w.w};
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+      deq_int8_word(wa[m], sa, frag[m][0], frag[m][2]);
+      deq_int8_word(wb[m], sb, frag[m][1], frag[m][3]);
+    }
+  } else {
+    frag[0][0] = ra.w.x; frag[0][1] = rb.w.x; frag[0][2] = ra.w.y; frag[0][3] = rb.w.y;
+    frag[1][0] = ra.w.z; frag[1][1] = rb.w.z; frag[1][2] = ra.w.w; frag[1][3] = rb.w.w;
+  }
+}
+
+// MMAs of one dequantised chunk against the staged activations; MMA j uses
+// activation sub-row j/2 (words x,y for even j, z,w for odd j) and
+// accumulator chain j&1, so consecutive MMAs are independent.
+template <int FMT, int NG>
+__device__ __forceinline__ void chunk_mma_frag(const uint32_t (&frag)[ChunkMma<FMT>::N][4],
+                                               const uint8_t* xs, int colstride, int nch_pad,
+                                               int lchunk, const int (&colx)[NG],
+                                               float (&acc)[NG][2][4]) {
+  constexpr int NM = ChunkMma<FMT>::N;
+#pragma unroll
+  for (int cg = 0; cg < NG; ++cg) {
+#pragma unroll
+    for (int sub = 0; sub < NM / 2; ++sub) {
+      const uint4 xf = *reinterpret_cast<const uint4*>(xs + (long)colx[cg] * colstride +
+                                                       ((long)sub * nch_pad + lchunk) * 16);
+      const int j = 2 * sub;
+      mma16816(acc[cg][0], frag[j][0], frag[j][1], frag[j][2], frag[j][3], xf.x, xf.y);
+      mma16816(acc[cg][1], frag[j + 1][0], frag[j + 1][1], frag[j + 1][2], frag[j + 1][3], xf.z, xf.w);
+    }
+  }
+}
+
 }  // namespace r4q

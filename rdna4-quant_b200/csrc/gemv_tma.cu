@@ -1,20 +1,23 @@
 // Dequant-GEMV, TMA path (the default when the shape allows it).
 //
 // Persistent, warp-specialised kernel, one CTA per SM:
-//  * warp 8 (producer): one lane streams the CTA's weight tiles — 64 rows x
-//    256 k per stage — and their (scale, zero) tiles into an NS-deep
-//    shared-memory ring with cp.async.bulk.tensor (TMA) and mbarrier
+//  * warp 16 (producer): one lane streams the CTA's weight tiles — 64 rows x
+//    512 k per stage for INT4 — and their (scale, zero) tiles into a
+//    shared-memory ring (~120 KB) with cp.async.bulk.tensor (TMA) and mbarrier
 //    transaction counts.  Weights are read from HBM exactly once and no
-//    register holds data in flight, so the ring depth (80-96 KB per SM) sets
-//    the bytes in flight;
-//  * warps 0-7 (consumers): warp (m-tile, half) takes 16 rows x 128 k of each
-//    stage, reads its 16-byte chunks with conflict-free LDS.128 (128-byte TMA
-//    swizzle + a row order in which rows sharing a quarter-warp differ in bit
-//    2), dequantises in registers into m16n8k16 A fragments and accumulates in
-//    fp32 on the tensor cores against the activations staged once per CTA;
+//    register holds data in flight.  Each row contributes >= 256 contiguous
+//    bytes per stage: with 128 bytes per row per stage the TMA stream alone
+//    stalls near 4.2 TB/s on B200; with 256-512 bytes it reaches the roofline;
+//  * warps 0-15 (consumers): warp (m-tile, k quarter) takes 16 rows x 1/4 of
+//    each stage's k, reads its 16-byte chunks with conflict-free LDS.128
+//    (128-byte TMA swizzle + a row order in which rows sharing a quarter-warp
+//    differ in bit 2), dequantises in registers into m16n8k16 A fragments,
+//    releases the ring slot, then accumulates in fp32 on the tensor cores
+//    (two independent accumulator chains) against the activations staged
+//    once per CTA;
 //  * units = (64-row tile, K split); each CTA owns one K split (activations are
 //    staged once) and a strided set of tiles; split partials merge in the
-//    last-arriving CTA of a tile (deterministic order), as in the LDG path.
+//    last-arriving CTA of a tile (deterministic order);
 //  * programmatic dependent launch: the producer starts streaming weights
 //    before griddepcontrol.wait; everything that reads the previous kernel's
 //    outputs (activations, sums of squares, residual) comes after it.
@@ -27,30 +30,31 @@
 
 namespace r4q {
 
-constexpr int kTmaConsumers = 8;
+constexpr int kTmaConsumers = 16;
 constexpr int kTmaThreads = (kTmaConsumers + 1) * 32;
 constexpr int kTileRows = 64;
-constexpr int kStageK = 256;
 constexpr int kTmaMaxSplit = 32;
 constexpr long kSpinLimit = 1L << 26;  // bounded mbarrier waits (seconds of wall time)
 
+// A stage is 64 rows x SK k.
 template <int FMT> struct TmaFmt;
 template <> struct TmaFmt<W_INT4> {
-  static constexpr int CPS = 8;          // 16-byte chunks per row per stage
-  static constexpr int BOXES = 1;        // 128-byte weight boxes per row per stage
-  static constexpr int SBYTES = 32;      // scale bytes per row per stage
-  static constexpr int NS = 8;           // ring depth
+  static constexpr int SK = 512;         // k per stage
+  static constexpr int CPS = 16;         // 16-byte chunks per row per stage
+  static constexpr int BOXES = 2;        // 128-byte weight boxes per row per stage
+  static constexpr int SBYTES = 64;      // (scale, zero) bytes per row per stage
+  static constexpr int NS = 6;           // ring depth
 };
 template <> struct TmaFmt<W_INT8> {
-  static constexpr int CPS = 16, BOXES = 2, SBYTES = 16, NS = 5;
+  static constexpr int SK = 512, CPS = 32, BOXES = 4, SBYTES = 32, NS = 4;
 };
 template <> struct TmaFmt<W_FP16> {
-  static constexpr int CPS = 32, BOXES = 4, SBYTES = 0, NS = 3;
+  static constexpr int SK = 256, CPS = 32, BOXES = 4, SBYTES = 0, NS = 4;
 };
 
 struct TmaParams {
   GemvParams p;
-  int nstages;     // 256-k stages over the whole K
+  int nstages;     // stages over the whole K
   int tiles;       // 64-row tiles
   int gt;          // CTAs per K split
   int x_bytes;     // activation smem bytes
@@ -119,6 +123,8 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
   constexpr int W_STAGE = kTileRows * T::CPS * 16;     // bytes of weights per stage
   constexpr int S_STAGE = kTileRows * T::SBYTES;
   constexpr int NS = T::NS;
+  constexpr int V = T::CPS / 16;                       // chunks per thread per row per stage
+  constexpr int NM = ChunkMma<FMT>::N;
   const GemvParams& p = tp.p;
 
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -126,8 +132,8 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
   uint8_t* ring_w = smem;
   uint8_t* ring_s = ring_w + NS * W_STAGE;
   uint8_t* xs = ring_s + NS * S_STAGE;
-  float* red = reinterpret_cast<float*>(xs + tp.x_bytes);        // [4 m-tiles][NG*4][32]
-  uint64_t* full = reinterpret_cast<uint64_t*>(red + 4 * NG * 4 * 32);
+  float* red = reinterpret_cast<float*>(xs + tp.x_bytes);          // [4 m-tiles][3][NG*4][32]
+  uint64_t* full = reinterpret_cast<uint64_t*>(red + 4 * 3 * NG * 4 * 32);
   uint64_t* empty = full + NS;
   __shared__ float s_rrms[16];
   __shared__ unsigned s_last;
@@ -179,7 +185,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
   // ------------------------------------------------------------ consumers
   // everything below may read outputs of the previous kernel in the stream
   asm volatile("griddepcontrol.wait;" ::: "memory");
-  const int ctid = tid;  // 0 .. 255
+  const int ctid = tid;  // 0 .. kTmaConsumers*32-1
   const int ncolx = p.B;
   const int nch_pad = nst * T::CPS;
   const int colstride = tp.x_bytes / (ncolx > 0 ? ncolx : 1);
@@ -203,7 +209,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
   }
   {
     const int nblk = nch_pad * F::CK / 32;
-    const int k_base = st0 * kStageK;
+    const int k_base = st0 * T::SK;
     for (int item = ctid; item < ncolx * nblk; item += kTmaConsumers * 32) {
       const int col = item / nblk, blk = item - col * nblk;
       __half v[32];
@@ -214,68 +220,90 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
   }
   consumer_sync();
 
+  // warp -> (k quarter, m-tile); every stage is consumed by all 16 warps
   const int g = lane >> 2, t = lane & 3;
-  const int mt = warp & 3, half = warp >> 2;
+  const int mt = warp & 3, part = warp >> 2;
   const int ra = mt * 16 + row_perm(g), rb = ra + 8;       // rows inside the 64-row tile
   int colx[NG];
 #pragma unroll
   for (int cg = 0; cg < NG; ++cg) colx[cg] = min(cg * 8 + g, p.B - 1);
-  constexpr int V = T::CPS / 8;                             // chunks per thread per row per stage
 
-  int it = 0;
+  int it0 = 0;                                              // ring index of the unit's first stage
   bool ok = true;
-  for (int tile = cta_in_split; tile < tp.tiles; tile += tp.gt) {
-    float acc[NG][4];
+  for (int tile = cta_in_split; tile < tp.tiles; tile += tp.gt, it0 += nst) {
+    float acc[NG][2][4];
 #pragma unroll
     for (int cg = 0; cg < NG; ++cg)
 #pragma unroll
-      for (int i = 0; i < 4; ++i) acc[cg][i] = 0.0f;
+      for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) acc[cg][h][i] = 0.0f;
 
-    for (int st = 0; st < nst; ++st, ++it) {
+    for (int st = 0; st < nst; ++st) {
+      const int it = it0 + st;
       const int slot = it % NS;
       const unsigned ph = (unsigned)(it / NS) & 1u;
       if (ok) ok = mbar_wait(&full[slot], ph, tp.status);
       const uint8_t* wst = ring_w + slot * W_STAGE;
       const uint8_t* sst = ring_s + slot * S_STAGE;
+      uint32_t frag[V][NM][4];
 #pragma unroll
       for (int v = 0; v < V; ++v) {
-        const int c = half * (T::CPS / 2) + 4 * v + t;         // chunk within the stage row
+        const int c = part * (T::CPS / 4) + 4 * v + t;     // chunk within the stage row
         const int box = c >> 3, cb = c & 7;
         RowChunk A, Bq;
         A.w = *reinterpret_cast<const uint4*>(wst + box * (kTileRows * 128) + ra * 128 + ((cb ^ (ra & 7)) << 4));
         Bq.w = *reinterpret_cast<const uint4*>(wst + box * (kTileRows * 128) + rb * 128 + ((cb ^ (rb & 7)) << 4));
         if constexpr (FMT == W_INT4) {
-          // 32-byte rows, 32-byte swizzle: the 16-byte half index flips with row bit 2
-          const int hsw_a = ((c >> 2) ^ ((ra >> 2) & 1)) << 4, hsw_b = ((c >> 2) ^ ((rb >> 2) & 1)) << 4;
-          A.s = *reinterpret_cast<const uint32_t*>(sst + ra * 32 + hsw_a + (c & 3) * 4);
-          Bq.s = *reinterpret_cast<const uint32_t*>(sst + rb * 32 + hsw_b + (c & 3) * 4);
+          // 64-byte rows, 64-byte swizzle: 16-byte unit index ^= row bits 1-2
+          const int ua = ((c >> 2) ^ ((ra >> 1) & 3)) << 4, ub = ((c >> 2) ^ ((rb >> 1) & 3)) << 4;
+          A.s = *reinterpret_cast<const uint32_t*>(sst + ra * 64 + ua + (c & 3) * 4);
+          Bq.s = *reinterpret_cast<const uint32_t*>(sst + rb * 64 + ub + (c & 3) * 4);
         } else if constexpr (FMT == W_INT8) {
-          A.s = *reinterpret_cast<const uint16_t*>(sst + ra * 16 + (c >> 1) * 2);
-          Bq.s = *reinterpret_cast<const uint16_t*>(sst + rb * 16 + (c >> 1) * 2);
+          // 32-byte rows, 32-byte swizzle: 16-byte half index ^= row bit 2
+          const int b = c >> 1;
+          const int ha = ((b >> 3) ^ ((ra >> 2) & 1)) << 4, hb = ((b >> 3) ^ ((rb >> 2) & 1)) << 4;
+          A.s = *reinterpret_cast<const uint16_t*>(sst + ra * 32 + ha + (b & 7) * 2);
+          Bq.s = *reinterpret_cast<const uint16_t*>(sst + rb * 32 + hb + (b & 7) * 2);
         } else {
           A.s = Bq.s = 0;
         }
-        chunk_mma<FMT, NG>(A, Bq, xs, colstride, nch_pad, st * T::CPS + c, colx, acc);
+        chunk_dequant<FMT>(A, Bq, frag[v]);
       }
+      // the slot is free once its bytes are in registers; the MMAs follow
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[slot]);
+#pragma unroll
+      for (int v = 0; v < V; ++v) {
+        const int c = part * (T::CPS / 4) + 4 * v + t;
+        chunk_mma_frag<FMT, NG>(frag[v], xs, colstride, nch_pad, st * T::CPS + c, colx, acc);
+      }
     }
+#pragma unroll
+    for (int cg = 0; cg < NG; ++cg)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) acc[cg][0][i] += acc[cg][1][i];
 
-    // ---- combine the two halves of each m-tile, then the epilogue ----
-    if (half == 1) {
+    // ---- combine the 4 k-quarter partials of each m-tile (fixed order) ----
+    if (part != 0) {
 #pragma unroll
       for (int cg = 0; cg < NG; ++cg)
 #pragma unroll
-        for (int i = 0; i < 4; ++i) red[(mt * NG * 4 + cg * 4 + i) * 32 + lane] = acc[cg][i];
+        for (int i = 0; i < 4; ++i) red[(((mt * 3 + part - 1) * NG + cg) * 4 + i) * 32 + lane] = acc[cg][0][i];
     }
     consumer_sync();
     const int row0 = tile * kTileRows + mt * 16;
-    const bool rows_ok = row0 < p.N;
-    if (half == 0 && rows_ok) {
+    if (part == 0 && row0 < p.N) {
+      float r[NG][4];
 #pragma unroll
       for (int cg = 0; cg < NG; ++cg)
 #pragma unroll
-        for (int i = 0; i < 4; ++i) acc[cg][i] += red[(mt * NG * 4 + cg * 4 + i) * 32 + lane];
+        for (int i = 0; i < 4; ++i) {
+          float v = acc[cg][0][i];
+#pragma unroll
+          for (int q = 0; q < 3; ++q) v += red[(((mt * 3 + q) * NG + cg) * 4 + i) * 32 + lane];
+          r[cg][i] = v;
+        }
       const int row_a = tile * kTileRows + ra, row_b = tile * kTileRows + rb;
       if (S == 1) {
 #pragma unroll
@@ -285,8 +313,8 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
           for (int h = 0; h < 2; ++h) {
             const int c = cg * 8 + 2 * t + h;
             if (c < p.B) {
-              float va = __half2float(__float2half(acc[cg][h]));
-              float vb = __half2float(__float2half(acc[cg][2 + h]));
+              float va = __half2float(__float2half(r[cg][h]));
+              float vb = __half2float(__float2half(r[cg][2 + h]));
               if (p.res) {
                 va += __half2float(p.res[(long)c * p.ldres + row_a]);
                 vb += __half2float(p.res[(long)c * p.ldres + row_b]);
@@ -309,40 +337,41 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
           }
         }
       } else {
-        float* part = p.part + (long)ks * p.B * p.N;
+        float* prt = p.part + (long)ks * p.B * p.N;
 #pragma unroll
         for (int cg = 0; cg < NG; ++cg)
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
             const int c = cg * 8 + 2 * t + h;
             if (c < p.B) {
-              part[(long)c * p.N + row_a] = acc[cg][h];
-              part[(long)c * p.N + row_b] = acc[cg][2 + h];
+              prt[(long)c * p.N + row_a] = r[cg][h];
+              prt[(long)c * p.N + row_b] = r[cg][2 + h];
             }
           }
       }
     }
     if (S > 1) {
-      // last CTA of this tile sums the split partials in split order
-      __threadfence();
+      // the partial stores of this CTA are ordered before thread 0's gpu-scope
+      // acq_rel atomic by the barrier; the last arriving CTA of the tile sums
+      // the split partials in split order
       consumer_sync();
       if (ctid == 0) {
-        const unsigned old = atomicAdd(&p.cnt[tile], 1u);
+        unsigned old;
+        asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(old) : "l"(p.cnt + tile) : "memory");
         s_last = (old == (unsigned)S - 1) ? 1u : 0u;
       }
       consumer_sync();
       if (s_last) {
-        __threadfence();
         const int trow0 = tile * kTileRows;
         const int tiles16 = min(4, (p.N - trow0) >> 4);
         for (int task = warp; task < tiles16 * p.B; task += kTmaConsumers) {
           const int ti = task / p.B, col = task - ti * p.B;
-          const int r = trow0 + ti * 16 + (lane & 15);
+          const int rr = trow0 + ti * 16 + (lane & 15);
           float v = 0.0f;
-          for (int k2 = 0; k2 < S; ++k2) v += __ldcg(p.part + ((long)k2 * p.B + col) * p.N + r);
+          for (int k2 = 0; k2 < S; ++k2) v += __ldcg(p.part + ((long)k2 * p.B + col) * p.N + rr);
           v = __half2float(__float2half(v));
-          if (p.res) v += __half2float(p.res[(long)col * p.ldres + r]);
-          if (lane < 16) p.y[(long)col * p.ldy + r] = __float2half(v);
+          if (p.res) v += __half2float(p.res[(long)col * p.ldres + rr]);
+          if (lane < 16) p.y[(long)col * p.ldy + rr] = __float2half(v);
           float sq = (lane < 16) ? v * v : 0.0f;
           sq = warp_sum(sq);
           if (p.ss_out && lane == 0) p.ss_out[(long)((trow0 >> 4) + ti) * p.B + col] = sq;
@@ -401,15 +430,42 @@ struct TmaPlan {
   int x_bytes;
 };
 
+// Largest dynamic shared memory this kernel may use: the per-block opt-in
+// limit minus its static shared memory.  Sets the attribute once per device.
+template <int FMT, int NG>
+static size_t tma_smem_limit() {
+  static std::mutex mu;
+  static std::unordered_map<int, size_t> lim;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lk(mu);
+  auto it = lim.find(dev);
+  if (it != lim.end()) return it->second;
+  int optin = 0;
+  cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+  cudaFuncAttributes fa{};
+  size_t v = 0;
+  if (optin > 0 && cudaFuncGetAttributes(&fa, gemv_tma_kernel<FMT, NG>) == cudaSuccess) {
+    v = (size_t)optin - fa.sharedSizeBytes;
+    if (cudaFuncSetAttribute(gemv_tma_kernel<FMT, NG>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)v) != cudaSuccess)
+      v = 0;
+  }
+  cudaGetLastError();  // leave no error behind for the caller's runtime
+  lim[dev] = v;
+  return v;
+}
+
 template <int FMT, int NG>
 static TmaPlan plan_tma(int B, int N, int K, size_t ws_bytes) {
   using T = TmaFmt<FMT>;
   using F = Fmt<FMT>;
   const int nsm = num_sms();
   const int tiles = (N + kTileRows - 1) / kTileRows;
-  const int nst = (K + kStageK - 1) / kStageK;
+  const int nst = (K + T::SK - 1) / T::SK;
   const size_t fixed = 1024 + (size_t)T::NS * (kTileRows * T::CPS * 16 + kTileRows * T::SBYTES) +
-                       4 * NG * 4 * 32 * 4 + 2 * T::NS * 8;
+                       4 * 3 * NG * 4 * 32 * 4 + 2 * T::NS * 8;
+  const size_t smem_limit = tma_smem_limit<FMT, NG>();
   TmaPlan best{1, 1, 0, 0};
   double best_cost = 1e30;
   for (int S = 1; S <= kTmaMaxSplit && S <= nst; ++S) {
@@ -419,7 +475,7 @@ static TmaPlan plan_tma(int B, int N, int K, size_t ws_bytes) {
     const int per = (nst + S - 1) / S;                       // stages per unit (max)
     const int colstride = x_colstride(per * T::CPS / 4 / F::U, F::NSUB, F::U);
     const size_t xb = (size_t)colstride * B;
-    if (fixed + xb > 226 * 1024) continue;
+    if (fixed + xb > smem_limit) continue;
     const int rounds = (tiles + gt - 1) / gt;
     // busiest CTA streams rounds * per stages; S > 1 adds a merge per tile
     const double cost = (double)rounds * per + (S > 1 ? 0.35 * rounds : 0.0) + 0.02 * S;
@@ -441,8 +497,8 @@ static int launch_tma_t(const GemvArgs& a) {
   const long rowbytes = (FMT == W_INT4) ? a.K / 2 : (FMT == W_INT8 ? a.K : 2L * a.K);
   int st = make_map(&tmw, a.w, a.N, rowbytes, 128, kTileRows, CU_TENSOR_MAP_SWIZZLE_128B);
   if (st) return st;
-  if (FMT == W_INT4) st = make_map(&tms, a.s, a.N, a.K / 8, 32, kTileRows, CU_TENSOR_MAP_SWIZZLE_32B);
-  else if (FMT == W_INT8) st = make_map(&tms, a.s, a.N, a.K / 16, 16, kTileRows, CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (FMT == W_INT4) st = make_map(&tms, a.s, a.N, a.K / 8, 64, kTileRows, CU_TENSOR_MAP_SWIZZLE_64B);
+  else if (FMT == W_INT8) st = make_map(&tms, a.s, a.N, a.K / 16, 32, kTileRows, CU_TENSOR_MAP_SWIZZLE_32B);
   else tms = tmw;
   if (st) return st;
 
@@ -467,21 +523,12 @@ static int launch_tma_t(const GemvArgs& a) {
   p.ss_out = a.ss_out;
   p.cnt = reinterpret_cast<unsigned*>(a.ws);
   p.part = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(a.ws) + gemv_cnt_bytes(a.N));
-  tp.nstages = (a.K + kStageK - 1) / kStageK;
+  tp.nstages = (a.K + T::SK - 1) / T::SK;
   tp.tiles = (a.N + kTileRows - 1) / kTileRows;
   tp.gt = pl.gt;
   tp.x_bytes = pl.x_bytes;
   tp.status = a.ws ? reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(a.ws) + gemv_cnt_bytes(a.N) - 4) : nullptr;
 
-  static std::mutex mu;
-  static bool attr = false;
-  {
-    std::lock_guard<std::mutex> lk(mu);
-    if (!attr) {
-      cudaFuncSetAttribute(gemv_tma_kernel<FMT, NG>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-      attr = true;
-    }
-  }
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(pl.S * pl.gt);
   cfg.blockDim = dim3(kTmaThreads);
@@ -493,7 +540,10 @@ static int launch_tma_t(const GemvArgs& a) {
   cfg.attrs = attrs;
   cfg.numAttrs = 1;
   cudaError_t e = cudaLaunchKernelEx(&cfg, gemv_tma_kernel<FMT, NG>, tmw, tms, tp);
-  if (e != cudaSuccess) return set_error(R4Q_ERR_CUDA, "gemv_tma_kernel: %s", cudaGetErrorString(e));
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return set_error(R4Q_ERR_CUDA, "gemv_tma_kernel (smem %zu): %s", pl.smem, cudaGetErrorString(e));
+  }
   return R4Q_OK;
 }
 

@@ -228,3 +228,37 @@ print('ok')
     r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True,
                        cwd=str(__import__('pathlib').Path(__file__).parent))
     assert r.returncode == 0 and "ok" in r.stdout, r.stdout + r.stderr
+
+
+@pytest.mark.parametrize("fmt", ["int4", "int8", "fp16"])
+def test_ldg_path_forced(fmt):
+    """The LDG kernel (used for shapes the TMA kernel cannot take) meets the
+    bar on the same data; it is forced with R4Q_GEMV_PATH=ldg in a subprocess."""
+    import os
+    import subprocess
+    import sys
+    from pathlib import Path
+    code = f"""
+import sys, numpy as np
+sys.path[:0] = {[str(p) for p in sys.path[:4]]!r}
+import r4q_oracle as O
+from test_gpu_gemv import close, cuda, make_int4
+from r4q import ops
+rng = np.random.default_rng(4)
+N, K, B = 1024, 5120, 3
+x = rng.standard_normal((B, K)).astype(np.float16)
+if '{fmt}' == 'int4':
+    p, s = make_int4(rng, N, K); ref = O.gemv_int4(x, p, s)
+elif '{fmt}' == 'int8':
+    W = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
+    q, s = O.quantize_int8_sym(W.reshape(N, K // 32, 32)); p = q.reshape(N, K); ref = O.gemv_int8(x, p, s)
+else:
+    p = (rng.standard_normal((N, K)) * 0.02).astype(np.float16); s = None; ref = O.gemv_fp16(x, p)
+y = ops.gemv('{fmt}', cuda(x), cuda(p), None if s is None else cuda(s), N, K).cpu().numpy()
+close(y, ref)
+print('ok')
+"""
+    env = dict(os.environ, R4Q_GEMV_PATH="ldg")
+    r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True,
+                       cwd=str(Path(__file__).parent))
+    assert r.returncode == 0 and "ok" in r.stdout, r.stdout + r.stderr
