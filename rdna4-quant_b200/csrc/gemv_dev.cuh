@@ -243,6 +243,102 @@ __device__ __forceinline__ void chunk_mma(const RowChunk& ra, const RowChunk& rb
 }
 
 
+// Activation staging with 4 lanes per 32-block: lane q of a quad owns k =
+// 8q..8q+7, applies the prologue, runs the FWHT (strides 1,2,4 in registers,
+// 8 and 16 across the quad, same stage order as the 32-register form) and
+// stores its 8 values as one 16-byte sub-row of the permuted layout.  All 32
+// lanes of the warp must call it (shuffles); `valid` masks the stores.
+template <int FMT, bool DIAG>
+__device__ __forceinline__ void stage_quad(const GemvParams& p, int col, int k0, int q, float rrms,
+                                           uint8_t* xs_col, int nch_pad, int blk, bool valid,
+                                           float2* xsum_slot) {
+  __half v[8];
+  const bool in = valid && k0 < p.K;
+  const __half* xr = p.x + (long)col * p.ldx + k0 + 8 * q;
+  if (p.prologue == R4Q_PRO_NONE) {
+    uint4 raw = in ? *reinterpret_cast<const uint4*>(xr) : make_uint4(0, 0, 0, 0);
+    *reinterpret_cast<uint4*>(v) = raw;
+  } else {
+    float f[8];
+    if (in) {
+      const uint4 raw = *reinterpret_cast<const uint4*>(xr);
+      const __half* h = reinterpret_cast<const __half*>(&raw);
+      if (p.prologue == R4Q_PRO_SILU_FWHT) {
+        const uint4 ru = *reinterpret_cast<const uint4*>(xr + p.K);
+        const __half* hu = reinterpret_cast<const __half*>(&ru);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float g = __half2float(h[j]);
+          f[j] = g / (1.0f + expf(-g)) * __half2float(hu[j]);
+        }
+      } else if (p.prologue == R4Q_PRO_RMSNORM_FWHT) {
+        const uint4 rw = __ldg(reinterpret_cast<const uint4*>(p.norm_w + k0 + 8 * q));
+        const __half* hw = reinterpret_cast<const __half*>(&rw);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) f[j] = __half2float(h[j]) * rrms * __half2float(hw[j]);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) f[j] = __half2float(h[j]);
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) f[j] = 0.0f;
+    }
+#pragma unroll
+    for (int s = 1; s < 8; s <<= 1) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        if ((j & s) == 0) {
+          const float a = f[j], b = f[j + s];
+          f[j] = a + b;
+          f[j + s] = a - b;
+        }
+      }
+    }
+#pragma unroll
+    for (int s = 1; s < 4; s <<= 1) {   // k strides 8 and 16: lane q ^ s
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float o = __shfl_xor_sync(0xffffffffu, f[j], s);
+        f[j] = (q & s) ? (o - f[j]) : (f[j] + o);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = __float2half(f[j] * kInvSqrt32);
+  }
+  if constexpr (DIAG) {
+    float se = 0.0f, so = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 8; j += 2) {
+      se += __half2float(v[j]);
+      so += __half2float(v[j + 1]);
+    }
+    se += __shfl_xor_sync(0xffffffffu, se, 1);
+    so += __shfl_xor_sync(0xffffffffu, so, 1);
+    se += __shfl_xor_sync(0xffffffffu, se, 2);
+    so += __shfl_xor_sync(0xffffffffu, so, 2);
+    if (valid && q == 0) *xsum_slot = make_float2(se + so, 1024.0f * se + 64.0f * so);
+  }
+  if (!valid) return;
+  __half o[8];
+  int sub, chunk;
+  if constexpr (FMT == W_INT4) {
+    o[0] = v[0]; o[1] = v[4]; o[2] = v[1]; o[3] = v[5]; o[4] = v[2]; o[5] = v[6]; o[6] = v[3]; o[7] = v[7];
+    sub = q;
+    chunk = blk;
+  } else if constexpr (FMT == W_INT8) {
+    o[0] = v[0]; o[1] = v[2]; o[2] = v[1]; o[3] = v[3]; o[4] = v[4]; o[5] = v[6]; o[6] = v[5]; o[7] = v[7];
+    sub = q & 1;
+    chunk = 2 * blk + (q >> 1);
+  } else {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o[j] = v[j];
+    sub = 0;
+    chunk = 4 * blk + q;
+  }
+  *reinterpret_cast<uint4*>(xs_col + ((long)sub * nch_pad + chunk) * 16) = *reinterpret_cast<uint4*>(o);
+}
+
 // MMAs per 16-byte chunk: INT4 8 (32 k), INT8 4 (16 k), FP16 2 (8 k).
 template <int FMT> struct ChunkMma { static constexpr int N = FMT == W_INT4 ? 8 : (FMT == W_INT8 ? 4 : 2); };
 

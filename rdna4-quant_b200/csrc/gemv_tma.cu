@@ -23,6 +23,7 @@
 //    outputs (activations, sums of squares, residual) comes after it.
 #include <cuda.h>
 
+#include <cstdlib>
 #include <mutex>
 #include <unordered_map>
 
@@ -34,16 +35,33 @@ constexpr int kTmaConsumers = 16;
 constexpr int kTmaThreads = (kTmaConsumers + 1) * 32;
 constexpr int kTileRows = 64;
 constexpr int kTmaMaxSplit = 32;
-constexpr long kSpinLimit = 1L << 26;  // bounded mbarrier waits (seconds of wall time)
+constexpr long kSpinLimit = 1L << 26;
+
+#ifdef R4Q_TRACE
+// Development-only event trace (compiled only with -DR4Q_TRACE).
+__device__ unsigned long long g_trace[8][256];
+__device__ __forceinline__ unsigned long long gtime() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ int g_dbg_mode;  // 1: consumers only wait/release, 2: dequant without MMA
+#define TRACE(slot, idx) do { int _c = (blockIdx.x == 0) ? 0 : (blockIdx.x == 70 ? 1 : -1); \
+  if (_c >= 0 && (idx) < 256) g_trace[_c * 4 + (slot)][(idx)] = gtime(); } while (0)
+#define DBG_MODE g_dbg_mode
+#else
+#define TRACE(slot, idx) do {} while (0)
+#define DBG_MODE 0
+#endif  // bounded mbarrier waits (seconds of wall time)
 
 // A stage is 64 rows x SK k.
 template <int FMT> struct TmaFmt;
 template <> struct TmaFmt<W_INT4> {
-  static constexpr int SK = 512;         // k per stage
-  static constexpr int CPS = 16;         // 16-byte chunks per row per stage
-  static constexpr int BOXES = 2;        // 128-byte weight boxes per row per stage
-  static constexpr int SBYTES = 64;      // (scale, zero) bytes per row per stage
-  static constexpr int NS = 6;           // ring depth
+  static constexpr int SK = 1024;        // k per stage
+  static constexpr int CPS = 32;         // 16-byte chunks per row per stage
+  static constexpr int BOXES = 4;        // 128-byte weight boxes per row per stage
+  static constexpr int SBYTES = 128;     // (scale, zero) bytes per row per stage
+  static constexpr int NS = 4;           // maximum ring depth
 };
 template <> struct TmaFmt<W_INT8> {
   static constexpr int SK = 512, CPS = 32, BOXES = 4, SBYTES = 32, NS = 4;
@@ -58,6 +76,8 @@ struct TmaParams {
   int tiles;       // 64-row tiles
   int gt;          // CTAs per K split
   int x_bytes;     // activation smem bytes
+  int xsum_bytes;  // per-block activation sums (block-diagonal path)
+  int ns;          // ring depth (stages), sized to the shared memory left
   int* status;     // set to 1 when a bounded wait gives up
 };
 
@@ -79,7 +99,7 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* b) {
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* b, unsigned parity) {
   uint32_t ok;
   asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n"
       " selp.u32 %0, 1, 0, p;\n}\n"
       : "=r"(ok)
       : "r"(smem_u32(b)), "r"(parity)
@@ -108,13 +128,69 @@ __device__ __forceinline__ void consumer_sync() {
   asm volatile("bar.sync 1, %0;" ::"n"(kTmaConsumers * 32) : "memory");
 }
 
+// Shared-space loads on 32-bit addresses (volatile: they must stay after the
+// mbarrier wait that publishes the data).
+__device__ __forceinline__ uint4 lds128(uint32_t a) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ uint32_t lds32(uint32_t a) {
+  uint32_t v;
+  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ uint32_t lds16(uint32_t a) {
+  unsigned short v;
+  asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ float2 lds_f2(uint32_t a) {
+  float2 v;
+  asm volatile("ld.shared.v2.f32 {%0,%1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(a));
+  return v;
+}
+
+__device__ __forceinline__ void named_sync(int id, int n) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
+}
+__device__ __forceinline__ void named_arrive(int id, int n) {
+  asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(n) : "memory");
+}
+
 // Row order inside a 16-row m-tile: rows read by the same quarter-warp
 // (groups 2q, 2q+1) differ in bit 2, so the 128-byte swizzle maps their
 // chunks to disjoint banks.
 __device__ __forceinline__ int row_perm(int g) { return ((g & 1) << 2) | (g >> 1); }
 
+// ------------------------------------------------------- work schedule ---
+// A unit is a run of stages [sb, se) of one 64-row tile; contributor j of the
+// n CTAs (K splits) that share the tile (n == 1: the whole tile).
+struct Seg {
+  int tile, sb, se, j, n;
+};
+
+// CTA (ks, c) of a K-split grid takes tiles c, c + gt, c + 2 gt, ... so that
+// at any time all SMs stream neighbouring tiles.
+struct SegIter {
+  int tiles, gt, tile, st0, st1, ks, S;
+  __device__ __forceinline__ bool next(Seg& sg) {
+    if (tile >= tiles) return false;
+    sg = Seg{tile, st0, st1, ks, S};
+    tile += gt;
+    return true;
+  }
+};
+
 // ------------------------------------------------------------- kernel ----
-template <int FMT, int NG>
+// DIAG (INT4, B <= 2): activation column n of every MMA is (block 2n.., batch
+// n & 1): lane (g, t) feeds its activations only for column g when g >> 1 == t,
+// zeros otherwise, so the accumulator holds one partial sum per (row, block,
+// batch).  The MMA then runs on raw biased nibbles (1024 + q for even k,
+// 64 + q for odd k: one LOP3 per pair, no subtract, no scale multiply) and the
+// bias, zero point and scale are applied once per block in fp32:
+//   sum_k (q - z) x = C - (1024 X_even + 64 X_odd) - z X,  times s.
+template <int FMT, int NG, bool DIAG>
 __global__ void __launch_bounds__(kTmaThreads, 1)
     gemv_tma_kernel(const __grid_constant__ CUtensorMap tmw, const __grid_constant__ CUtensorMap tms,
                     const TmaParams tp) {
@@ -122,7 +198,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
   using F = Fmt<FMT>;
   constexpr int W_STAGE = kTileRows * T::CPS * 16;     // bytes of weights per stage
   constexpr int S_STAGE = kTileRows * T::SBYTES;
-  constexpr int NS = T::NS;
+  const int NS = tp.ns;
   constexpr int V = T::CPS / 16;                       // chunks per thread per row per stage
   constexpr int NM = ChunkMma<FMT>::N;
   const GemvParams& p = tp.p;
@@ -132,11 +208,12 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
   uint8_t* ring_w = smem;
   uint8_t* ring_s = ring_w + NS * W_STAGE;
   uint8_t* xs = ring_s + NS * S_STAGE;
-  float* red = reinterpret_cast<float*>(xs + tp.x_bytes);          // [4 m-tiles][3][NG*4][32]
+  float2* xsum = reinterpret_cast<float2*>(xs + tp.x_bytes);        // [B][chunks] (X, E)
+  uint8_t* zero16 = xs + tp.x_bytes + tp.xsum_bytes;
+  float* red = reinterpret_cast<float*>(zero16 + 16);               // [4 m-tiles][3][NG*4][32]
   uint64_t* full = reinterpret_cast<uint64_t*>(red + 4 * 3 * NG * 4 * 32);
   uint64_t* empty = full + NS;
   __shared__ float s_rrms[16];
-  __shared__ unsigned s_last;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int S = p.ksplit;
@@ -145,7 +222,9 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
   const int st0 = (int)((long)ks * tp.nstages / S);
   const int st1 = (int)((long)(ks + 1) * tp.nstages / S);
   const int nst = st1 - st0;
+  SegIter iter0{tp.tiles, tp.gt, cta_in_split, st0, st1, ks, S};
 
+  if (tid == 0) TRACE(0, 0);
   if (tid == 0) {
     for (int i = 0; i < NS; ++i) {
       mbar_init(&full[i], 1);
@@ -162,18 +241,23 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
       if (T::SBYTES) asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tms)) : "memory");
       int it = 0;
       bool ok = true;
-      for (int tile = cta_in_split; tile < tp.tiles && ok; tile += tp.gt) {
-        for (int st = st0; st < st1 && ok; ++st, ++it) {
+      SegIter iter = iter0;
+      Seg sg;
+      while (ok && iter.next(sg)) {
+        const int tile = sg.tile;
+        for (int st = sg.sb; st < sg.se && ok; ++st, ++it) {
           const int slot = it % NS;
           const unsigned ph = (unsigned)(it / NS) & 1u;
           if (it >= NS) ok = mbar_wait(&empty[slot], ph ^ 1u, tp.status);
           if (!ok) break;
-          mbar_expect_tx(&full[slot], W_STAGE + S_STAGE);
+          TRACE(1, it);
+          const bool load_s = T::SBYTES && DBG_MODE != 3;
+          mbar_expect_tx(&full[slot], W_STAGE + (load_s ? S_STAGE : 0));
 #pragma unroll
           for (int b = 0; b < T::BOXES; ++b)
             tma_load_2d(ring_w + slot * W_STAGE + b * (kTileRows * 128), &tmw,
                         st * (T::CPS * 16) + b * 128, tile * kTileRows, &full[slot]);
-          if (T::SBYTES)
+          if (load_s)
             tma_load_2d(ring_s + slot * S_STAGE, &tms, st * T::SBYTES, tile * kTileRows, &full[slot]);
         }
       }
@@ -210,15 +294,22 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
   {
     const int nblk = nch_pad * F::CK / 32;
     const int k_base = st0 * T::SK;
-    for (int item = ctid; item < ncolx * nblk; item += kTmaConsumers * 32) {
-      const int col = item / nblk, blk = item - col * nblk;
-      __half v[32];
-      load_block32(p, col, k_base + blk * 32,
-                   p.prologue == R4Q_PRO_RMSNORM_FWHT ? s_rrms[col] : 1.0f, v);
-      store_block32<FMT>(xs + (long)col * colstride, nch_pad, blk, v);
+    const int total = ncolx * nblk * 4;                  // (column, block, quarter) items
+    for (int base = warp * 32; base < total; base += kTmaConsumers * 32) {
+      const int item = base + lane;
+      const bool valid = item < total;
+      const int it2 = valid ? item : 0;
+      const int q = it2 & 3, cb = it2 >> 2;
+      const int col = cb / nblk, blk = cb - col * nblk;
+      stage_quad<FMT, DIAG>(p, col, k_base + blk * 32, q,
+                            p.prologue == R4Q_PRO_RMSNORM_FWHT ? s_rrms[col] : 1.0f,
+                            xs + (long)col * colstride, nch_pad, blk, valid,
+                            xsum + col * nch_pad + blk);
     }
+    if (ctid < 4) reinterpret_cast<uint32_t*>(zero16)[ctid] = 0u;
   }
   consumer_sync();
+  if (ctid == 0) TRACE(0, 1);
 
   // warp -> (k quarter, m-tile); every stage is consumed by all 16 warps
   const int g = lane >> 2, t = lane & 3;
@@ -227,10 +318,57 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
   int colx[NG];
 #pragma unroll
   for (int cg = 0; cg < NG; ++cg) colx[cg] = min(cg * 8 + g, p.B - 1);
+  // block-diagonal path: this lane feeds column g (= block g>>1, batch g&1)
+  const bool feed = ((g >> 1) == t) && ((g & 1) < p.B);
+  const uint8_t* xfeed = feed ? xs + (long)(g & 1) * colstride : nullptr;
 
-  int it0 = 0;                                              // ring index of the unit's first stage
+  // Stage-invariant shared-memory offsets of this thread's chunks (the stage
+  // slot base is added per stage).  Chunk v of row r sits in 128-byte box
+  // c >> 3 at 16-byte unit (c & 7) ^ (r & 7) (128-byte swizzle).
+  constexpr int SPT = T::CPS / 4;                           // chunks per warp per row per stage
+  int offA[V], offB[V], soffA[V], soffB[V], cidx[V];
+#pragma unroll
+  for (int v = 0; v < V; ++v) {
+    const int c = part * SPT + 4 * v + t;
+    cidx[v] = c;
+    const int box = c >> 3, cb = c & 7;
+    offA[v] = box * (kTileRows * 128) + ra * 128 + ((cb ^ (ra & 7)) << 4);
+    offB[v] = box * (kTileRows * 128) + rb * 128 + ((cb ^ (rb & 7)) << 4);
+    if constexpr (FMT == W_INT4) {
+      // 128-byte scale rows, 128-byte swizzle: (scale, zero) of block c
+      soffA[v] = ra * 128 + (((c >> 2) ^ (ra & 7)) << 4) + (c & 3) * 4;
+      soffB[v] = rb * 128 + (((c >> 2) ^ (rb & 7)) << 4) + (c & 3) * 4;
+    } else if constexpr (FMT == W_INT8) {
+      // 32-byte scale rows, 32-byte swizzle: fp16 scale of block c >> 1
+      const int bk = c >> 1;
+      soffA[v] = ra * 32 + (((bk >> 3) ^ ((ra >> 2) & 1)) << 4) + (bk & 7) * 2;
+      soffB[v] = rb * 32 + (((bk >> 3) ^ ((rb >> 2) & 1)) << 4) + (bk & 7) * 2;
+    } else {
+      soffA[v] = soffB[v] = 0;
+    }
+  }
+  // activation pointers (block-diagonal path: lanes that feed nothing read a
+  // 16-byte zero line with zero strides)
+  const uint32_t xbase = DIAG ? (feed ? smem_u32(xfeed) + cidx[0] * 16 : smem_u32(zero16)) : 0u;
+  const uint32_t xsub = DIAG ? (feed ? nch_pad * 16 : 0) : nch_pad * 16;   // bytes between sub-rows
+  const uint32_t xstep = DIAG ? (feed ? T::CPS * 16 : 0) : T::CPS * 16;    // bytes per stage
+  uint32_t xrow[NG];
+#pragma unroll
+  for (int cg = 0; cg < NG; ++cg) xrow[cg] = smem_u32(xs) + colx[cg] * colstride;
+  const uint32_t ring_w_u = smem_u32(ring_w), ring_s_u = smem_u32(ring_s);
+  const uint32_t xsum0 = smem_u32(xsum) + cidx[0] * 8, xsum1 = xsum0 + nch_pad * 8;
+
+  int slot = 0;
+  unsigned phase = 0;
   bool ok = true;
-  for (int tile = cta_in_split; tile < tp.tiles; tile += tp.gt, it0 += nst) {
+  int uidx = 0;
+  SegIter iter = iter0;
+  Seg sg;
+  bool more = iter.next(sg);
+  while (more) {
+    const Seg cur = sg;
+    more = iter.next(sg);                                   // is there a next unit?
+    const int tile = cur.tile;
     float acc[NG][2][4];
 #pragma unroll
     for (int cg = 0; cg < NG; ++cg)
@@ -239,148 +377,219 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
 #pragma unroll
         for (int i = 0; i < 4; ++i) acc[cg][h][i] = 0.0f;
 
-    for (int st = 0; st < nst; ++st) {
-      const int it = it0 + st;
-      const int slot = it % NS;
-      const unsigned ph = (unsigned)(it / NS) & 1u;
-      if (ok) ok = mbar_wait(&full[slot], ph, tp.status);
-      const uint8_t* wst = ring_w + slot * W_STAGE;
-      const uint8_t* sst = ring_s + slot * S_STAGE;
-      uint32_t frag[V][NM][4];
-#pragma unroll
-      for (int v = 0; v < V; ++v) {
-        const int c = part * (T::CPS / 4) + 4 * v + t;     // chunk within the stage row
-        const int box = c >> 3, cb = c & 7;
-        RowChunk A, Bq;
-        A.w = *reinterpret_cast<const uint4*>(wst + box * (kTileRows * 128) + ra * 128 + ((cb ^ (ra & 7)) << 4));
-        Bq.w = *reinterpret_cast<const uint4*>(wst + box * (kTileRows * 128) + rb * 128 + ((cb ^ (rb & 7)) << 4));
-        if constexpr (FMT == W_INT4) {
-          // 64-byte rows, 64-byte swizzle: 16-byte unit index ^= row bits 1-2
-          const int ua = ((c >> 2) ^ ((ra >> 1) & 3)) << 4, ub = ((c >> 2) ^ ((rb >> 1) & 3)) << 4;
-          A.s = *reinterpret_cast<const uint32_t*>(sst + ra * 64 + ua + (c & 3) * 4);
-          Bq.s = *reinterpret_cast<const uint32_t*>(sst + rb * 64 + ub + (c & 3) * 4);
-        } else if constexpr (FMT == W_INT8) {
-          // 32-byte rows, 32-byte swizzle: 16-byte half index ^= row bit 2
-          const int b = c >> 1;
-          const int ha = ((b >> 3) ^ ((ra >> 2) & 1)) << 4, hb = ((b >> 3) ^ ((rb >> 2) & 1)) << 4;
-          A.s = *reinterpret_cast<const uint16_t*>(sst + ra * 32 + ha + (b & 7) * 2);
-          Bq.s = *reinterpret_cast<const uint16_t*>(sst + rb * 32 + hb + (b & 7) * 2);
-        } else {
-          A.s = Bq.s = 0;
-        }
-        chunk_dequant<FMT>(A, Bq, frag[v]);
+    for (int st = cur.sb - st0; st < cur.se - st0; ++st) {  // st: stage index inside the staged x
+      if (ok) ok = mbar_wait(&full[slot], phase, tp.status);
+      const uint32_t wst = ring_w_u + slot * W_STAGE;
+      const uint32_t sst = ring_s_u + slot * S_STAGE;
+      uint64_t* emp = &empty[slot];
+      if (++slot == NS) {
+        slot = 0;
+        phase ^= 1u;
       }
-      // the slot is free once its bytes are in registers; the MMAs follow
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[slot]);
+      if (DBG_MODE == 1) {
+        __syncwarp();
+        if (lane == 0) mbar_arrive(emp);
+        continue;
+      }
+      if constexpr (DIAG) {
+        uint4 wa[V], wb[V];
+        uint32_t sza[V], szb[V];
 #pragma unroll
-      for (int v = 0; v < V; ++v) {
-        const int c = part * (T::CPS / 4) + 4 * v + t;
-        chunk_mma_frag<FMT, NG>(frag[v], xs, colstride, nch_pad, st * T::CPS + c, colx, acc);
+        for (int v = 0; v < V; ++v) {
+          wa[v] = lds128(wst + offA[v]);
+          wb[v] = lds128(wst + offB[v]);
+          sza[v] = lds32(sst + soffA[v]);
+          szb[v] = lds32(sst + soffB[v]);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(emp);
+        const uint32_t xst = xbase + st * xstep;
+#pragma unroll
+        for (int v = 0; v < V; ++v) {
+          const uint32_t wa_[4] = {wa[v].x, wa[v].y, wa[v].z, wa[v].w};
+          const uint32_t wb_[4] = {wb[v].x, wb[v].y, wb[v].z, wb[v].w};
+          const uint32_t xv = xst + (feed ? 4 * v * 16 : 0);
+          float c0[4] = {0.f, 0.f, 0.f, 0.f}, c1[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+          for (int m = 0; m < 4; ++m) {
+            const uint32_t a8 = wa_[m] >> 8, b8 = wb_[m] >> 8;
+            const uint32_t alo = lop3_and_or(wa_[m], 0x000F000Fu, 0x64006400u);
+            const uint32_t ahi = lop3_and_or(wa_[m], 0x00F000F0u, 0x54005400u);
+            const uint32_t blo = lop3_and_or(wb_[m], 0x000F000Fu, 0x64006400u);
+            const uint32_t bhi = lop3_and_or(wb_[m], 0x00F000F0u, 0x54005400u);
+            const uint32_t alo2 = lop3_and_or(a8, 0x000F000Fu, 0x64006400u);
+            const uint32_t ahi2 = lop3_and_or(a8, 0x00F000F0u, 0x54005400u);
+            const uint32_t blo2 = lop3_and_or(b8, 0x000F000Fu, 0x64006400u);
+            const uint32_t bhi2 = lop3_and_or(b8, 0x00F000F0u, 0x54005400u);
+            const uint4 xf = lds128(xv + m * xsub);
+            mma16816(c0, alo, blo, ahi, bhi, xf.x, xf.y);
+            mma16816(c1, alo2, blo2, ahi2, bhi2, xf.z, xf.w);
+          }
+          // accumulator column 2t + b = (block of lane t, batch b)
+          const uint32_t xso = (st * T::CPS + 4 * v) * 8;
+          const float2 fa = __half22float2(u32_as_h2(sza[v])), fb = __half22float2(u32_as_h2(szb[v]));
+          const float2 xe0 = lds_f2(xsum0 + xso);
+          acc[0][0][0] += fa.x * ((c0[0] + c1[0]) - fmaf(fa.y, xe0.x, xe0.y));
+          acc[0][0][2] += fb.x * ((c0[2] + c1[2]) - fmaf(fb.y, xe0.x, xe0.y));
+          if (p.B > 1) {
+            const float2 xe1 = lds_f2(xsum1 + xso);
+            acc[0][0][1] += fa.x * ((c0[1] + c1[1]) - fmaf(fa.y, xe1.x, xe1.y));
+            acc[0][0][3] += fb.x * ((c0[3] + c1[3]) - fmaf(fb.y, xe1.x, xe1.y));
+          }
+        }
+      } else {
+        uint32_t frag[V][NM][4];
+#pragma unroll
+        for (int v = 0; v < V; ++v) {
+          RowChunk A, Bq;
+          A.w = lds128(wst + offA[v]);
+          Bq.w = lds128(wst + offB[v]);
+          if constexpr (FMT == W_INT4) {
+            A.s = lds32(sst + soffA[v]);
+            Bq.s = lds32(sst + soffB[v]);
+          } else if constexpr (FMT == W_INT8) {
+            A.s = lds16(sst + soffA[v]);
+            Bq.s = lds16(sst + soffB[v]);
+          } else {
+            A.s = Bq.s = 0;
+          }
+          chunk_dequant<FMT>(A, Bq, frag[v]);
+        }
+        // the slot is free once its bytes are in registers; the MMAs follow
+        __syncwarp();
+        if (lane == 0) mbar_arrive(emp);
+#pragma unroll
+        for (int v = 0; v < V; ++v) {
+          const int off = (st * T::CPS + cidx[v]) * 16;
+#pragma unroll
+          for (int cg = 0; cg < NG; ++cg) {
+#pragma unroll
+            for (int sub = 0; sub < NM / 2; ++sub) {
+              const uint4 xf = lds128(xrow[cg] + off + sub * xsub);
+              const int j = 2 * sub;
+              mma16816(acc[cg][0], frag[v][j][0], frag[v][j][1], frag[v][j][2], frag[v][j][3], xf.x, xf.y);
+              mma16816(acc[cg][1], frag[v][j + 1][0], frag[v][j + 1][1], frag[v][j + 1][2], frag[v][j + 1][3], xf.z, xf.w);
+            }
+          }
+        }
       }
     }
+    if constexpr (DIAG) {
+      // the 4 lanes of a group hold different blocks: sum them
 #pragma unroll
-    for (int cg = 0; cg < NG; ++cg)
+      for (int i = 0; i < 4; ++i) {
+        float v = acc[0][0][i];
+        v += __shfl_xor_sync(0xffffffffu, v, 1);
+        v += __shfl_xor_sync(0xffffffffu, v, 2);
+        acc[0][0][i] = v;
+      }
+    } else {
 #pragma unroll
-      for (int i = 0; i < 4; ++i) acc[cg][0][i] += acc[cg][1][i];
+      for (int cg = 0; cg < NG; ++cg)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) acc[cg][0][i] += acc[cg][1][i];
+    }
 
-    // ---- combine the 4 k-quarter partials of each m-tile (fixed order) ----
+    // ---- combine the 4 k-quarter partials of this m-tile (fixed order).
+    // Only the 4 warps of the m-tile synchronise: writers arrive on barrier
+    // 2+mt, the reader waits on it; the reader arrives on 6+mt once red[] is
+    // consumed, which the writers wait for before their next write.
+    ++uidx;
     if (part != 0) {
+      if (uidx > 1) named_sync(6 + mt, 128);
 #pragma unroll
       for (int cg = 0; cg < NG; ++cg)
 #pragma unroll
         for (int i = 0; i < 4; ++i) red[(((mt * 3 + part - 1) * NG + cg) * 4 + i) * 32 + lane] = acc[cg][0][i];
+      named_arrive(2 + mt, 128);
+      continue;
     }
-    consumer_sync();
+    named_sync(2 + mt, 128);
+    float r[NG][4];
+#pragma unroll
+    for (int cg = 0; cg < NG; ++cg)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        float v = acc[cg][0][i];
+#pragma unroll
+        for (int q = 0; q < 3; ++q) v += red[(((mt * 3 + q) * NG + cg) * 4 + i) * 32 + lane];
+        r[cg][i] = v;
+      }
+    if (more) named_arrive(6 + mt, 128);
     const int row0 = tile * kTileRows + mt * 16;
-    if (part == 0 && row0 < p.N) {
-      float r[NG][4];
+    if (row0 >= p.N) continue;
+    const int row_a = tile * kTileRows + ra, row_b = tile * kTileRows + rb;
+    if (cur.n == 1) {
+#pragma unroll
+      for (int cg = 0; cg < NG; ++cg) {
+        float sq[2] = {0.0f, 0.0f};
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int c = cg * 8 + 2 * t + h;
+          if (c < p.B) {
+            float va = __half2float(__float2half(r[cg][h]));
+            float vb = __half2float(__float2half(r[cg][2 + h]));
+            if (p.res) {
+              va += __half2float(p.res[(long)c * p.ldres + row_a]);
+              vb += __half2float(p.res[(long)c * p.ldres + row_b]);
+            }
+            sq[h] = va * va + vb * vb;
+            p.y[(long)c * p.ldy + row_a] = __float2half(va);
+            p.y[(long)c * p.ldy + row_b] = __float2half(vb);
+          }
+        }
+        if (p.ss_out) {
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            float v = sq[h];
+            v += __shfl_xor_sync(0xffffffffu, v, 4);
+            v += __shfl_xor_sync(0xffffffffu, v, 8);
+            v += __shfl_xor_sync(0xffffffffu, v, 16);
+            const int c = cg * 8 + 2 * t + h;
+            if (g == 0 && c < p.B) p.ss_out[(long)(row0 >> 4) * p.B + c] = v;
+          }
+        }
+      }
+    } else {
+      // split K: store this split's partial for the 16 rows; the warp that
+      // arrives last for this m-tile sums the partials in split order
+      float* prt = p.part + (long)cur.j * p.B * p.N;
 #pragma unroll
       for (int cg = 0; cg < NG; ++cg)
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          float v = acc[cg][0][i];
-#pragma unroll
-          for (int q = 0; q < 3; ++q) v += red[(((mt * 3 + q) * NG + cg) * 4 + i) * 32 + lane];
-          r[cg][i] = v;
-        }
-      const int row_a = tile * kTileRows + ra, row_b = tile * kTileRows + rb;
-      if (S == 1) {
-#pragma unroll
-        for (int cg = 0; cg < NG; ++cg) {
-          float sq[2] = {0.0f, 0.0f};
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            const int c = cg * 8 + 2 * t + h;
-            if (c < p.B) {
-              float va = __half2float(__float2half(r[cg][h]));
-              float vb = __half2float(__float2half(r[cg][2 + h]));
-              if (p.res) {
-                va += __half2float(p.res[(long)c * p.ldres + row_a]);
-                vb += __half2float(p.res[(long)c * p.ldres + row_b]);
-              }
-              sq[h] = va * va + vb * vb;
-              p.y[(long)c * p.ldy + row_a] = __float2half(va);
-              p.y[(long)c * p.ldy + row_b] = __float2half(vb);
-            }
-          }
-          if (p.ss_out) {
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-              float v = sq[h];
-              v += __shfl_xor_sync(0xffffffffu, v, 4);
-              v += __shfl_xor_sync(0xffffffffu, v, 8);
-              v += __shfl_xor_sync(0xffffffffu, v, 16);
-              const int c = cg * 8 + 2 * t + h;
-              if (g == 0 && c < p.B) p.ss_out[(long)(row0 >> 4) * p.B + c] = v;
-            }
+        for (int h = 0; h < 2; ++h) {
+          const int c = cg * 8 + 2 * t + h;
+          if (c < p.B) {
+            prt[(long)c * p.N + row_a] = r[cg][h];
+            prt[(long)c * p.N + row_b] = r[cg][2 + h];
           }
         }
-      } else {
-        float* prt = p.part + (long)ks * p.B * p.N;
-#pragma unroll
-        for (int cg = 0; cg < NG; ++cg)
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            const int c = cg * 8 + 2 * t + h;
-            if (c < p.B) {
-              prt[(long)c * p.N + row_a] = r[cg][h];
-              prt[(long)c * p.N + row_b] = r[cg][2 + h];
-            }
-          }
-      }
-    }
-    if (S > 1) {
-      // the partial stores of this CTA are ordered before thread 0's gpu-scope
-      // acq_rel atomic by the barrier; the last arriving CTA of the tile sums
-      // the split partials in split order
-      consumer_sync();
-      if (ctid == 0) {
+      __syncwarp();
+      unsigned last = 0;
+      if (lane == 0) {
         unsigned old;
-        asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(old) : "l"(p.cnt + tile) : "memory");
-        s_last = (old == (unsigned)S - 1) ? 1u : 0u;
+        asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(old) : "l"(p.cnt + (row0 >> 4)) : "memory");
+        last = (old == (unsigned)cur.n - 1) ? 1u : 0u;
       }
-      consumer_sync();
-      if (s_last) {
-        const int trow0 = tile * kTileRows;
-        const int tiles16 = min(4, (p.N - trow0) >> 4);
-        for (int task = warp; task < tiles16 * p.B; task += kTmaConsumers) {
-          const int ti = task / p.B, col = task - ti * p.B;
-          const int rr = trow0 + ti * 16 + (lane & 15);
+      last = __shfl_sync(0xffffffffu, last, 0);
+      if (last) {
+        const int rr = row0 + (lane & 15);
+        for (int col = 0; col < p.B; ++col) {
           float v = 0.0f;
-          for (int k2 = 0; k2 < S; ++k2) v += __ldcg(p.part + ((long)k2 * p.B + col) * p.N + rr);
+          for (int k2 = 0; k2 < cur.n; ++k2) v += __ldcg(p.part + ((long)k2 * p.B + col) * p.N + rr);
           v = __half2float(__float2half(v));
           if (p.res) v += __half2float(p.res[(long)col * p.ldres + rr]);
           if (lane < 16) p.y[(long)col * p.ldy + rr] = __float2half(v);
           float sq = (lane < 16) ? v * v : 0.0f;
           sq = warp_sum(sq);
-          if (p.ss_out && lane == 0) p.ss_out[(long)((trow0 >> 4) + ti) * p.B + col] = sq;
+          if (p.ss_out && lane == 0) p.ss_out[(long)(row0 >> 4) * p.B + col] = sq;
         }
-        if (ctid == 0) p.cnt[tile] = 0u;
+        if (lane == 0) p.cnt[row0 >> 4] = 0u;
       }
     }
-    consumer_sync();  // red[] and s_last are reused by the next tile
+    if (ctid == 0) TRACE(3, uidx);
   }
+  if (ctid == 0) TRACE(0, 2);
 }
 
 // --------------------------------------------------------------- host ----
@@ -428,11 +637,13 @@ struct TmaPlan {
   int S, gt;
   size_t smem;
   int x_bytes;
+  int xsum_bytes;
+  int ns;
 };
 
 // Largest dynamic shared memory this kernel may use: the per-block opt-in
 // limit minus its static shared memory.  Sets the attribute once per device.
-template <int FMT, int NG>
+template <int FMT, int NG, bool DIAG>
 static size_t tma_smem_limit() {
   static std::mutex mu;
   static std::unordered_map<int, size_t> lim;
@@ -445,9 +656,9 @@ static size_t tma_smem_limit() {
   cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
   cudaFuncAttributes fa{};
   size_t v = 0;
-  if (optin > 0 && cudaFuncGetAttributes(&fa, gemv_tma_kernel<FMT, NG>) == cudaSuccess) {
+  if (optin > 0 && cudaFuncGetAttributes(&fa, gemv_tma_kernel<FMT, NG, DIAG>) == cudaSuccess) {
     v = (size_t)optin - fa.sharedSizeBytes;
-    if (cudaFuncSetAttribute(gemv_tma_kernel<FMT, NG>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    if (cudaFuncSetAttribute(gemv_tma_kernel<FMT, NG, DIAG>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)v) != cudaSuccess)
       v = 0;
   }
@@ -456,17 +667,17 @@ static size_t tma_smem_limit() {
   return v;
 }
 
-template <int FMT, int NG>
+template <int FMT, int NG, bool DIAG>
 static TmaPlan plan_tma(int B, int N, int K, size_t ws_bytes) {
   using T = TmaFmt<FMT>;
   using F = Fmt<FMT>;
   const int nsm = num_sms();
   const int tiles = (N + kTileRows - 1) / kTileRows;
   const int nst = (K + T::SK - 1) / T::SK;
-  const size_t fixed = 1024 + (size_t)T::NS * (kTileRows * T::CPS * 16 + kTileRows * T::SBYTES) +
-                       4 * 3 * NG * 4 * 32 * 4 + 2 * T::NS * 8;
-  const size_t smem_limit = tma_smem_limit<FMT, NG>();
-  TmaPlan best{1, 1, 0, 0};
+  const size_t stage = (size_t)kTileRows * T::CPS * 16 + (size_t)kTileRows * T::SBYTES;
+  const size_t fixed = 1024 + 4 * 3 * NG * 4 * 32 * 4 + 2 * T::NS * 8 + 16;
+  const size_t smem_limit = tma_smem_limit<FMT, NG, DIAG>();
+  TmaPlan best{1, 1, 0, 0, 0, 0};
   double best_cost = 1e30;
   for (int S = 1; S <= kTmaMaxSplit && S <= nst; ++S) {
     const int gt = nsm / S;
@@ -475,29 +686,36 @@ static TmaPlan plan_tma(int B, int N, int K, size_t ws_bytes) {
     const int per = (nst + S - 1) / S;                       // stages per unit (max)
     const int colstride = x_colstride(per * T::CPS / 4 / F::U, F::NSUB, F::U);
     const size_t xb = (size_t)colstride * B;
-    if (fixed + xb > smem_limit) continue;
+    const size_t xsb = DIAG ? (size_t)2 * per * T::CPS * sizeof(float2) : 0;
+    if (fixed + xb + xsb + 2 * stage > smem_limit) continue;
+    // the ring takes all shared memory the activations leave: under full HBM
+    // load a stage takes microseconds to land, so depth is bandwidth
+    int ns = (int)((smem_limit - fixed - xb - xsb) / stage);
+    if (ns > T::NS) ns = T::NS;
     const int rounds = (tiles + gt - 1) / gt;
-    // busiest CTA streams rounds * per stages; S > 1 adds a merge per tile
-    const double cost = (double)rounds * per + (S > 1 ? 0.35 * rounds : 0.0) + 0.02 * S;
+    // busiest CTA streams rounds * per stages (slower with a shallow ring);
+    // S > 1 adds a partial merge per tile
+    const double depth_pen = ns < 8 ? (8.0 - ns) * 0.08 : 0.0;
+    const double cost = (double)rounds * per * (1.0 + depth_pen) + (S > 1 ? 1.0 * rounds : 0.0) + 0.02 * S;
     if (cost < best_cost) {
       best_cost = cost;
-      best = TmaPlan{S, gt, fixed + xb, (int)xb};
+      best = TmaPlan{S, gt, fixed + xb + xsb + (size_t)ns * stage, (int)xb, (int)xsb, ns};
     }
   }
   return best;
 }
 
-template <int FMT, int NG>
+template <int FMT, int NG, bool DIAG>
 static int launch_tma_t(const GemvArgs& a) {
   using T = TmaFmt<FMT>;
-  const TmaPlan pl = plan_tma<FMT, NG>(a.B, a.N, a.K, a.ws_bytes);
+  const TmaPlan pl = plan_tma<FMT, NG, DIAG>(a.B, a.N, a.K, a.ws_bytes);
   if (pl.smem == 0) return set_error(R4Q_ERR_CAPACITY, "gemv: no TMA plan fits shared memory");
   if (pl.S > 1 && !a.ws) return set_error(R4Q_ERR_CAPACITY, "gemv: workspace required");
   CUtensorMap tmw, tms;
   const long rowbytes = (FMT == W_INT4) ? a.K / 2 : (FMT == W_INT8 ? a.K : 2L * a.K);
   int st = make_map(&tmw, a.w, a.N, rowbytes, 128, kTileRows, CU_TENSOR_MAP_SWIZZLE_128B);
   if (st) return st;
-  if (FMT == W_INT4) st = make_map(&tms, a.s, a.N, a.K / 8, 64, kTileRows, CU_TENSOR_MAP_SWIZZLE_64B);
+  if (FMT == W_INT4) st = make_map(&tms, a.s, a.N, a.K / 8, 128, kTileRows, CU_TENSOR_MAP_SWIZZLE_128B);
   else if (FMT == W_INT8) st = make_map(&tms, a.s, a.N, a.K / 16, 32, kTileRows, CU_TENSOR_MAP_SWIZZLE_32B);
   else tms = tmw;
   if (st) return st;
@@ -527,6 +745,8 @@ static int launch_tma_t(const GemvArgs& a) {
   tp.tiles = (a.N + kTileRows - 1) / kTileRows;
   tp.gt = pl.gt;
   tp.x_bytes = pl.x_bytes;
+  tp.xsum_bytes = pl.xsum_bytes;
+  tp.ns = pl.ns;
   tp.status = a.ws ? reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(a.ws) + gemv_cnt_bytes(a.N) - 4) : nullptr;
 
   cudaLaunchConfig_t cfg{};
@@ -539,7 +759,7 @@ static int launch_tma_t(const GemvArgs& a) {
   attrs[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attrs;
   cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, gemv_tma_kernel<FMT, NG>, tmw, tms, tp);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, gemv_tma_kernel<FMT, NG, DIAG>, tmw, tms, tp);
   if (e != cudaSuccess) {
     cudaGetLastError();
     return set_error(R4Q_ERR_CUDA, "gemv_tma_kernel (smem %zu): %s", pl.smem, cudaGetErrorString(e));
@@ -547,12 +767,27 @@ static int launch_tma_t(const GemvArgs& a) {
   return R4Q_OK;
 }
 
+#ifdef R4Q_TRACE
+extern "C" int r4q_trace_read(unsigned long long* host) {
+  return cudaMemcpyFromSymbol(host, g_trace, sizeof(g_trace)) == cudaSuccess ? 0 : -4;
+}
+extern "C" int r4q_trace_mode(int m) {
+  return cudaMemcpyToSymbol(g_dbg_mode, &m, sizeof(int)) == cudaSuccess ? 0 : -4;
+}
+extern "C" int r4q_trace_clear() {
+  static unsigned long long z[8][256];
+  return cudaMemcpyToSymbol(g_trace, z, sizeof(g_trace)) == cudaSuccess ? 0 : -4;
+}
+#endif
+
 int launch_gemv_tma(const GemvArgs& a, int fmt) {
   const bool two = a.B > 8;
   switch (fmt) {
-    case W_INT4: return two ? launch_tma_t<W_INT4, 2>(a) : launch_tma_t<W_INT4, 1>(a);
-    case W_INT8: return two ? launch_tma_t<W_INT8, 2>(a) : launch_tma_t<W_INT8, 1>(a);
-    case W_FP16: return two ? launch_tma_t<W_FP16, 2>(a) : launch_tma_t<W_FP16, 1>(a);
+    case W_INT4:
+      if (a.B <= 2) return launch_tma_t<W_INT4, 1, true>(a);
+      return two ? launch_tma_t<W_INT4, 2, false>(a) : launch_tma_t<W_INT4, 1, false>(a);
+    case W_INT8: return two ? launch_tma_t<W_INT8, 2, false>(a) : launch_tma_t<W_INT8, 1, false>(a);
+    case W_FP16: return two ? launch_tma_t<W_FP16, 2, false>(a) : launch_tma_t<W_FP16, 1, false>(a);
   }
   return set_error(R4Q_ERR_ARG, "gemv: unknown weight format %d", fmt);
 }

@@ -56,7 +56,7 @@ def test_gemv_int4(ops, N, K, B):
     close(y, O.gemv_int4_blockwise(x, packed, sz), 2e-3)
 
 
-@pytest.mark.parametrize("B", [1, 3, 8, 9])
+@pytest.mark.parametrize("B", [1, 2, 3, 8, 9])
 def test_gemv_int4_odd_batches(ops, B):
     rng = np.random.default_rng(B)
     N, K = 512, 1024
