@@ -39,7 +39,7 @@ LAYER_SHAPES = [  # (name, N, K, prologue)
 METRIC = "INT4 GEMV HBM GB/s (Qwen3-14B decode-layer GEMV set)"
 # dram__bytes_read.sum + dram__bytes_write.sum of one gate_up launch at B=1,
 # from the ncu capture summarised in profiles/gemv_tma_int4_gate_up_b1.md
-TRAFFIC_GATE_UP_B1 = None
+TRAFFIC_GATE_UP_B1 = 111478016 + 4093696
 
 
 def parse():
@@ -51,6 +51,8 @@ def parse():
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--layers", type=int, default=40)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--kernel-probe", default=None, choices=[n for n, *_ in LAYER_SHAPES],
+                    help="run one GEMV of this shape 4 times and exit (for ncu captures)")
     return ap.parse_args()
 
 
@@ -360,9 +362,27 @@ def main_reference(a):
     print(json.dumps(line), flush=True)
 
 
+def kernel_probe(a):
+    import torch
+    from r4q import lib as Lb, ops, synth
+    dev = torch.device("cuda", 0)
+    name, N, K, pro = next(t for t in LAYER_SHAPES if t[0] == a.kernel_probe)
+    g = torch.Generator(device=dev).manual_seed(0)
+    _, w, sc = synth.linear_int4(N, K, g, dev)
+    kin = 2 * K if pro == "silu_fwht" else K
+    x = torch.randn(a.batch, kin, device=dev, generator=g).half()
+    prol = Lb.PRO_SILU_FWHT if pro == "silu_fwht" else Lb.PRO_FWHT
+    for _ in range(4):
+        ops.gemv("int4", x, w, sc, N, K, prologue=prol)
+    torch.cuda.synchronize()
+    print(f"probe {name} N={N} K={K} B={a.batch} ok")
+
+
 if __name__ == "__main__":
     args = parse()
-    if args.impl == "reference":
+    if args.kernel_probe:
+        kernel_probe(args)
+    elif args.impl == "reference":
         main_reference(args)
     else:
         main_ours(args)
