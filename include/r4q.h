@@ -102,6 +102,20 @@ int r4q_gemv(int wfmt, const void* x, long ldx, const void* w, const void* s, vo
              int B, int N, int K, int prologue, const r4q_gemv_fused* fused, void* workspace,
              size_t ws_bytes, void* stream);
 
+/* Same as r4q_gemv_int4, but allocates nothing and takes no workspace: for
+ * callers that cannot call cudaMalloc (inside a stream capture that must not
+ * allocate, or a plugin whose host process owns all device memory).  No
+ * counterpart in the reference.  Its split-K scratch is a fixed 4.06 MiB
+ * static device array held by every GPU that loads the library; calls with
+ * B * N > 524288 are rejected with R4Q_ERR_CAPACITY.  The first call on a
+ * device looks up the array's device address (cudaGetSymbolAddress), so make
+ * it before any stream capture.  Every call clears the scratch's counters on
+ * `stream`; all calls on one device share the array, so calls that overlap on
+ * the GPU (e.g. on different streams) race and must be serialised by the
+ * caller. */
+int r4q_gemv_int4_noalloc(const void* x, long ldx, const void* w, const void* sz, void* y,
+                          long ldy, int B, int N, int K, int prologue, void* stream);
+
 /* --------------------------------------------------------- conversions --- */
 /* out[N, K] fp16 = fp16((q - z) * s); bit-exact to `dequant_int4_kernel`
  * (int4_decode_step.hip:3568-3603) and dequantize_int4_asym

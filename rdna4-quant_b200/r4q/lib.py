@@ -52,6 +52,7 @@ _SIGS = {
     "r4q_gemv_fp16": (i32, [vp, i64, vp, vp, i64, i32, i32, i32, i32, vp, sz_t, vp]),
     "r4q_gemv": (i32, [i32, vp, i64, vp, vp, vp, i64, i32, i32, i32, i32, C.POINTER(GemvFused),
                        vp, sz_t, vp]),
+    "r4q_gemv_int4_noalloc": (i32, [vp, i64, vp, vp, vp, i64, i32, i32, i32, i32, vp]),
     "r4q_dequant_int4": (i32, [vp, vp, vp, i32, i32, vp]),
     "r4q_fp16_to_fp8": (i32, [vp, vp, i64, vp]),
     "r4q_fp8_to_fp32": (i32, [vp, vp, i64, vp]),
