@@ -116,6 +116,32 @@ int r4q_gemv(int wfmt, const void* x, long ldx, const void* w, const void* s, vo
 int r4q_gemv_int4_noalloc(const void* x, long ldx, const void* w, const void* sz, void* y,
                           long ldy, int B, int N, int K, int prologue, void* stream);
 
+/* ----------------------------------------------------- norms and heads --- */
+/* y[r] = fp16(v * rsqrt(mean(v^2) + eps) * w) with v = x[r] (+ res[r]) in fp32;
+ * res_out[r] = fp16(v) when given.  x/res rows are ldx apart, y/res_out are
+ * contiguous [rows, D].  RMSNorm.forward (engine_utils.py:58-63), fused_rmsnorm
+ * (fused_ops.py:12-41), rmsnorm_ds / fused_res_norm (int4_decode_step.hip:795-846). */
+int r4q_rmsnorm(const void* x, const void* res, const void* w, void* y, void* res_out, int rows,
+                int D, long ldx, float eps, void* stream);
+
+enum { R4Q_HEAD_NORM = 1, R4Q_HEAD_ROPE = 2, R4Q_HEAD_KV = 4 };
+/* Per-head RMSNorm (flag NORM), half-split RoPE at position `pos` (ROPE), and
+ * the FP8 KV-cache write of K (after norm+RoPE) and V at `pos` (KV), in fp32
+ * with one fp16 rounding.  q: [B][ld_in] with H heads of D, k and v likewise
+ * with Hk heads; outputs q_out/k_out [B][ld_out] (may alias the inputs; NULL
+ * skips); caches [B, Hk, max_seq, D] uint8; tables fp16 [rows][tab_stride],
+ * row `pos`.  pos_dev (int64 [B], device) overrides `pos` per batch row (graph
+ * replay).  k_scale/v_scale (fp32 [B, Hk], optional): the stored byte is
+ * enc(x / scale).  Replaces head_rmsnorm_rope_kv (int4_decode_step.hip:1620-1683),
+ * head_rmsnorm (:849), rope_ds (:888), fused_qknorm_rope_decode and
+ * fused_rope_decode (fused_ops.py:155-215). */
+int r4q_head_norm_rope(void* q, void* k, const void* v, const void* q_norm_w,
+                       const void* k_norm_w, const void* cos_tab, const void* sin_tab,
+                       long tab_stride, int pos, const long long* pos_dev, void* q_out,
+                       void* k_out, void* k_cache, void* v_cache, const float* k_scale,
+                       const float* v_scale, int B, int H, int Hk, int D, long ld_in,
+                       long ld_out, int max_seq, float eps, int flags, void* stream);
+
 /* --------------------------------------------------------- conversions --- */
 /* out[N, K] fp16 = fp16((q - z) * s); bit-exact to `dequant_int4_kernel`
  * (int4_decode_step.hip:3568-3603) and dequantize_int4_asym

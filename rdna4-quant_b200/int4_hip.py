@@ -10,6 +10,7 @@ from __future__ import annotations
 
 import torch
 
+from r4q import lib as _lib
 from r4q import ops as _ops
 
 
@@ -39,3 +40,35 @@ def fp16_to_fp8(src: torch.Tensor) -> torch.Tensor:
     """fp16 tensor -> uint8 tensor of the same shape, reference E4M3 encoder
     (int4_decode_step.hip:3606-3618)."""
     return _ops.fp16_to_fp8(src)
+
+
+def dbg_rmsnorm(X: torch.Tensor, W: torch.Tensor, eps: float) -> torch.Tensor:
+    """RMSNorm of the flat vector X (int4_decode_step.hip:3473-3484)."""
+    return _ops.rmsnorm(X.reshape(1, -1), W, eps).reshape(X.shape)
+
+
+def dbg_fused_res_norm(X: torch.Tensor, Res: torch.Tensor, W: torch.Tensor, eps: float):
+    """[Y, ResOut]: r = X + Res in fp32, Y = RMSNorm(r) from the unrounded r,
+    ResOut = fp16(r) (int4_decode_step.hip:818-846, 3524-3539)."""
+    y, r = _ops.rmsnorm(X.reshape(1, -1), W, eps, res=Res.reshape(1, -1), want_res=True)
+    return [y.reshape(X.shape), r.reshape(X.shape)]
+
+
+def dbg_head_rmsnorm(Q, K, QW, KW, H, Hk, D, eps):
+    """[Q_out, K_out]: per-head RMSNorm of flat Q [H*D], K [Hk*D] (hip:849-884, 3486-3504)."""
+    H, Hk, D = int(H), int(Hk), int(D)
+    qo, ko = torch.empty_like(Q), torch.empty_like(K)
+    _ops.head_norm_rope(Q, K, q_w=QW, k_w=KW, q_out=qo, k_out=ko, H=H, Hk=Hk, D=D,
+                        ld_in=0, ld_out=0, eps=eps, flags=_lib.HEAD_NORM)
+    return [qo, ko]
+
+
+def dbg_rope(Q, K, COS, SIN, H, Hk, D):
+    """[Q_out, K_out]: half-split RoPE with the table rows COS/SIN [D/2]
+    (hip:888-912, 3506-3522)."""
+    H, Hk, D = int(H), int(Hk), int(D)
+    qo, ko = torch.empty_like(Q), torch.empty_like(K)
+    _ops.head_norm_rope(Q, K, cos=COS.reshape(1, -1), sin=SIN.reshape(1, -1), pos=0,
+                        q_out=qo, k_out=ko, H=H, Hk=Hk, D=D, ld_in=0, ld_out=0,
+                        flags=_lib.HEAD_ROPE)
+    return [qo, ko]

@@ -53,6 +53,9 @@ _SIGS = {
     "r4q_gemv": (i32, [i32, vp, i64, vp, vp, vp, i64, i32, i32, i32, i32, C.POINTER(GemvFused),
                        vp, sz_t, vp]),
     "r4q_gemv_int4_noalloc": (i32, [vp, i64, vp, vp, vp, i64, i32, i32, i32, i32, vp]),
+    "r4q_rmsnorm": (i32, [vp, vp, vp, vp, vp, i32, i32, i64, f32, vp]),
+    "r4q_head_norm_rope": (i32, [vp, vp, vp, vp, vp, vp, vp, i64, i32, vp, vp, vp, vp, vp, vp, vp,
+                                 i32, i32, i32, i32, i64, i64, i32, f32, i32, vp]),
     "r4q_dequant_int4": (i32, [vp, vp, vp, i32, i32, vp]),
     "r4q_fp16_to_fp8": (i32, [vp, vp, i64, vp]),
     "r4q_fp8_to_fp32": (i32, [vp, vp, i64, vp]),
@@ -80,3 +83,4 @@ def call(name: str, *args) -> None:
 # activation prologues (enum in include/r4q.h)
 PRO_NONE, PRO_FWHT, PRO_SILU_FWHT, PRO_RMSNORM_FWHT = 0, 1, 2, 3
 W_INT4, W_INT8, W_FP16 = 0, 1, 2
+HEAD_NORM, HEAD_ROPE, HEAD_KV = 1, 2, 4

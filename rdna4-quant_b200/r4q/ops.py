@@ -112,3 +112,34 @@ def fp8_to_fp32(src: torch.Tensor) -> torch.Tensor:
     out = torch.empty(s.shape, dtype=torch.float32, device=dev)
     L.call("r4q_fp8_to_fp32", s.data_ptr(), out.data_ptr(), s.numel(), stream_handle(dev))
     return out
+
+
+def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float = 1e-6, res: torch.Tensor | None = None,
+            want_res: bool = False):
+    """y = fp16(v * rsqrt(mean(v^2) + eps) * w), v = x (+ res) over the last axis."""
+    dev = _require_cuda(x, w)
+    D = x.shape[-1]
+    x2 = x.reshape(-1, D).contiguous()
+    r2 = None if res is None else res.reshape(-1, D).contiguous()
+    y = torch.empty_like(x2)
+    ro = torch.empty_like(x2) if want_res else None
+    L.call("r4q_rmsnorm", x2.data_ptr(), _ptr(r2), w.data_ptr(), y.data_ptr(), _ptr(ro),
+           x2.shape[0], D, D, float(eps), stream_handle(dev))
+    y = y.reshape(x.shape)
+    return (y, ro.reshape(x.shape)) if want_res else y
+
+
+def head_norm_rope(q, k, *, v=None, q_w=None, k_w=None, cos=None, sin=None, pos=0,
+                   pos_dev=None, q_out=None, k_out=None, k_cache=None, v_cache=None,
+                   k_scale=None, v_scale=None, B=1, H=0, Hk=0, D=128, ld_in=None, ld_out=None,
+                   eps=1e-6, flags=0):
+    """Per-head norm / RoPE / FP8 KV write (r4q_head_norm_rope); tensors as described
+    in include/r4q.h.  Outputs are written in place into q_out / k_out."""
+    dev = _require_cuda(q if q is not None else k)
+    max_seq = 0 if k_cache is None else int(k_cache.shape[-2])
+    L.call("r4q_head_norm_rope", _ptr(q), _ptr(k), _ptr(v), _ptr(q_w), _ptr(k_w), _ptr(cos),
+           _ptr(sin), 0 if cos is None else cos.stride(0), int(pos), _ptr(pos_dev), _ptr(q_out),
+           _ptr(k_out), _ptr(k_cache), _ptr(v_cache), _ptr(k_scale), _ptr(v_scale), B, H, Hk, D,
+           ld_in if ld_in is not None else (H + 2 * Hk) * D,
+           ld_out if ld_out is not None else (H + 2 * Hk) * D,
+           max_seq, float(eps), flags, stream_handle(dev))
