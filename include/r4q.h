@@ -142,6 +142,25 @@ int r4q_head_norm_rope(void* q, void* k, const void* v, const void* q_norm_w,
                        const float* v_scale, int B, int H, int Hk, int D, long ld_in,
                        long ld_out, int max_seq, float eps, int flags, void* stream);
 
+/* --------------------------------------------------------------- attention --- */
+enum { R4Q_ATTN_FWHT = 1 };
+/* Bytes of workspace r4q_flash_decode needs (zero once before first use; left
+ * zeroed by every call). */
+size_t r4q_flash_decode_workspace_bytes(int B, int H, int Hk, int max_seq);
+/* o[b, h, :] = softmax(q[b,h]·K^T / sqrt(D)) V over positions [0, seq) of the
+ * FP8 cache of kv head h / (H / Hk), fp32 softmax/accumulate, fp16 out; with
+ * R4Q_ATTN_FWHT the H32 FWHT is applied to every 32-element block of each head
+ * (as the reference's reduce does before o_proj).  q: fp16 [B][ldq] with H
+ * heads of D = 128; caches uint8 [B, Hk, max_seq, 128] (reference codec);
+ * k_scale/v_scale fp32 [B, Hk] or NULL (stored byte = enc(x / scale)); seq =
+ * seq_dev[b] (int64, device) when given, else seq_len.  Replaces
+ * flash_decode_partial/_reduce/_fused and launch_flash_decode
+ * (int4_decode_step.hip:1326-1593); Q is kept in full precision. */
+int r4q_flash_decode(const void* q, long ldq, const void* k_cache, const void* v_cache,
+                     const float* k_scale, const float* v_scale, void* o, long ldo, int B, int H,
+                     int Hk, int D, int max_seq, int seq_len, const long long* seq_dev, int flags,
+                     void* workspace, size_t ws_bytes, void* stream);
+
 /* --------------------------------------------------------- conversions --- */
 /* out[N, K] fp16 = fp16((q - z) * s); bit-exact to `dequant_int4_kernel`
  * (int4_decode_step.hip:3568-3603) and dequantize_int4_asym

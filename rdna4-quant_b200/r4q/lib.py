@@ -56,6 +56,9 @@ _SIGS = {
     "r4q_rmsnorm": (i32, [vp, vp, vp, vp, vp, i32, i32, i64, f32, vp]),
     "r4q_head_norm_rope": (i32, [vp, vp, vp, vp, vp, vp, vp, i64, i32, vp, vp, vp, vp, vp, vp, vp,
                                  i32, i32, i32, i32, i64, i64, i32, f32, i32, vp]),
+    "r4q_flash_decode_workspace_bytes": (sz_t, [i32, i32, i32, i32]),
+    "r4q_flash_decode": (i32, [vp, i64, vp, vp, vp, vp, vp, i64, i32, i32, i32, i32, i32, i32, vp,
+                               i32, vp, sz_t, vp]),
     "r4q_dequant_int4": (i32, [vp, vp, vp, i32, i32, vp]),
     "r4q_fp16_to_fp8": (i32, [vp, vp, i64, vp]),
     "r4q_fp8_to_fp32": (i32, [vp, vp, i64, vp]),
@@ -84,3 +87,4 @@ def call(name: str, *args) -> None:
 PRO_NONE, PRO_FWHT, PRO_SILU_FWHT, PRO_RMSNORM_FWHT = 0, 1, 2, 3
 W_INT4, W_INT8, W_FP16 = 0, 1, 2
 HEAD_NORM, HEAD_ROPE, HEAD_KV = 1, 2, 4
+ATTN_FWHT = 1

@@ -143,3 +143,33 @@ def head_norm_rope(q, k, *, v=None, q_w=None, k_w=None, cos=None, sin=None, pos=
            ld_in if ld_in is not None else (H + 2 * Hk) * D,
            ld_out if ld_out is not None else (H + 2 * Hk) * D,
            max_seq, float(eps), flags, stream_handle(dev))
+
+
+_aws: dict = {}
+
+
+def attn_workspace(dev: torch.device, B: int, H: int, Hk: int, max_seq: int) -> torch.Tensor:
+    need = int(L.LIB.r4q_flash_decode_workspace_bytes(B, H, Hk, max_seq))
+    key = (dev.index, stream_handle(dev))
+    with _ws_lock:
+        cur = _aws.get(key)
+        if cur is None or cur.numel() < need:
+            cur = torch.zeros(max(need, 1 << 16), dtype=torch.uint8, device=dev)
+            _aws[key] = cur
+    return cur
+
+
+def flash_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, seq_len: int,
+                 *, k_scale=None, v_scale=None, fwht: bool = False, out=None, seq_dev=None):
+    """q fp16 [B, H, 128]; caches uint8 [B, Hk, max_seq, 128] -> o fp16 [B, H, 128]."""
+    dev = _require_cuda(q, k_cache, v_cache)
+    B, H, D = q.shape
+    Hk, max_seq = k_cache.shape[1], k_cache.shape[2]
+    q2 = q.reshape(B, H * D).contiguous()
+    o = out if out is not None else torch.empty(B, H, D, dtype=torch.float16, device=dev)
+    ws = attn_workspace(dev, B, H, Hk, max_seq)
+    L.call("r4q_flash_decode", q2.data_ptr(), H * D, k_cache.data_ptr(), v_cache.data_ptr(),
+           _ptr(k_scale), _ptr(v_scale), o.data_ptr(), H * D, B, H, Hk, D, max_seq, int(seq_len),
+           _ptr(seq_dev), L.ATTN_FWHT if fwht else 0, ws.data_ptr(), ws.numel(),
+           stream_handle(dev))
+    return o
