@@ -161,6 +161,51 @@ int r4q_flash_decode(const void* q, long ldq, const void* k_cache, const void* v
                      int Hk, int D, int max_seq, int seq_len, const long long* seq_dev, int flags,
                      void* workspace, size_t ws_bytes, void* stream);
 
+/* ------------------------------------------------------------- decode step --- */
+/* One transformer layer's weights and caches (device pointers).  *_fmt is
+ * R4Q_W_INT4 (packed [N, K/2] + (scale, zero) pairs [N, K/16]) or R4Q_W_INT8
+ * (int8 [N, K] + fp16 scales [N, K/32]).  qkv rows: q heads, k heads, v heads;
+ * gate_up rows: gate then up (the reference's fused layouts). */
+typedef struct r4q_layer_desc {
+  int qkv_fmt, o_fmt, gate_up_fmt, down_fmt;
+  const void *qkv_w, *qkv_s, *o_w, *o_s, *gate_up_w, *gate_up_s, *down_w, *down_s;
+  const void *in_norm, *post_norm, *q_norm, *k_norm;   /* fp16 [hidden] / [head_dim] */
+  void *k_cache, *v_cache;                              /* uint8 [batch, Hk, max_seq, head_dim] */
+  const float *k_scale, *v_scale;                       /* fp32 [batch, Hk] or NULL */
+} r4q_layer_desc;
+
+typedef struct r4q_model_desc {
+  int num_layers, batch, hidden, intermediate, num_heads, num_kv_heads, head_dim, max_seq;
+  float rms_eps;
+  const void *rope_cos, *rope_sin;   /* fp16 [rows, head_dim/2] */
+  long rope_stride;                  /* elements between table rows */
+  const void* final_norm;            /* fp16 [hidden] */
+  int lm_fmt;                        /* R4Q_W_INT4 / R4Q_W_INT8 / R4Q_W_FP16 */
+  const void *lm_w, *lm_s;           /* lm_s NULL for fp16 */
+  int lm_n;                          /* vocabulary rows */
+} r4q_model_desc;
+
+typedef struct r4q_decode_ctx r4q_decode_ctx;
+
+/* Allocate the scratch of a decode step for this model on the current device
+ * (the layer table is copied; the weights/caches it points to stay owned by the
+ * caller).  Replaces the lazily grown global scratch `g_ds`
+ * (int4_decode_step.hip:2325-2412). */
+int r4q_decode_ctx_create(const r4q_model_desc* model, const r4q_layer_desc* layers,
+                          r4q_decode_ctx** out);
+void r4q_decode_ctx_destroy(r4q_decode_ctx* ctx);
+
+/* Enqueue one decode step for all `batch` rows at position `pos` on `stream`:
+ * hidden_in fp16 [batch, hidden] (device) -> hidden_out (NULL to skip) and
+ * logits_out fp16 [batch, lm_n] (NULL to skip the final norm + lm_head).  K/V of
+ * `pos` are written to every layer's cache.  use_graph = 1 captures the step
+ * once into a CUDA graph (the position is a device scalar) and replays it on
+ * later calls.  Replaces int4_decode_step / int4_decode_step_logits
+ * (int4_decode_step.hip:2343-2595) and the graph replay of :2801-3041.  A
+ * context is not thread-safe and must not run on two streams at once. */
+int r4q_decode_step(r4q_decode_ctx* ctx, const void* hidden_in, int pos, void* hidden_out,
+                    void* logits_out, int use_graph, void* stream);
+
 /* --------------------------------------------------------- conversions --- */
 /* out[N, K] fp16 = fp16((q - z) * s); bit-exact to `dequant_int4_kernel`
  * (int4_decode_step.hip:3568-3603) and dequantize_int4_asym

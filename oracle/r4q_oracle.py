@@ -442,24 +442,35 @@ def lse_merge(pmax: np.ndarray, psum: np.ndarray, pout: np.ndarray) -> np.ndarra
 # --------------------------------------------------------------------------
 # Decode step composition  (int4_decode_step.hip:2343-2595)
 # --------------------------------------------------------------------------
+# INT4 GEMV arithmetic used by decode_layer/decode_step*: 'blockwise' is the
+# reference decode kernel's (gemv_warp, int4_decode_step.hip:131-169: per-block
+# fp32 dot times scale, weights never rounded); 'dequant' is the reference
+# Python/prefill path's (dequantize_int4_asym to fp16, then matmul).
+INT4_MODE = {'mode': 'blockwise'}
+
+
 def linear(x, lin):
     """Dispatch a linear layer by its precision: ('int4', packed, sz) |
     ('int8', w, s) | ('fp16', w)."""
     kind = lin[0]
     if kind == 'int4':
+        if INT4_MODE['mode'] == 'blockwise':
+            return gemv_int4_blockwise(x, lin[1], lin[2])
         return gemv_int4(x, lin[1], lin[2])
     if kind == 'int8':
         return gemv_int8(x, lin[1], lin[2])
     return gemv_fp16(x, lin[1])
 
 
-def decode_layer(h, rot, layer, next_norm, cfg, kc, vc, pos, cos_row, sin_row):
+def decode_layer(h, rot, layer, next_norm, cfg, kc, vc, pos, cos_row, sin_row, write_kv=True):
     """One transformer layer of ``int4_decode_step`` (hip:2474-2524) for a
     batch of rows sharing ``pos``.  h fp16 [B, D] is the residual stream and
     rot the already normalised+rotated layer input.  kc/vc u8
     [B,Hk,max_seq,hd] are updated in place.  The closing residual+norm uses
     ``next_norm`` (the next layer's input norm; layer 0's for the last layer,
-    hip:2519-2523).  Returns (h_new, rot_next)."""
+    hip:2519-2523).  With ``write_kv=False`` the bytes already in the cache at
+    ``pos`` are used instead of this layer's own encoding (to check a device
+    step against the cache it wrote).  Returns (h_new, rot_next)."""
     H, Hk, hd, I, eps = (cfg['num_heads'], cfg['num_kv_heads'], cfg['head_dim'],
                          cfg['intermediate_size'], cfg['rms_eps'])
     B = h.shape[0]
@@ -470,8 +481,9 @@ def decode_layer(h, rot, layer, next_norm, cfg, kc, vc, pos, cos_row, sin_row):
     v = qkv[:, qd + kd:qd + 2 * kd].reshape(B, Hk, hd)
     qo, _, kb, vb = qknorm_rope_kv(q, k, v, layer['q_norm'], layer['k_norm'],
                                    cos_row, sin_row, eps)
-    kc[:, :, pos, :] = kb
-    vc[:, :, pos, :] = vb
+    if write_kv:
+        kc[:, :, pos, :] = kb
+        vc[:, :, pos, :] = vb
     att = attention_decode(qo, kc, vc, pos + 1, fwht_out=True).reshape(B, qd)
     o = linear(att, layer['o'])
     rot, r = res_norm_fwht(o, h, layer['post_norm'], eps)
@@ -482,7 +494,7 @@ def decode_layer(h, rot, layer, next_norm, cfg, kc, vc, pos, cos_row, sin_row):
     return h_new, rot_next
 
 
-def decode_step(h, layers, cfg, kcs, vcs, pos, cos, sin):
+def decode_step(h, layers, cfg, kcs, vcs, pos, cos, sin, write_kv=True):
     """``int4_decode_step`` (hip:2343-2528): returns the final hidden fp16 [B, D]."""
     eps = cfg['rms_eps']
     h = np.atleast_2d(np.asarray(h, dtype=np.float16))
@@ -491,14 +503,14 @@ def decode_step(h, layers, cfg, kcs, vcs, pos, cos, sin):
     for li, layer in enumerate(layers):
         nxt = layers[li + 1]['in_norm'] if li < L - 1 else layers[0]['in_norm']
         h, rot = decode_layer(h, rot, layer, nxt, cfg, kcs[li], vcs[li], pos,
-                              cos[pos], sin[pos])
+                              cos[pos], sin[pos], write_kv)
     return h
 
 
-def decode_step_logits(h, layers, cfg, kcs, vcs, pos, cos, sin, final_norm, lm):
+def decode_step_logits(h, layers, cfg, kcs, vcs, pos, cos, sin, final_norm, lm, write_kv=True):
     """``int4_decode_step_logits`` (hip:2534-2595): all layers, then
     RMSNorm+FWHT of the final hidden with ``final_norm`` and the lm_head GEMV.
     Returns (fp16 logits [B, vocab], final hidden fp16 [B, D])."""
-    h = decode_step(h, layers, cfg, kcs, vcs, pos, cos, sin)
+    h = decode_step(h, layers, cfg, kcs, vcs, pos, cos, sin, write_kv)
     rot = rmsnorm_fwht(h, final_norm, cfg['rms_eps'])
     return linear(rot, lm), h

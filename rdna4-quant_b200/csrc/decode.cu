@@ -1,0 +1,254 @@
+// Decode-step runtime: the whole transformer decode step on one GPU.
+//
+// Replaces int4_decode_step / int4_decode_step_logits and the graph benchmark
+// (int4_decode_step.hip:2325-2595, 2801-3041).  Per layer (B rows share pos):
+//   1. qkv   = GEMV(in_norm, prologue RMSNorm+FWHT of h; rrms from the sums of
+//              squares the previous down-proj wrote, or from h itself on layer 0)
+//   2. q, k  <- per-head RMSNorm + RoPE(pos); K, V -> FP8 cache at pos
+//   3. attn  = flash-decode over positions [0, pos] with the FWHT epilogue
+//   4. r     = GEMV_o(attn) + h      (residual epilogue + sums of squares)
+//   5. gu    = GEMV_gate_up(RMSNorm+FWHT of r with post_norm)
+//   6. h     = GEMV_down(FWHT(silu(g) * u)) + r   (residual epilogue + ss)
+// then logits = GEMV_lm(RMSNorm+FWHT of h with final_norm, rrms from the fp16
+// h as the reference's final fused_rmsnorm_fwht does).
+//
+// The context owns every scratch buffer; one call enqueues the step on the
+// caller's stream.  With use_graph the step is captured once into a CUDA graph
+// (positions come from a device scalar, so one graph serves every token) and
+// replayed.
+#include <cstdio>
+#include <cstring>
+#include <vector>
+
+#include "gemv.cuh"
+#include "r4q_common.cuh"
+
+struct r4q_decode_ctx {
+  r4q_model_desc m;
+  std::vector<r4q_layer_desc> layers;
+  int dev;
+  // scratch
+  __half *h_in, *h, *r, *qkv, *attn, *gu, *logits, *h_out;
+  float *ss_post, *ss_h;
+  long long* pos_dev;   // [B] position of the token being decoded
+  long long* seq_dev;   // [B] pos + 1
+  void* gemv_ws;
+  size_t gemv_ws_bytes;
+  void* attn_ws;
+  size_t attn_ws_bytes;
+  // graph cache
+  cudaStream_t cap_stream;
+  cudaGraphExec_t graph[2];  // [without lm_head, with lm_head]
+};
+
+namespace r4q {
+
+__global__ void set_positions(long long* pos, long long* seq, int B, int p) {
+  const int i = threadIdx.x;
+  if (i < B) {
+    pos[i] = p;
+    seq[i] = p + 1;
+  }
+}
+
+static int gemv_call(r4q_decode_ctx* c, int fmt, const void* w, const void* s, const void* x, void* y,
+                     int N, int K, int prologue, const void* norm_w, const float* ss_in, int ss_parts,
+                     const void* res, float* ss_out, cudaStream_t st) {
+  GemvArgs a{};
+  a.x = x;
+  a.ldx = (prologue == R4Q_PRO_SILU_FWHT) ? 2L * K : K;
+  a.w = w;
+  a.s = s;
+  a.y = y;
+  a.ldy = N;
+  a.B = c->m.batch;
+  a.N = N;
+  a.K = K;
+  a.prologue = prologue;
+  a.ws = c->gemv_ws;
+  a.ws_bytes = c->gemv_ws_bytes;
+  a.stream = st;
+  a.norm_w = norm_w;
+  a.eps = c->m.rms_eps;
+  a.ss_in = ss_in;
+  a.ss_in_parts = ss_parts;
+  a.res = res;
+  a.ldres = N;
+  a.ss_out = ss_out;
+  return launch_gemv(a, fmt);
+}
+
+static int enqueue_step(r4q_decode_ctx* c, bool with_logits, cudaStream_t st) {
+  const r4q_model_desc& m = c->m;
+  const int B = m.batch, D = m.hidden, I = m.intermediate, H = m.num_heads, Hk = m.num_kv_heads,
+            hd = m.head_dim;
+  const int qd = H * hd, kvd = Hk * hd, qkv_n = qd + 2 * kvd;
+  const int L = m.num_layers;
+  int rc = 0;
+  for (int li = 0; li < L && !rc; ++li) {
+    const r4q_layer_desc& ly = c->layers[li];
+    const __half* hin = (li == 0) ? c->h_in : c->h;
+    // 1. qkv projection, RMSNorm + FWHT prologue
+    rc = gemv_call(c, ly.qkv_fmt, ly.qkv_w, ly.qkv_s, hin, c->qkv, qkv_n, D, R4Q_PRO_RMSNORM_FWHT,
+                   ly.in_norm, li == 0 ? nullptr : c->ss_h, D / 16, nullptr, nullptr, st);
+    if (rc) break;
+    // 2. QK norm + RoPE in place, K/V to the FP8 cache
+    rc = r4q_head_norm_rope(c->qkv, c->qkv + qd, c->qkv + qd + kvd, ly.q_norm, ly.k_norm, m.rope_cos,
+                            m.rope_sin, m.rope_stride, 0, c->pos_dev, c->qkv, c->qkv + qd, ly.k_cache,
+                            ly.v_cache, ly.k_scale, ly.v_scale, B, H, Hk, hd, qkv_n, qkv_n,
+                            m.max_seq, m.rms_eps, R4Q_HEAD_NORM | R4Q_HEAD_ROPE | R4Q_HEAD_KV, st);
+    if (rc) break;
+    // 3. attention over [0, pos], FWHT on the output (feeds o_proj)
+    rc = r4q_flash_decode(c->qkv, qkv_n, ly.k_cache, ly.v_cache, ly.k_scale, ly.v_scale, c->attn, qd,
+                          B, H, Hk, hd, m.max_seq, 0, c->seq_dev, R4Q_ATTN_FWHT, c->attn_ws,
+                          c->attn_ws_bytes, st);
+    if (rc) break;
+    // 4. o_proj + residual -> r, sums of squares for the post-attention norm
+    rc = gemv_call(c, ly.o_fmt, ly.o_w, ly.o_s, c->attn, c->r, D, qd, R4Q_PRO_NONE, nullptr, nullptr,
+                   0, hin, c->ss_post, st);
+    if (rc) break;
+    // 5. gate_up with RMSNorm + FWHT of r
+    rc = gemv_call(c, ly.gate_up_fmt, ly.gate_up_w, ly.gate_up_s, c->r, c->gu, 2 * I, D,
+                   R4Q_PRO_RMSNORM_FWHT, ly.post_norm, c->ss_post, D / 16, nullptr, nullptr, st);
+    if (rc) break;
+    // 6. down with SiLU*up + FWHT, + residual r -> h, sums of squares for the next norm
+    rc = gemv_call(c, ly.down_fmt, ly.down_w, ly.down_s, c->gu, c->h, D, I, R4Q_PRO_SILU_FWHT, nullptr,
+                   nullptr, 0, c->r, c->ss_h, st);
+  }
+  if (rc || !with_logits) return rc;
+  return gemv_call(c, m.lm_fmt, m.lm_w, m.lm_s, L > 0 ? c->h : c->h_in, c->logits, m.lm_n, D,
+                   R4Q_PRO_RMSNORM_FWHT, m.final_norm, nullptr, 0, nullptr, nullptr, st);
+}
+
+static void free_ctx(r4q_decode_ctx* c) {
+  for (int i = 0; i < 2; ++i)
+    if (c->graph[i]) cudaGraphExecDestroy(c->graph[i]);
+  if (c->cap_stream) cudaStreamDestroy(c->cap_stream);
+  void* bufs[] = {c->h_in, c->h, c->r, c->qkv, c->attn, c->gu, c->logits, c->h_out, c->ss_post,
+                  c->ss_h, c->pos_dev, c->seq_dev, c->gemv_ws, c->attn_ws};
+  for (void* b : bufs)
+    if (b) cudaFree(b);
+  delete c;
+}
+
+}  // namespace r4q
+
+using namespace r4q;
+
+extern "C" int r4q_decode_ctx_create(const r4q_model_desc* md, const r4q_layer_desc* layers,
+                                     r4q_decode_ctx** out) {
+  if (!md || !out || (md->num_layers > 0 && !layers))
+    return set_error(R4Q_ERR_ARG, "decode_ctx_create: null argument");
+  const r4q_model_desc& m = *md;
+  if (m.batch < 1 || m.batch > 16 || m.hidden % 128 || m.intermediate % 128 || m.head_dim != 128 ||
+      m.num_heads % m.num_kv_heads || m.num_heads / m.num_kv_heads > 8 || m.max_seq < 1 ||
+      (m.num_heads * m.head_dim) % 128)
+    return set_error(R4Q_ERR_ARG, "decode_ctx_create: unsupported model shape");
+  r4q_decode_ctx* c = new r4q_decode_ctx();  // value-initialised: all pointers null
+  c->m = m;
+  c->layers.assign(layers, layers + m.num_layers);
+  cudaGetDevice(&c->dev);
+  const int B = m.batch, D = m.hidden, I = m.intermediate;
+  const int qkv_n = (m.num_heads + 2 * m.num_kv_heads) * m.head_dim;
+  const int qd = m.num_heads * m.head_dim;
+  int nmax = qkv_n;
+  if (2 * I > nmax) nmax = 2 * I;
+  if (m.lm_n > nmax) nmax = m.lm_n;
+  c->gemv_ws_bytes = r4q_gemv_workspace_bytes(B, nmax, D > I ? D : I);
+  c->attn_ws_bytes = r4q_flash_decode_workspace_bytes(B, m.num_heads, m.num_kv_heads, m.max_seq);
+  struct {
+    void** p;
+    size_t n;
+  } al[] = {{(void**)&c->h_in, (size_t)B * D * 2},       {(void**)&c->h, (size_t)B * D * 2},
+            {(void**)&c->r, (size_t)B * D * 2},          {(void**)&c->qkv, (size_t)B * qkv_n * 2},
+            {(void**)&c->attn, (size_t)B * qd * 2},      {(void**)&c->gu, (size_t)B * 2 * I * 2},
+            {(void**)&c->logits, (size_t)B * m.lm_n * 2 + 16}, {(void**)&c->h_out, (size_t)B * D * 2},
+            {(void**)&c->ss_post, (size_t)D / 16 * B * 4}, {(void**)&c->ss_h, (size_t)D / 16 * B * 4},
+            {(void**)&c->pos_dev, (size_t)B * 8},         {(void**)&c->seq_dev, (size_t)B * 8},
+            {&c->gemv_ws, c->gemv_ws_bytes},              {&c->attn_ws, c->attn_ws_bytes}};
+  for (auto& a : al) {
+    cudaError_t e = cudaMalloc(a.p, a.n);
+    if (e == cudaSuccess) e = cudaMemset(*a.p, 0, a.n);
+    if (e != cudaSuccess) {
+      free_ctx(c);
+      return set_error(R4Q_ERR_CUDA, "decode_ctx_create: %s", cudaGetErrorString(e));
+    }
+  }
+  cudaError_t e = cudaStreamCreateWithFlags(&c->cap_stream, cudaStreamNonBlocking);
+  if (e != cudaSuccess) {
+    free_ctx(c);
+    return set_error(R4Q_ERR_CUDA, "decode_ctx_create: stream: %s", cudaGetErrorString(e));
+  }
+  *out = c;
+  return R4Q_OK;
+}
+
+extern "C" void r4q_decode_ctx_destroy(r4q_decode_ctx* c) {
+  if (c) {
+    cudaDeviceSynchronize();
+    free_ctx(c);
+  }
+}
+
+extern "C" int r4q_decode_step(r4q_decode_ctx* c, const void* hidden_in, int pos, void* hidden_out,
+                               void* logits_out, int use_graph, void* stream) {
+  if (!c || !hidden_in) return set_error(R4Q_ERR_ARG, "decode_step: null argument");
+  if (pos < 0 || pos >= c->m.max_seq)
+    return set_error(R4Q_ERR_CAPACITY, "decode_step: pos %d outside the KV cache (max_seq %d)", pos,
+                     c->m.max_seq);
+  cudaStream_t st = (cudaStream_t)stream;
+  const int B = c->m.batch, D = c->m.hidden;
+  const bool with_logits = logits_out != nullptr;
+  cudaError_t e = cudaMemcpyAsync(c->h_in, hidden_in, (size_t)B * D * 2, cudaMemcpyDeviceToDevice, st);
+  if (e != cudaSuccess) return set_error(R4Q_ERR_CUDA, "decode_step: copy in: %s", cudaGetErrorString(e));
+  set_positions<<<1, 32, 0, st>>>(c->pos_dev, c->seq_dev, B, pos);
+  int rc = check_launch("set_positions");
+  if (rc) return rc;
+  if (use_graph) {
+    cudaGraphExec_t& ge = c->graph[with_logits ? 1 : 0];
+    if (!ge) {
+      // one eager run first: it initialises every per-kernel setting (shared
+      // memory limits, tensor-map entry point) outside the capture; running the
+      // step twice is harmless (same inputs, same cache bytes at pos)
+      rc = enqueue_step(c, with_logits, st);
+      if (rc) return rc;
+      // capture on the context's stream, ordered after the caller's stream
+      cudaEvent_t ev;
+      cudaEventCreateWithFlags(&ev, cudaEventDisableTiming);
+      cudaEventRecord(ev, st);
+      cudaStreamWaitEvent(c->cap_stream, ev, 0);
+      cudaEventDestroy(ev);
+      cudaGraph_t g = nullptr;
+      e = cudaStreamBeginCapture(c->cap_stream, cudaStreamCaptureModeThreadLocal);
+      if (e != cudaSuccess) return set_error(R4Q_ERR_CUDA, "decode_step: begin capture: %s", cudaGetErrorString(e));
+      rc = enqueue_step(c, with_logits, c->cap_stream);
+      e = cudaStreamEndCapture(c->cap_stream, &g);
+      if (rc) {
+        if (g) cudaGraphDestroy(g);
+        return rc;
+      }
+      if (e != cudaSuccess) return set_error(R4Q_ERR_CUDA, "decode_step: end capture: %s", cudaGetErrorString(e));
+      e = cudaGraphInstantiate(&ge, g, 0);
+      cudaGraphDestroy(g);
+      if (e != cudaSuccess) {
+        ge = nullptr;
+        return set_error(R4Q_ERR_CUDA, "decode_step: instantiate: %s", cudaGetErrorString(e));
+      }
+    }
+    e = cudaGraphLaunch(ge, st);
+    if (e != cudaSuccess) return set_error(R4Q_ERR_CUDA, "decode_step: graph launch: %s", cudaGetErrorString(e));
+  } else {
+    rc = enqueue_step(c, with_logits, st);
+    if (rc) return rc;
+  }
+  const __half* hfinal = c->m.num_layers > 0 ? c->h : c->h_in;
+  if (hidden_out) {
+    e = cudaMemcpyAsync(hidden_out, hfinal, (size_t)B * D * 2, cudaMemcpyDeviceToDevice, st);
+    if (e != cudaSuccess) return set_error(R4Q_ERR_CUDA, "decode_step: copy out: %s", cudaGetErrorString(e));
+  }
+  if (logits_out) {
+    e = cudaMemcpyAsync(logits_out, c->logits, (size_t)B * c->m.lm_n * 2, cudaMemcpyDeviceToDevice, st);
+    if (e != cudaSuccess) return set_error(R4Q_ERR_CUDA, "decode_step: copy logits: %s", cudaGetErrorString(e));
+  }
+  return R4Q_OK;
+}

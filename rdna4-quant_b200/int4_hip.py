@@ -10,8 +10,13 @@ from __future__ import annotations
 
 import torch
 
+from r4q import decode as _dec
 from r4q import lib as _lib
 from r4q import ops as _ops
+
+# CUDA-graph replay of the decode step (one capture per context; the position is
+# a device scalar).  Set to False to enqueue the kernels eagerly.
+USE_GRAPH = True
 
 
 def dbg_gemv(X: torch.Tensor, W: torch.Tensor, S: torch.Tensor, N: int, K: int) -> torch.Tensor:
@@ -72,3 +77,42 @@ def dbg_rope(Q, K, COS, SIN, H, Hk, D):
                         q_out=qo, k_out=ko, H=H, Hk=Hk, D=D, ld_in=0, ld_out=0,
                         flags=_lib.HEAD_ROPE)
     return [qo, ko]
+
+
+def decode_step(hidden_in, qkv_w, qkv_s, qkv_N, o_w, o_s, o_N, gu_w, gu_s, gu_N, down_w, down_s,
+                down_N, in_norm_w, post_norm_w, q_norm_w, k_norm_w, rope_cos, rope_sin, pos,
+                num_heads, num_kv_heads, head_dim, hidden_size, intermediate_size, rms_eps,
+                k_caches, v_caches, hadamard_mat=None):
+    """All layers of one decode token; returns the final hidden state
+    [B, 1, hidden] (int4_decode_step.hip:2343-2528).  Weights per layer are
+    INT4 (uint8 packed + (scale, zero) pairs) or INT8 (int8 + fp16 scales);
+    ``hadamard_mat`` is accepted and unused, as in the reference."""
+    B = hidden_in.numel() // int(hidden_size)
+    ctx = _dec.get_context(qkv_w, qkv_s, o_w, o_s, gu_w, gu_s, down_w, down_s, in_norm_w,
+                           post_norm_w, q_norm_w, k_norm_w, rope_cos, rope_sin, num_heads,
+                           num_kv_heads, head_dim, hidden_size, intermediate_size, rms_eps,
+                           k_caches, v_caches, batch=B)
+    h = hidden_in.reshape(B, int(hidden_size)).contiguous()
+    out = torch.empty(B, 1, int(hidden_size), dtype=torch.float16, device=h.device)
+    ctx.step(h, pos, hidden_out=out, use_graph=USE_GRAPH)
+    return out
+
+
+def decode_step_logits(hidden_in, qkv_w, qkv_s, qkv_N, o_w, o_s, o_N, gu_w, gu_s, gu_N, down_w,
+                       down_s, down_N, in_norm_w, post_norm_w, q_norm_w, k_norm_w, rope_cos,
+                       rope_sin, pos, num_heads, num_kv_heads, head_dim, hidden_size,
+                       intermediate_size, rms_eps, k_caches, v_caches, final_norm_w, lm_w, lm_s,
+                       lm_N, lm_K, hadamard_mat=None):
+    """One decode token through every layer, the final RMSNorm+FWHT and the
+    lm_head; returns logits [B, 1, lm_N] fp16 (int4_decode_step.hip:2534-2595).
+    lm_head may be INT4 (the reference's converted symmetric INT4), INT8 or
+    fp16 (lm_s None)."""
+    B = hidden_in.numel() // int(hidden_size)
+    ctx = _dec.get_context(qkv_w, qkv_s, o_w, o_s, gu_w, gu_s, down_w, down_s, in_norm_w,
+                           post_norm_w, q_norm_w, k_norm_w, rope_cos, rope_sin, num_heads,
+                           num_kv_heads, head_dim, hidden_size, intermediate_size, rms_eps,
+                           k_caches, v_caches, final_norm_w, lm_w, lm_s, lm_N, batch=B)
+    h = hidden_in.reshape(B, int(hidden_size)).contiguous()
+    logits = torch.empty(B, 1, int(lm_N), dtype=torch.float16, device=h.device)
+    ctx.step(h, pos, logits_out=logits, use_graph=USE_GRAPH)
+    return logits

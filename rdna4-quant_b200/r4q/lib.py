@@ -43,6 +43,24 @@ class GemvFused(C.Structure):
 
 vp, i32, i64, sz_t, f32 = C.c_void_p, C.c_int, C.c_long, C.c_size_t, C.c_float
 
+
+class LayerDesc(C.Structure):
+    """r4q_layer_desc (include/r4q.h)."""
+    _fields_ = [("qkv_fmt", C.c_int), ("o_fmt", C.c_int), ("gate_up_fmt", C.c_int),
+                ("down_fmt", C.c_int)] + [(n, C.c_void_p) for n in (
+                    "qkv_w", "qkv_s", "o_w", "o_s", "gate_up_w", "gate_up_s", "down_w", "down_s",
+                    "in_norm", "post_norm", "q_norm", "k_norm", "k_cache", "v_cache", "k_scale",
+                    "v_scale")]
+
+
+class ModelDesc(C.Structure):
+    """r4q_model_desc (include/r4q.h)."""
+    _fields_ = [(n, C.c_int) for n in ("num_layers", "batch", "hidden", "intermediate", "num_heads",
+                                        "num_kv_heads", "head_dim", "max_seq")] + [
+        ("rms_eps", C.c_float), ("rope_cos", C.c_void_p), ("rope_sin", C.c_void_p),
+        ("rope_stride", C.c_long), ("final_norm", C.c_void_p), ("lm_fmt", C.c_int),
+        ("lm_w", C.c_void_p), ("lm_s", C.c_void_p), ("lm_n", C.c_int)]
+
 _SIGS = {
     "r4q_last_error": (C.c_char_p, []),
     "r4q_version": (i32, []),
@@ -59,6 +77,9 @@ _SIGS = {
     "r4q_flash_decode_workspace_bytes": (sz_t, [i32, i32, i32, i32]),
     "r4q_flash_decode": (i32, [vp, i64, vp, vp, vp, vp, vp, i64, i32, i32, i32, i32, i32, i32, vp,
                                i32, vp, sz_t, vp]),
+    "r4q_decode_ctx_create": (i32, [C.POINTER(ModelDesc), C.POINTER(LayerDesc), C.POINTER(C.c_void_p)]),
+    "r4q_decode_ctx_destroy": (None, [vp]),
+    "r4q_decode_step": (i32, [vp, vp, i32, vp, vp, i32, vp]),
     "r4q_dequant_int4": (i32, [vp, vp, vp, i32, i32, vp]),
     "r4q_fp16_to_fp8": (i32, [vp, vp, i64, vp]),
     "r4q_fp8_to_fp32": (i32, [vp, vp, i64, vp]),
