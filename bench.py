@@ -51,6 +51,11 @@ def parse():
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--layers", type=int, default=40)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--decode-ctx", default="128,2048",
+                    help="prompt lengths for the Qwen3-14B decode tok/s measurement ('' skips it)")
+    ap.add_argument("--decode-tokens", type=int, default=256)
+    ap.add_argument("--decode-probe", action="store_true",
+                    help="build the 40-layer model, decode 3 tokens eagerly and exit (for ncu)")
     ap.add_argument("--kernel-probe", default=None, choices=[n for n, *_ in LAYER_SHAPES],
                     help="run one GEMV of this shape 4 times and exit (for ncu captures)")
     return ap.parse_args()
@@ -320,6 +325,10 @@ def main_ours(a):
         "gpu_launches": nlaunch * a.steps,
         "clocks": clk.summary(),
     }
+    if a.decode_ctx:
+        del layers
+        torch.cuda.empty_cache()
+        line["decode"] = decode_tok_s(a, dev, peak)
     if rank == 0 and ws == 1 and not a.no_cpu_baseline:
         threads = os.cpu_count() or 1
         nb, dt = cpu_port_run(cpu_port_setup(B), threads)
@@ -362,6 +371,58 @@ def main_reference(a):
     print(json.dumps(line), flush=True)
 
 
+def decode_tok_s(a, dev, peak):
+    """BASELINE config 3 at TP=1: 40-layer Qwen3-14B-shaped decode (random-init,
+    80 % INT4 / 20 % INT8 groups by seed, fp16 embedding + lm_head), KV cache
+    pre-filled for `ctx` prompt positions, greedy decode of `tokens` tokens,
+    each through int4_hip.decode_step_logits (CUDA-graph replay) + argmax +
+    embedding lookup on the device."""
+    import torch
+    import int4_hip
+    from r4q import synth
+    cfg = synth.qwen3_14b_config()
+    ctxs = [int(c) for c in a.decode_ctx.split(",") if c]
+    max_seq = max(ctxs) + a.decode_tokens + 16
+    m = synth.build_decode_model(cfg, dev, seed=3, max_seq=max_seq)
+    res = []
+    for ctx in ctxs:
+        synth.fill_kv_synthetic(m, ctx, seed=ctx)
+        gen = torch.Generator(device=dev).manual_seed(ctx)
+        tok = torch.randint(0, cfg['vocab'], (1,), generator=gen, device=dev)
+
+        def step(pos, tok):
+            h = m['embed'][tok].reshape(1, 1, -1)
+            lg = int4_hip.decode_step_logits(
+                h, m['qkv_w'], m['qkv_s'], 0, m['o_w'], m['o_s'], 0, m['gu_w'], m['gu_s'], 0,
+                m['down_w'], m['down_s'], 0, m['in_norm_w'], m['post_norm_w'], m['q_norm_w'],
+                m['k_norm_w'], m['rope_cos'], m['rope_sin'], pos, cfg['num_heads'],
+                cfg['num_kv_heads'], cfg['head_dim'], cfg['hidden'], cfg['intermediate'],
+                cfg['rms_eps'], m['k_caches'], m['v_caches'], m['final_norm_w'], m['lm_w'],
+                m['lm_s'], cfg['vocab'], cfg['hidden'], None)
+            return lg.reshape(-1).argmax().reshape(1)
+        for w in range(3):                         # warm-up (graph capture on the first)
+            tok = step(ctx + w, tok)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for t in range(a.decode_tokens):
+            tok = step(ctx + t, tok)
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / a.decode_tokens
+        kv = cfg['num_layers'] * 2 * cfg['num_kv_heads'] * cfg['head_dim'] * (ctx + a.decode_tokens // 2)
+        byt = m['weight_bytes'] + kv + 2 * cfg['hidden']
+        res.append({"ctx": ctx, "tok_s": round(1e3 / ms, 1), "ms_per_token": round(ms, 4),
+                    "bytes_per_token": byt, "GBps": round(byt / ms / 1e6, 1),
+                    "roofline_tok_s": round(peak * 1e9 / byt, 1),
+                    "frac": round((byt / ms / 1e6) / peak, 4)})
+    return {"model": "Qwen3-14B shape, random init", "int8_groups": m['int8_groups'],
+            "lm_head": "fp16", "batch": 1, "tokens": a.decode_tokens,
+            "kv": "prompt K/V pre-filled with seeded FP8 values (no prefill compute)",
+            "api": "int4_hip.decode_step_logits per token (graph replay) + argmax + embedding",
+            "results": res}
+
+
 def kernel_probe(a):
     import torch
     from r4q import lib as Lb, ops, synth
@@ -378,9 +439,35 @@ def kernel_probe(a):
     print(f"probe {name} N={N} K={K} B={a.batch} ok")
 
 
+def decode_probe(a):
+    import torch
+    import int4_hip
+    from r4q import synth
+    dev = torch.device("cuda", 0)
+    int4_hip.USE_GRAPH = False
+    cfg = synth.qwen3_14b_config()
+    m = synth.build_decode_model(cfg, dev, seed=3, max_seq=2304)
+    synth.fill_kv_synthetic(m, 2048, seed=1)
+    tok = torch.zeros(1, dtype=torch.long, device=dev)
+    for t in range(3):
+        h = m['embed'][tok].reshape(1, 1, -1)
+        lg = int4_hip.decode_step_logits(
+            h, m['qkv_w'], m['qkv_s'], 0, m['o_w'], m['o_s'], 0, m['gu_w'], m['gu_s'], 0,
+            m['down_w'], m['down_s'], 0, m['in_norm_w'], m['post_norm_w'], m['q_norm_w'],
+            m['k_norm_w'], m['rope_cos'], m['rope_sin'], 2048 + t, cfg['num_heads'],
+            cfg['num_kv_heads'], cfg['head_dim'], cfg['hidden'], cfg['intermediate'],
+            cfg['rms_eps'], m['k_caches'], m['v_caches'], m['final_norm_w'], m['lm_w'], m['lm_s'],
+            cfg['vocab'], cfg['hidden'], None)
+        tok = lg.reshape(-1).argmax().reshape(1)
+    torch.cuda.synchronize()
+    print("decode probe ok")
+
+
 if __name__ == "__main__":
     args = parse()
-    if args.kernel_probe:
+    if args.decode_probe:
+        decode_probe(args)
+    elif args.kernel_probe:
         kernel_probe(args)
     elif args.impl == "reference":
         main_reference(args)

@@ -84,3 +84,70 @@ def gemv_bytes(fmt: str, B: int, N: int, K: int) -> int:
     if fmt == 'int8':
         return N * K + 2 * N * K // 32 + act
     return 2 * N * K + act
+
+
+def qwen3_14b_config(layers: int = 40) -> dict:
+    return dict(num_layers=layers, hidden=5120, intermediate=17408, num_heads=40, num_kv_heads=8,
+                head_dim=128, vocab=151936, rms_eps=1e-6, rope_theta=1e6)
+
+
+def build_decode_model(cfg: dict, device, seed: int = 0, int8_frac: float = 0.2,
+                       max_seq: int = 2304, batch: int = 1, lm_fp16: bool = True):
+    """Random-init weights of a Qwen3-architecture decoder in the reference's
+    runtime layout: per layer the fused qkv / o / gate_up /
+    down projections, ``int8_frac`` of the (layer, projection) groups INT8 and
+    the rest INT4 (chosen by ``seed``), fp16 embedding and lm_head, FP8 KV caches
+    [batch, Hk, max_seq, head_dim].  Returns the keyword arguments of
+    int4_hip.decode_step_logits (minus hidden_in/pos) plus 'embed'."""
+    g = torch.Generator(device=device).manual_seed(seed)
+    L, D, I = cfg['num_layers'], cfg['hidden'], cfg['intermediate']
+    H, Hk, hd = cfg['num_heads'], cfg['num_kv_heads'], cfg['head_dim']
+    groups = [(li, p) for li in range(L) for p in ('qkv', 'o', 'gate_up', 'down')]
+    pick = torch.randperm(len(groups), generator=torch.Generator().manual_seed(seed))
+    int8 = {groups[i] for i in pick[:int(round(int8_frac * len(groups)))].tolist()}
+    shapes = {'qkv': ((H + 2 * Hk) * hd, D), 'o': (D, H * hd), 'gate_up': (2 * I, D), 'down': (D, I)}
+    out = {k: [] for k in ('qkv_w', 'qkv_s', 'o_w', 'o_s', 'gu_w', 'gu_s', 'down_w', 'down_s',
+                           'in_norm_w', 'post_norm_w', 'q_norm_w', 'k_norm_w', 'k_caches', 'v_caches')}
+    names = {'qkv': 'qkv', 'o': 'o', 'gate_up': 'gu', 'down': 'down'}
+    wbytes = 0
+    for li in range(L):
+        for p, (N, K) in shapes.items():
+            if (li, p) in int8:
+                _, w, s = linear_int8(N, K, g, device)
+                wbytes += gemv_bytes('int8', 0, N, K)
+            else:
+                _, w, s = linear_int4(N, K, g, device)
+                wbytes += gemv_bytes('int4', 0, N, K)
+            out[names[p] + '_w'].append(w)
+            out[names[p] + '_s'].append(s)
+        for k, n in (('in_norm_w', D), ('post_norm_w', D), ('q_norm_w', hd), ('k_norm_w', hd)):
+            out[k].append((1 + 0.01 * torch.randn(n, generator=g, device=device)).half())
+        out['k_caches'].append(torch.zeros(batch, Hk, max_seq, hd, dtype=torch.uint8, device=device))
+        out['v_caches'].append(torch.zeros(batch, Hk, max_seq, hd, dtype=torch.uint8, device=device))
+    V = cfg['vocab']
+    out['embed'] = (torch.randn(V, D, generator=g, device=device) * 0.02).half()
+    out['final_norm_w'] = (1 + 0.01 * torch.randn(D, generator=g, device=device)).half()
+    if lm_fp16:
+        out['lm_w'] = (torch.randn(V, D, generator=g, device=device) * 0.02).half()
+        out['lm_s'] = None
+        wbytes += 2 * V * D
+    else:
+        _, out['lm_w'], out['lm_s'] = linear_int4(V, D, g, device)
+        wbytes += gemv_bytes('int4', 0, V, D)
+    inv = 1.0 / (cfg['rope_theta'] ** (torch.arange(0, hd, 2, device=device).float() / hd))
+    f = torch.outer(torch.arange(max_seq + 128, device=device).float(), inv)
+    out['rope_cos'], out['rope_sin'] = f.cos().half(), f.sin().half()
+    out['weight_bytes'] = wbytes
+    out['int8_groups'] = len(int8)
+    return out
+
+
+def fill_kv_synthetic(model: dict, ctx: int, seed: int = 0):
+    """Stand-in for the prompt's prefill: FP8 K/V of ctx positions from seeded
+    N(0,1) values through the reference encoder (fp16_to_fp8)."""
+    from . import ops
+    g = torch.Generator(device=model['k_caches'][0].device).manual_seed(seed)
+    for kc, vc in zip(model['k_caches'], model['v_caches']):
+        for c in (kc, vc):
+            x = torch.randn(c.shape[0], c.shape[1], ctx, c.shape[3], generator=g, device=c.device).half()
+            c[:, :, :ctx] = ops.fp16_to_fp8(x)
