@@ -328,7 +328,7 @@ def main_ours(a):
     if a.decode_ctx:
         del layers
         torch.cuda.empty_cache()
-        line["decode"] = decode_tok_s(a, dev, peak)
+        line["decode"] = decode_tok_s(a, dev, peak, ws, rank)
     if rank == 0 and ws == 1 and not a.no_cpu_baseline:
         threads = os.cpu_count() or 1
         nb, dt = cpu_port_run(cpu_port_setup(B), threads)
@@ -371,19 +371,32 @@ def main_reference(a):
     print(json.dumps(line), flush=True)
 
 
-def decode_tok_s(a, dev, peak):
-    """BASELINE config 3 at TP=1: 40-layer Qwen3-14B-shaped decode (random-init,
+def decode_tok_s(a, dev, peak, ws=1, rank=0):
+    """40-layer Qwen3-14B-shaped decode (random-init,
     80 % INT4 / 20 % INT8 groups by seed, fp16 embedding + lm_head), KV cache
     pre-filled for `ctx` prompt positions, greedy decode of `tokens` tokens,
-    each through int4_hip.decode_step_logits (CUDA-graph replay) + argmax +
-    embedding lookup on the device."""
+    each one decode step with logits (CUDA-graph replay) + argmax + embedding
+    lookup on the device.  TP=1: through int4_hip.decode_step_logits.  TP=ws>1
+    (torchrun, one rank per GPU): each rank holds its shard (r4q.tp) and the
+    step's exchanges run over NVLink peer memory (r4q_comm); time is the max
+    over ranks."""
     import torch
+    import torch.distributed as dist
     import int4_hip
-    from r4q import synth
+    from r4q import synth, tp
     cfg = synth.qwen3_14b_config()
     ctxs = [int(c) for c in a.decode_ctx.split(",") if c]
     max_seq = max(ctxs) + a.decode_tokens + 16
     m = synth.build_decode_model(cfg, dev, seed=3, max_seq=max_seq)
+    wbytes, int8_groups = m['weight_bytes'], m['int8_groups']
+    dec = None
+    if ws > 1:
+        sh = tp.shard_decode_model(m, cfg, rank, ws)
+        del m
+        torch.cuda.empty_cache()
+        m = sh
+        comm = tp.Comm(rank, ws, max_batch=1, hidden=cfg['hidden'], vocab=cfg['vocab'])
+        dec = tp.TPDecoder(m, cfg, comm, batch=1)
     res = []
     for ctx in ctxs:
         synth.fill_kv_synthetic(m, ctx, seed=ctx)
@@ -392,17 +405,22 @@ def decode_tok_s(a, dev, peak):
 
         def step(pos, tok):
             h = m['embed'][tok].reshape(1, 1, -1)
-            lg = int4_hip.decode_step_logits(
-                h, m['qkv_w'], m['qkv_s'], 0, m['o_w'], m['o_s'], 0, m['gu_w'], m['gu_s'], 0,
-                m['down_w'], m['down_s'], 0, m['in_norm_w'], m['post_norm_w'], m['q_norm_w'],
-                m['k_norm_w'], m['rope_cos'], m['rope_sin'], pos, cfg['num_heads'],
-                cfg['num_kv_heads'], cfg['head_dim'], cfg['hidden'], cfg['intermediate'],
-                cfg['rms_eps'], m['k_caches'], m['v_caches'], m['final_norm_w'], m['lm_w'],
-                m['lm_s'], cfg['vocab'], cfg['hidden'], None)
+            if dec is not None:
+                lg = dec.step(h, pos)
+            else:
+                lg = int4_hip.decode_step_logits(
+                    h, m['qkv_w'], m['qkv_s'], 0, m['o_w'], m['o_s'], 0, m['gu_w'], m['gu_s'], 0,
+                    m['down_w'], m['down_s'], 0, m['in_norm_w'], m['post_norm_w'], m['q_norm_w'],
+                    m['k_norm_w'], m['rope_cos'], m['rope_sin'], pos, cfg['num_heads'],
+                    cfg['num_kv_heads'], cfg['head_dim'], cfg['hidden'], cfg['intermediate'],
+                    cfg['rms_eps'], m['k_caches'], m['v_caches'], m['final_norm_w'], m['lm_w'],
+                    m['lm_s'], cfg['vocab'], cfg['hidden'], None)
             return lg.reshape(-1).argmax().reshape(1)
         for w in range(3):                         # warm-up (graph capture on the first)
             tok = step(ctx + w, tok)
         torch.cuda.synchronize()
+        if ws > 1:
+            dist.barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
         for t in range(a.decode_tokens):
@@ -410,16 +428,29 @@ def decode_tok_s(a, dev, peak):
         e1.record()
         torch.cuda.synchronize()
         ms = e0.elapsed_time(e1) / a.decode_tokens
+        if ws > 1:
+            comm.status()
+            tt = torch.tensor([ms], device=dev)
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            ms = float(tt.item())
         kv = cfg['num_layers'] * 2 * cfg['num_kv_heads'] * cfg['head_dim'] * (ctx + a.decode_tokens // 2)
-        byt = m['weight_bytes'] + kv + 2 * cfg['hidden']
+        byt = (wbytes + kv) // ws + 2 * cfg['hidden']          # per GPU
         res.append({"ctx": ctx, "tok_s": round(1e3 / ms, 1), "ms_per_token": round(ms, 4),
-                    "bytes_per_token": byt, "GBps": round(byt / ms / 1e6, 1),
+                    "bytes_per_token_per_gpu": byt, "GBps_per_gpu": round(byt / ms / 1e6, 1),
                     "roofline_tok_s": round(peak * 1e9 / byt, 1),
                     "frac": round((byt / ms / 1e6) / peak, 4)})
-    return {"model": "Qwen3-14B shape, random init", "int8_groups": m['int8_groups'],
-            "lm_head": "fp16", "batch": 1, "tokens": a.decode_tokens,
+    if dec is not None:
+        dec = None
+        from r4q import decode
+        decode.clear_contexts()
+        dist.barrier()
+        comm.close()
+    return {"model": "Qwen3-14B shape, random init", "int8_groups": int8_groups,
+            "lm_head": "fp16", "batch": 1, "tokens": a.decode_tokens, "tp": ws,
             "kv": "prompt K/V pre-filled with seeded FP8 values (no prefill compute)",
-            "api": "int4_hip.decode_step_logits per token (graph replay) + argmax + embedding",
+            "api": ("int4_hip.decode_step_logits per token (graph replay) + argmax + embedding"
+                    if ws == 1 else "r4q.tp.TPDecoder.step per token (graph replay, NVLink P2P "
+                    "exchanges fused into the GEMV epilogues) + argmax + embedding"),
             "results": res}
 
 

@@ -62,6 +62,8 @@ typedef struct r4q_gemv_fused {
   const void* residual;   /* fp16 [B, ldres] or NULL; may alias y */
   long ldres;
   float* ss_out;          /* fp32 [N/16][B] or NULL */
+  float* y32;             /* non-NULL: write the unrounded fp32 sums here,
+                             [B, ldy] (y, residual and ss_out are then unused) */
 } r4q_gemv_fused;
 
 /* Message of the last failing call on this host thread ("" if none). */
@@ -166,6 +168,8 @@ int r4q_flash_decode(const void* q, long ldq, const void* k_cache, const void* v
  * R4Q_W_INT4 (packed [N, K/2] + (scale, zero) pairs [N, K/16]) or R4Q_W_INT8
  * (int8 [N, K] + fp16 scales [N, K/32]).  qkv rows: q heads, k heads, v heads;
  * gate_up rows: gate then up (the reference's fused layouts). */
+typedef struct r4q_comm r4q_comm;
+
 typedef struct r4q_layer_desc {
   int qkv_fmt, o_fmt, gate_up_fmt, down_fmt;
   const void *qkv_w, *qkv_s, *o_w, *o_s, *gate_up_w, *gate_up_s, *down_w, *down_s;
@@ -182,7 +186,16 @@ typedef struct r4q_model_desc {
   const void* final_norm;            /* fp16 [hidden] */
   int lm_fmt;                        /* R4Q_W_INT4 / R4Q_W_INT8 / R4Q_W_FP16 */
   const void *lm_w, *lm_s;           /* lm_s NULL for fp16 */
-  int lm_n;                          /* vocabulary rows */
+  int lm_n;                          /* vocabulary rows (of this rank's shard) */
+  /* Tensor parallelism (tp_size 1: single GPU, comm unused).  With tp_size > 1
+   * the layer tensors are this rank's shards: qkv rows of its num_heads /
+   * num_kv_heads (local counts), o_proj columns of those heads, gate_up rows of
+   * its intermediate slice (gate slice then up slice), down columns of that
+   * slice, KV caches of its kv heads, lm_head rows of its lm_n-row vocabulary
+   * slice; hidden, norms and rope tables are whole.  logits are gathered to
+   * [batch, lm_n * tp_size] on every rank; hidden states are replicated. */
+  int tp_rank, tp_size;
+  r4q_comm* comm;
 } r4q_model_desc;
 
 typedef struct r4q_decode_ctx r4q_decode_ctx;
@@ -205,6 +218,32 @@ void r4q_decode_ctx_destroy(r4q_decode_ctx* ctx);
  * context is not thread-safe and must not run on two streams at once. */
 int r4q_decode_step(r4q_decode_ctx* ctx, const void* hidden_in, int pos, void* hidden_out,
                     void* logits_out, int use_graph, void* stream);
+
+/* ------------------------------------------- tensor-parallel exchange --- */
+/* One comm per rank, one process per GPU.  It replaces the torch.distributed
+ * all_reduce the reference's TP path runs between per-layer GEMVs: each rank
+ * owns a peer-visible buffer, producers push fp32 partials straight into the
+ * peers' buffers over NVLink and a sync kernel (signal, bounded wait, reduce in
+ * rank order) finishes the exchange.  Set-up: r4q_comm_create on every rank,
+ * exchange the R4Q_COMM_HANDLE_BYTES handles out of band (all ranks' handles,
+ * rank order), then r4q_comm_open.  Every rank must issue the same sequence of
+ * exchanges.  A wait that times out (~2 s) records R4Q_ERR_TIMEOUT, readable
+ * with r4q_comm_status, and the kernel returns instead of hanging. */
+#define R4Q_COMM_HANDLE_BYTES 64
+/* max_batch x hidden: the decode all-reduce size; vocab: the full gathered
+ * vocabulary (0 if no lm_head gather); sa_cap: elements of the standalone
+ * all-reduce.  Writes this rank's handle to handle_out (host, 64 bytes). */
+int r4q_comm_create(int rank, int world, int max_batch, int hidden, int vocab, long sa_cap,
+                    r4q_comm** out, void* handle_out);
+/* handles: host array [world][R4Q_COMM_HANDLE_BYTES] in rank order. */
+int r4q_comm_open(r4q_comm* comm, const void* handles);
+/* Synchronous: R4Q_OK, or R4Q_ERR_TIMEOUT naming the ranks a wait gave up on. */
+int r4q_comm_status(r4q_comm* comm);
+int r4q_comm_clear_status(r4q_comm* comm);
+/* y[n] = sum over ranks of x[n] (fp32, summed in rank order: identical on
+ * every rank); x and y are device arrays of this rank, n <= sa_cap. */
+int r4q_comm_allreduce_f32(r4q_comm* comm, const float* x, float* y, long n, void* stream);
+void r4q_comm_destroy(r4q_comm* comm);
 
 /* --------------------------------------------------------- conversions --- */
 /* out[N, K] fp16 = fp16((q - z) * s); bit-exact to `dequant_int4_kernel`

@@ -242,17 +242,18 @@ def fp8_encodable_bytes() -> np.ndarray:
 # --------------------------------------------------------------------------
 # GEMV  (int4_decode_step.hip:116-170; int4_quant_v2.py:105-127)
 # --------------------------------------------------------------------------
-def gemv_int4(x: np.ndarray, packed: np.ndarray, sz: np.ndarray) -> np.ndarray:
+def gemv_int4(x: np.ndarray, packed: np.ndarray, sz: np.ndarray, acc: bool = False) -> np.ndarray:
     """Y[b, n] = fp16(sum_k fp16(W_deq)[n, k] * x[b, k]) with W_deq from the
     reference dequant (int4_quant_v2.py:105-127) — the reference test's
     ``x @ dequantize_int4_asym(...).T`` (tests/test_kernels.py:157-158) —
     accumulated in float64.  x fp16 [B, K] -> fp16 [B, N]."""
     W = dequant_int4_runtime(packed, sz).astype(np.float64)
     xb = np.atleast_2d(np.asarray(x, dtype=np.float16)).astype(np.float64)
-    return (xb @ W.T).astype(np.float16)
+    y = xb @ W.T
+    return y if acc else y.astype(np.float16)
 
 
-def gemv_int4_blockwise(x: np.ndarray, packed: np.ndarray, sz: np.ndarray) -> np.ndarray:
+def gemv_int4_blockwise(x: np.ndarray, packed: np.ndarray, sz: np.ndarray, acc: bool = False) -> np.ndarray:
     """Kernel semantics of ``gemv_warp`` (int4_decode_step.hip:131-169):
     y = sum_b s_b * sum_{i in b} x_i (q_i - z_b), float64, no fp16 weight rounding."""
     q = unpack_int4(packed).astype(np.float64)
@@ -262,21 +263,24 @@ def gemv_int4_blockwise(x: np.ndarray, packed: np.ndarray, sz: np.ndarray) -> np
     qb = q.reshape(N, K // BLOCK, BLOCK) - pairs[..., 1:2]
     xr = xb.reshape(xb.shape[0], K // BLOCK, BLOCK)
     part = np.einsum('nkj,bkj->bnk', qb, xr)
-    return np.einsum('bnk,nk->bn', part, pairs[..., 0]).astype(np.float16)
+    y = np.einsum('bnk,nk->bn', part, pairs[..., 0])
+    return y if acc else y.astype(np.float16)
 
 
-def gemv_int8(x: np.ndarray, w: np.ndarray, scale: np.ndarray) -> np.ndarray:
+def gemv_int8(x: np.ndarray, w: np.ndarray, scale: np.ndarray, acc: bool = False) -> np.ndarray:
     """INT8 GEMV oracle: x @ dequantize_int8(w, s).T (int8_quant.py:52-69), float64."""
     W = dequant_int8(w, scale).astype(np.float64)
     xb = np.atleast_2d(np.asarray(x, dtype=np.float16)).astype(np.float64)
-    return (xb @ W.T).astype(np.float16)
+    y = xb @ W.T
+    return y if acc else y.astype(np.float16)
 
 
-def gemv_fp16(x: np.ndarray, w: np.ndarray) -> np.ndarray:
+def gemv_fp16(x: np.ndarray, w: np.ndarray, acc: bool = False) -> np.ndarray:
     """fp16-weight GEMV (fp16 lm_head), float64 accumulate."""
     W = np.asarray(w, dtype=np.float16).astype(np.float64)
     xb = np.atleast_2d(np.asarray(x, dtype=np.float16)).astype(np.float64)
-    return (xb @ W.T).astype(np.float16)
+    y = xb @ W.T
+    return y if acc else y.astype(np.float16)
 
 
 # --------------------------------------------------------------------------
@@ -449,20 +453,22 @@ def lse_merge(pmax: np.ndarray, psum: np.ndarray, pout: np.ndarray) -> np.ndarra
 INT4_MODE = {'mode': 'blockwise'}
 
 
-def linear(x, lin):
+def linear(x, lin, acc=False):
     """Dispatch a linear layer by its precision: ('int4', packed, sz) |
-    ('int8', w, s) | ('fp16', w)."""
+    ('int8', w, s) | ('fp16', w).  ``acc=True`` returns the unrounded float64
+    sums (a tensor-parallel partial) instead of fp16."""
     kind = lin[0]
     if kind == 'int4':
         if INT4_MODE['mode'] == 'blockwise':
-            return gemv_int4_blockwise(x, lin[1], lin[2])
-        return gemv_int4(x, lin[1], lin[2])
+            return gemv_int4_blockwise(x, lin[1], lin[2], acc)
+        return gemv_int4(x, lin[1], lin[2], acc)
     if kind == 'int8':
-        return gemv_int8(x, lin[1], lin[2])
-    return gemv_fp16(x, lin[1])
+        return gemv_int8(x, lin[1], lin[2], acc)
+    return gemv_fp16(x, lin[1], acc)
 
 
-def decode_layer(h, rot, layer, next_norm, cfg, kc, vc, pos, cos_row, sin_row, write_kv=True):
+def decode_layer(h, rot, layer, next_norm, cfg, kc, vc, pos, cos_row, sin_row, write_kv=True,
+                 allreduce=None):
     """One transformer layer of ``int4_decode_step`` (hip:2474-2524) for a
     batch of rows sharing ``pos``.  h fp16 [B, D] is the residual stream and
     rot the already normalised+rotated layer input.  kc/vc u8
@@ -470,7 +476,12 @@ def decode_layer(h, rot, layer, next_norm, cfg, kc, vc, pos, cos_row, sin_row, w
     ``next_norm`` (the next layer's input norm; layer 0's for the last layer,
     hip:2519-2523).  With ``write_kv=False`` the bytes already in the cache at
     ``pos`` are used instead of this layer's own encoding (to check a device
-    step against the cache it wrote).  Returns (h_new, rot_next)."""
+    step against the cache it wrote).  Tensor parallel (no reference
+    counterpart): with ``allreduce`` given, ``layer``/``cfg`` describe this
+    rank's shard (its heads, its intermediate slice; o/down column slices) and
+    o_proj/down_proj produce unrounded partial sums that ``allreduce`` sums
+    over ranks before the single fp16 rounding of the single-GPU step.
+    Returns (h_new, rot_next)."""
     H, Hk, hd, I, eps = (cfg['num_heads'], cfg['num_kv_heads'], cfg['head_dim'],
                          cfg['intermediate_size'], cfg['rms_eps'])
     B = h.shape[0]
@@ -485,17 +496,24 @@ def decode_layer(h, rot, layer, next_norm, cfg, kc, vc, pos, cos_row, sin_row, w
         kc[:, :, pos, :] = kb
         vc[:, :, pos, :] = vb
     att = attention_decode(qo, kc, vc, pos + 1, fwht_out=True).reshape(B, qd)
-    o = linear(att, layer['o'])
+    if allreduce is None:
+        o = linear(att, layer['o'])
+    else:
+        o = np.asarray(allreduce(linear(att, layer['o'], acc=True))).astype(np.float16)
     rot, r = res_norm_fwht(o, h, layer['post_norm'], eps)
     gu = linear(rot, layer['gate_up'])
     act = silu_fwht(gu[:, :I], gu[:, I:2 * I])
-    d = linear(act, layer['down'])
+    if allreduce is None:
+        d = linear(act, layer['down'])
+    else:
+        d = np.asarray(allreduce(linear(act, layer['down'], acc=True))).astype(np.float16)
     rot_next, h_new = res_norm_fwht(d, r, next_norm, eps)
     return h_new, rot_next
 
 
-def decode_step(h, layers, cfg, kcs, vcs, pos, cos, sin, write_kv=True):
-    """``int4_decode_step`` (hip:2343-2528): returns the final hidden fp16 [B, D]."""
+def decode_step(h, layers, cfg, kcs, vcs, pos, cos, sin, write_kv=True, allreduce=None):
+    """``int4_decode_step`` (hip:2343-2528): returns the final hidden fp16 [B, D].
+    ``allreduce``: tensor-parallel shards, see ``decode_layer``."""
     eps = cfg['rms_eps']
     h = np.atleast_2d(np.asarray(h, dtype=np.float16))
     rot = rmsnorm_fwht(h, layers[0]['in_norm'], eps)
@@ -503,7 +521,7 @@ def decode_step(h, layers, cfg, kcs, vcs, pos, cos, sin, write_kv=True):
     for li, layer in enumerate(layers):
         nxt = layers[li + 1]['in_norm'] if li < L - 1 else layers[0]['in_norm']
         h, rot = decode_layer(h, rot, layer, nxt, cfg, kcs[li], vcs[li], pos,
-                              cos[pos], sin[pos], write_kv)
+                              cos[pos], sin[pos], write_kv, allreduce)
     return h
 
 

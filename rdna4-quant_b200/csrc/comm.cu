@@ -1,0 +1,360 @@
+// Tensor-parallel exchange over NVLink peer memory: the collective steps of the
+// TP decode (all-reduce after o_proj and down_proj, vocabulary gather after
+// lm_head).  The reference's TP is torch.distributed / RCCL all_reduce between
+// per-layer GEMVs (SURVEY configs 2-3; int4_engine_v5.py TP wrapper); here the
+// GEMV epilogues push fp32 partials into the peers' buffers and one small
+// kernel per exchange does signal + bounded wait + reduce + residual + sums of
+// squares, so an exchange costs one launch and one NVLink hop.
+//
+// Synchronisation.  flags[src] on every rank holds the last epoch rank src
+// signalled.  A sync kernel takes epoch e = seq + 1 (seq is this rank's local
+// count of completed sync kernels), block 0 publishes e to every peer with a
+// system-scope release store, and every block waits (acquire, bounded by time)
+// until flags[src] >= e for all src.  Monotone epochs make a late reader safe
+// against a peer that has already moved on.  Buffers are double-buffered by
+// call parity; a slot is rewritten by a producer only after that producer has
+// passed the next sync, which needs every reader to have started it, i.e. to
+// have finished reading the slot.  Summation runs in rank order, so every rank
+// computes bit-identical replicated activations.
+//
+// A wait that exceeds ~2 s records R4Q_ERR_TIMEOUT (with the missing ranks) in
+// a local status word (r4q_comm_status) and continues, so the context stays
+// usable; no kernel spins forever.
+#include <cstdio>
+#include <cstring>
+
+#include "comm.cuh"
+#include "r4q_common.cuh"
+
+struct r4q_comm {
+  int rank, world, dev;
+  int max_batch, hidden, vocab;
+  long sa_cap;
+  uint8_t* base;        // this rank's peer-visible allocation
+  size_t bytes;
+  uint8_t* peer[8];     // every rank's allocation as mapped here (peer[rank] = base)
+  bool opened;
+  unsigned long long* ctl;  // local: [0] seq, [1] done counter, [2] status bits
+  size_t off_red, off_gat, off_sa;
+  size_t red_slot, sa_slot;  // floats per (parity, src) slot
+  int sa_calls;
+};
+
+namespace r4q {
+
+namespace {
+
+constexpr int kMaxWorld = 8;
+
+__host__ __device__ inline size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+struct SyncArgs {
+  unsigned long long* flags_local;         // flags[8] of this rank
+  unsigned long long* flags_peer[kMaxWorld];  // flags[8] of each rank (mapped)
+  unsigned long long* ctl;                 // local control words
+  int rank, world;
+};
+
+__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_sys(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long globaltimer() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Signal (block 0) and wait for every rank's signal of this epoch.
+__device__ void comm_sync(const SyncArgs& a, unsigned long long& epoch) {
+  __shared__ unsigned long long s_ep;
+  if (threadIdx.x == 0) s_ep = *(volatile unsigned long long*)&a.ctl[0] + 1;
+  __syncthreads();
+  const unsigned long long e = s_ep;
+  epoch = e;
+  const int t = threadIdx.x;
+  if (blockIdx.x == 0 && t < a.world) {
+    __threadfence_system();  // pushes of earlier kernels are complete; order them first
+    st_release_sys(a.flags_peer[t] + a.rank, e);
+  }
+  if (t < a.world) {
+    const unsigned long long t0 = globaltimer();
+    unsigned it = 0;
+    while (ld_acquire_sys(a.flags_local + t) < e) {
+      if ((++it & 63) == 0 && globaltimer() - t0 > 2000000000ull) {
+        atomicOr(&a.ctl[2], 1ull << t);
+        break;
+      }
+      __nanosleep(64);
+    }
+  }
+  __syncthreads();
+}
+
+// Last block to finish publishes the epoch as completed.
+__device__ void comm_done(const SyncArgs& a, unsigned long long e) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const unsigned long long d = atomicAdd(&a.ctl[1], 1ull);
+    if (d == gridDim.x - 1) {
+      a.ctl[0] = e;
+      a.ctl[1] = 0;
+      __threadfence();
+    }
+  }
+}
+
+__global__ void reduce_residual_kernel(const SyncArgs s, const float* __restrict__ red, long slot,
+                                       const __half* res, __half* out, float* __restrict__ ss_out,
+                                       int B, int D) {
+  unsigned long long e;
+  comm_sync(s, e);
+  const long n = (long)B * D;
+  const long i = ((long)blockIdx.x * blockDim.x + threadIdx.x) * 4;
+  const bool ok = i < n;
+  float sq = 0.0f;
+  if (ok) {
+    float4 acc = __ldcg(reinterpret_cast<const float4*>(red + i));
+    for (int r = 1; r < s.world; ++r) {
+      const float4 v = __ldcg(reinterpret_cast<const float4*>(red + r * slot + i));
+      acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+    }
+    float a4[4] = {acc.x, acc.y, acc.z, acc.w};
+    __half o4[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      float v = __half2float(__float2half(a4[k]));
+      if (res) v += __half2float(res[i + k]);
+      sq += v * v;
+      o4[k] = __float2half(v);
+    }
+#pragma unroll
+    for (int k = 0; k < 4; ++k) out[i + k] = o4[k];
+  }
+  // four consecutive threads hold one 16-element tile (D % 16 == 0)
+  sq += __shfl_xor_sync(0xffffffffu, sq, 1);
+  sq += __shfl_xor_sync(0xffffffffu, sq, 2);
+  if (ok && ss_out && (threadIdx.x & 3) == 0) {
+    const int b = (int)(i / D), d = (int)(i - (long)b * D);
+    ss_out[(long)(d >> 4) * B + b] = sq;
+  }
+  comm_done(s, e);
+}
+
+__global__ void gather_kernel(const SyncArgs s, const float* __restrict__ gat, __half* __restrict__ out,
+                              long n) {
+  unsigned long long e;
+  comm_sync(s, e);
+  for (long i = ((long)blockIdx.x * blockDim.x + threadIdx.x) * 4; i < n; i += (long)gridDim.x * blockDim.x * 4) {
+    const float4 v = __ldcg(reinterpret_cast<const float4*>(gat + i));
+    out[i] = __float2half(v.x);
+    out[i + 1] = __float2half(v.y);
+    out[i + 2] = __float2half(v.z);
+    out[i + 3] = __float2half(v.w);
+  }
+  comm_done(s, e);
+}
+
+// Standalone all-reduce, step 1: push x into slot [rank] of every rank.
+struct PushTable {
+  float* p[kMaxWorld];
+};
+
+__global__ void push_kernel_t(const float* __restrict__ x, const PushTable t, int world, long n) {
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
+    const float v = x[i];
+    for (int r = 0; r < world; ++r) t.p[r][i] = v;
+  }
+  __threadfence_system();
+}
+
+// Standalone all-reduce, step 2: sync, y = sum over src in rank order.
+__global__ void sum_kernel(const SyncArgs s, const float* __restrict__ sa, long slot, float* __restrict__ y,
+                           long n) {
+  unsigned long long e;
+  comm_sync(s, e);
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
+    float v = __ldcg(sa + i);
+    for (int r = 1; r < s.world; ++r) v += __ldcg(sa + r * slot + i);
+    y[i] = v;
+  }
+  comm_done(s, e);
+}
+
+SyncArgs sync_args(r4q_comm* c) {
+  SyncArgs a{};
+  a.flags_local = reinterpret_cast<unsigned long long*>(c->base);
+  for (int r = 0; r < c->world; ++r) a.flags_peer[r] = reinterpret_cast<unsigned long long*>(c->peer[r]);
+  a.ctl = c->ctl;
+  a.rank = c->rank;
+  a.world = c->world;
+  return a;
+}
+
+}  // namespace
+
+float* comm_reduce_slot(r4q_comm* c, int peer, int parity) {
+  return reinterpret_cast<float*>(c->peer[peer] + c->off_red) +
+         ((size_t)(parity & 1) * c->world + c->rank) * c->red_slot;
+}
+float* comm_gather_base(r4q_comm* c, int peer) {
+  return reinterpret_cast<float*>(c->peer[peer] + c->off_gat);
+}
+int comm_rank(const r4q_comm* c) { return c->rank; }
+int comm_world(const r4q_comm* c) { return c->world; }
+int comm_vocab(const r4q_comm* c) { return c->vocab; }
+int comm_max_batch(const r4q_comm* c) { return c->max_batch; }
+int comm_hidden(const r4q_comm* c) { return c->hidden; }
+
+int comm_reduce_residual(r4q_comm* c, int parity, const __half* res, __half* out, float* ss_out, int B,
+                         int D, cudaStream_t st) {
+  if (!c->opened) return set_error(R4Q_ERR_ARG, "comm: peers not opened");
+  if (B > c->max_batch || D != c->hidden || D % 16)
+    return set_error(R4Q_ERR_CAPACITY, "comm reduce: B=%d D=%d exceeds the comm (%d, %d)", B, D,
+                     c->max_batch, c->hidden);
+  const float* red = reinterpret_cast<const float*>(c->base + c->off_red) +
+                     (size_t)(parity & 1) * c->world * c->red_slot;
+  const long n = (long)B * D;
+  const int thr = 256;
+  const int grid = (int)((n / 4 + thr - 1) / thr);
+  reduce_residual_kernel<<<grid, thr, 0, st>>>(sync_args(c), red, (long)c->red_slot, res, out, ss_out,
+                                                B, D);
+  return check_launch("reduce_residual_kernel");
+}
+
+int comm_gather_logits(r4q_comm* c, __half* logits, int B, cudaStream_t st) {
+  if (!c->opened) return set_error(R4Q_ERR_ARG, "comm: peers not opened");
+  if (B > c->max_batch) return set_error(R4Q_ERR_CAPACITY, "comm gather: B=%d > %d", B, c->max_batch);
+  const long n = (long)B * c->vocab;
+  int grid = (int)((n / 4 + 255) / 256);
+  if (grid > 4 * num_sms()) grid = 4 * num_sms();
+  gather_kernel<<<grid, 256, 0, st>>>(sync_args(c), reinterpret_cast<const float*>(c->base + c->off_gat),
+                                      logits, n);
+  return check_launch("gather_kernel");
+}
+
+}  // namespace r4q
+
+using namespace r4q;
+
+extern "C" int r4q_comm_create(int rank, int world, int max_batch, int hidden, int vocab, long sa_cap,
+                               r4q_comm** out, void* handle_out) {
+  if (!out || !handle_out || world < 1 || world > kMaxWorld || rank < 0 || rank >= world ||
+      max_batch < 1 || hidden < 16 || hidden % 16 || vocab < 0 || vocab % 4 || sa_cap < 0)
+    return set_error(R4Q_ERR_ARG, "comm_create: bad arguments (rank %d world %d B %d D %d V %d)", rank,
+                     world, max_batch, hidden, vocab);
+  r4q_comm* c = new r4q_comm();
+  c->rank = rank;
+  c->world = world;
+  c->max_batch = max_batch;
+  c->hidden = hidden;
+  c->vocab = vocab;
+  c->sa_cap = (sa_cap + 63) & ~63L;
+  cudaGetDevice(&c->dev);
+  c->red_slot = align256((size_t)max_batch * hidden * 4) / 4;
+  c->sa_slot = (size_t)c->sa_cap;
+  c->off_red = 256;
+  c->off_gat = c->off_red + 2 * world * c->red_slot * 4;
+  c->off_sa = c->off_gat + align256((size_t)max_batch * vocab * 4);
+  c->bytes = c->off_sa + 2 * world * c->sa_slot * 4 + 256;
+  cudaError_t e = cudaMalloc(&c->base, c->bytes);
+  if (e == cudaSuccess) e = cudaMemset(c->base, 0, c->bytes);
+  if (e == cudaSuccess) e = cudaMalloc(&c->ctl, 256);
+  if (e == cudaSuccess) e = cudaMemset(c->ctl, 0, 256);
+  cudaIpcMemHandle_t h;
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, c->base);
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) {
+    if (c->base) cudaFree(c->base);
+    if (c->ctl) cudaFree(c->ctl);
+    delete c;
+    return set_error(R4Q_ERR_CUDA, "comm_create: %s", cudaGetErrorString(e));
+  }
+  static_assert(sizeof(cudaIpcMemHandle_t) <= R4Q_COMM_HANDLE_BYTES, "IPC handle size");
+  memset(handle_out, 0, R4Q_COMM_HANDLE_BYTES);
+  memcpy(handle_out, &h, sizeof(h));
+  c->peer[rank] = c->base;
+  if (world == 1) c->opened = true;
+  *out = c;
+  return R4Q_OK;
+}
+
+extern "C" int r4q_comm_open(r4q_comm* c, const void* handles) {
+  if (!c || !handles) return set_error(R4Q_ERR_ARG, "comm_open: null argument");
+  if (c->opened) return R4Q_OK;
+  for (int r = 0; r < c->world; ++r) {
+    if (r == c->rank) continue;
+    cudaIpcMemHandle_t h;
+    memcpy(&h, static_cast<const uint8_t*>(handles) + (size_t)r * R4Q_COMM_HANDLE_BYTES, sizeof(h));
+    void* p = nullptr;
+    cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) {
+      for (int q = 0; q < r; ++q)
+        if (q != c->rank && c->peer[q]) {
+          cudaIpcCloseMemHandle(c->peer[q]);
+          c->peer[q] = nullptr;
+        }
+      return set_error(R4Q_ERR_CUDA, "comm_open: rank %d: %s", r, cudaGetErrorString(e));
+    }
+    c->peer[r] = static_cast<uint8_t*>(p);
+  }
+  c->opened = true;
+  return R4Q_OK;
+}
+
+extern "C" int r4q_comm_status(r4q_comm* c) {
+  if (!c) return set_error(R4Q_ERR_ARG, "comm_status: null comm");
+  unsigned long long bits = 0;
+  cudaError_t e = cudaMemcpy(&bits, c->ctl + 2, 8, cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return set_error(R4Q_ERR_CUDA, "comm_status: %s", cudaGetErrorString(e));
+  if (bits) {
+    char who[64] = "";
+    int n = 0;
+    for (int r = 0; r < c->world && n < 60; ++r)
+      if (bits >> r & 1) n += snprintf(who + n, sizeof(who) - n, "%s%d", n ? "," : "", r);
+    return set_error(R4Q_ERR_TIMEOUT, "comm: timed out waiting for rank(s) %s", who);
+  }
+  return R4Q_OK;
+}
+
+extern "C" int r4q_comm_clear_status(r4q_comm* c) {
+  if (!c) return set_error(R4Q_ERR_ARG, "comm_clear_status: null comm");
+  cudaError_t e = cudaMemset(c->ctl + 2, 0, 8);
+  return e == cudaSuccess ? R4Q_OK : set_error(R4Q_ERR_CUDA, "comm_clear_status: %s", cudaGetErrorString(e));
+}
+
+extern "C" int r4q_comm_allreduce_f32(r4q_comm* c, const float* x, float* y, long n, void* stream) {
+  if (!c || !x || !y || n < 0) return set_error(R4Q_ERR_ARG, "comm_allreduce: bad arguments");
+  if (!c->opened) return set_error(R4Q_ERR_ARG, "comm_allreduce: peers not opened");
+  if (n > c->sa_cap)
+    return set_error(R4Q_ERR_CAPACITY, "comm_allreduce: %ld elements > capacity %ld", n, c->sa_cap);
+  cudaStream_t st = (cudaStream_t)stream;
+  const int par = c->sa_calls & 1;
+  c->sa_calls++;
+  PushTable t{};
+  for (int r = 0; r < c->world; ++r)
+    t.p[r] = reinterpret_cast<float*>(c->peer[r] + c->off_sa) + ((size_t)par * c->world + c->rank) * c->sa_slot;
+  int grid = (int)((n + 255) / 256);
+  if (grid > 2 * num_sms()) grid = 2 * num_sms();
+  if (grid < 1) grid = 1;
+  push_kernel_t<<<grid, 256, 0, st>>>(x, t, c->world, n);
+  int rc = check_launch("push_kernel");
+  if (rc) return rc;
+  const float* sa = reinterpret_cast<const float*>(c->base + c->off_sa) + (size_t)par * c->world * c->sa_slot;
+  sum_kernel<<<grid, 256, 0, st>>>(sync_args(c), sa, (long)c->sa_slot, y, n);
+  return check_launch("sum_kernel");
+}
+
+extern "C" void r4q_comm_destroy(r4q_comm* c) {
+  if (!c) return;
+  cudaDeviceSynchronize();
+  for (int r = 0; r < c->world; ++r)
+    if (r != c->rank && c->peer[r]) cudaIpcCloseMemHandle(c->peer[r]);
+  if (c->base) cudaFree(c->base);
+  if (c->ctl) cudaFree(c->ctl);
+  delete c;
+}

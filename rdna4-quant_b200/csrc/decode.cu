@@ -20,6 +20,7 @@
 #include <cstring>
 #include <vector>
 
+#include "comm.cuh"
 #include "gemv.cuh"
 #include "r4q_common.cuh"
 
@@ -53,7 +54,8 @@ __global__ void set_positions(long long* pos, long long* seq, int B, int p) {
 
 static int gemv_call(r4q_decode_ctx* c, int fmt, const void* w, const void* s, const void* x, void* y,
                      int N, int K, int prologue, const void* norm_w, const float* ss_in, int ss_parts,
-                     const void* res, float* ss_out, cudaStream_t st) {
+                     const void* res, float* ss_out, cudaStream_t st, float* const* push = nullptr,
+                     int npush = 0, long ld_push = 0) {
   GemvArgs a{};
   a.x = x;
   a.ldx = (prologue == R4Q_PRO_SILU_FWHT) ? 2L * K : K;
@@ -75,7 +77,23 @@ static int gemv_call(r4q_decode_ctx* c, int fmt, const void* w, const void* s, c
   a.res = res;
   a.ldres = N;
   a.ss_out = ss_out;
+  if (npush) {  // fp32 partial sums straight into every rank's exchange buffer
+    a.npush = npush;
+    for (int q = 0; q < npush; ++q) a.y32p[q] = push[q];
+    a.ldy = ld_push;
+  }
   return launch_gemv(a, fmt);
+}
+
+// Push targets of this rank's slot in every rank's all-reduce buffer.
+struct PushSet {
+  float* p[8];
+  operator float* const*() const { return p; }
+};
+static PushSet push_slots(r4q_decode_ctx* c, int parity) {
+  PushSet s{};
+  for (int q = 0; q < c->m.tp_size; ++q) s.p[q] = comm_reduce_slot(c->m.comm, q, parity);
+  return s;
 }
 
 static int enqueue_step(r4q_decode_ctx* c, bool with_logits, cudaStream_t st) {
@@ -84,6 +102,8 @@ static int enqueue_step(r4q_decode_ctx* c, bool with_logits, cudaStream_t st) {
             hd = m.head_dim;
   const int qd = H * hd, kvd = Hk * hd, qkv_n = qd + 2 * kvd;
   const int L = m.num_layers;
+  const bool tp = m.tp_size > 1;
+  int par = 0;  // exchange-buffer parity: 2 exchanges per layer, every step starts at 0
   int rc = 0;
   for (int li = 0; li < L && !rc; ++li) {
     const r4q_layer_desc& ly = c->layers[li];
@@ -104,20 +124,44 @@ static int enqueue_step(r4q_decode_ctx* c, bool with_logits, cudaStream_t st) {
                           c->attn_ws_bytes, st);
     if (rc) break;
     // 4. o_proj + residual -> r, sums of squares for the post-attention norm
-    rc = gemv_call(c, ly.o_fmt, ly.o_w, ly.o_s, c->attn, c->r, D, qd, R4Q_PRO_NONE, nullptr, nullptr,
-                   0, hin, c->ss_post, st);
+    if (tp) {
+      // partial over this rank's heads, pushed to every rank; reduce + residual
+      rc = gemv_call(c, ly.o_fmt, ly.o_w, ly.o_s, c->attn, nullptr, D, qd, R4Q_PRO_NONE, nullptr,
+                     nullptr, 0, nullptr, nullptr, st, push_slots(c, par), m.tp_size, D);
+      if (!rc) rc = comm_reduce_residual(m.comm, par, hin, c->r, c->ss_post, B, D, st);
+      par ^= 1;
+    } else {
+      rc = gemv_call(c, ly.o_fmt, ly.o_w, ly.o_s, c->attn, c->r, D, qd, R4Q_PRO_NONE, nullptr, nullptr,
+                     0, hin, c->ss_post, st);
+    }
     if (rc) break;
     // 5. gate_up with RMSNorm + FWHT of r
     rc = gemv_call(c, ly.gate_up_fmt, ly.gate_up_w, ly.gate_up_s, c->r, c->gu, 2 * I, D,
                    R4Q_PRO_RMSNORM_FWHT, ly.post_norm, c->ss_post, D / 16, nullptr, nullptr, st);
     if (rc) break;
     // 6. down with SiLU*up + FWHT, + residual r -> h, sums of squares for the next norm
-    rc = gemv_call(c, ly.down_fmt, ly.down_w, ly.down_s, c->gu, c->h, D, I, R4Q_PRO_SILU_FWHT, nullptr,
-                   nullptr, 0, c->r, c->ss_h, st);
+    if (tp) {
+      rc = gemv_call(c, ly.down_fmt, ly.down_w, ly.down_s, c->gu, nullptr, D, I, R4Q_PRO_SILU_FWHT,
+                     nullptr, nullptr, 0, nullptr, nullptr, st, push_slots(c, par), m.tp_size, D);
+      if (!rc) rc = comm_reduce_residual(m.comm, par, c->r, c->h, c->ss_h, B, D, st);
+      par ^= 1;
+    } else {
+      rc = gemv_call(c, ly.down_fmt, ly.down_w, ly.down_s, c->gu, c->h, D, I, R4Q_PRO_SILU_FWHT, nullptr,
+                     nullptr, 0, c->r, c->ss_h, st);
+    }
   }
   if (rc || !with_logits) return rc;
-  return gemv_call(c, m.lm_fmt, m.lm_w, m.lm_s, L > 0 ? c->h : c->h_in, c->logits, m.lm_n, D,
-                   R4Q_PRO_RMSNORM_FWHT, m.final_norm, nullptr, 0, nullptr, nullptr, st);
+  const __half* hl = L > 0 ? c->h : c->h_in;
+  if (!tp)
+    return gemv_call(c, m.lm_fmt, m.lm_w, m.lm_s, hl, c->logits, m.lm_n, D, R4Q_PRO_RMSNORM_FWHT,
+                     m.final_norm, nullptr, 0, nullptr, nullptr, st);
+  // vocabulary slice of this rank pushed into every rank's gather buffer
+  float* gp[8];
+  for (int q = 0; q < m.tp_size; ++q) gp[q] = comm_gather_base(m.comm, q) + (long)m.tp_rank * m.lm_n;
+  rc = gemv_call(c, m.lm_fmt, m.lm_w, m.lm_s, hl, nullptr, m.lm_n, D, R4Q_PRO_RMSNORM_FWHT, m.final_norm,
+                 nullptr, 0, nullptr, nullptr, st, gp, m.tp_size, (long)m.lm_n * m.tp_size);
+  if (rc) return rc;
+  return comm_gather_logits(m.comm, c->logits, B, st);
 }
 
 static void free_ctx(r4q_decode_ctx* c) {
@@ -144,8 +188,20 @@ extern "C" int r4q_decode_ctx_create(const r4q_model_desc* md, const r4q_layer_d
       m.num_heads % m.num_kv_heads || m.num_heads / m.num_kv_heads > 8 || m.max_seq < 1 ||
       (m.num_heads * m.head_dim) % 128)
     return set_error(R4Q_ERR_ARG, "decode_ctx_create: unsupported model shape");
+  const int tps = m.tp_size < 1 ? 1 : m.tp_size;
+  if (tps > 1) {
+    if (tps > 8 || !m.comm || m.tp_rank < 0 || m.tp_rank >= tps || comm_world(m.comm) != tps ||
+        comm_rank(m.comm) != m.tp_rank)
+      return set_error(R4Q_ERR_ARG, "decode_ctx_create: tp_size %d / tp_rank %d do not match the comm",
+                       m.tp_size, m.tp_rank);
+    if (m.num_layers < 1 || m.batch > comm_max_batch(m.comm) || m.hidden != comm_hidden(m.comm) ||
+        (m.lm_w && (long)m.lm_n * tps != comm_vocab(m.comm)))
+      return set_error(R4Q_ERR_ARG, "decode_ctx_create: comm sized for B %d D %d V %d",
+                       comm_max_batch(m.comm), comm_hidden(m.comm), comm_vocab(m.comm));
+  }
   r4q_decode_ctx* c = new r4q_decode_ctx();  // value-initialised: all pointers null
   c->m = m;
+  c->m.tp_size = tps;
   c->layers.assign(layers, layers + m.num_layers);
   cudaGetDevice(&c->dev);
   const int B = m.batch, D = m.hidden, I = m.intermediate;
@@ -162,7 +218,7 @@ extern "C" int r4q_decode_ctx_create(const r4q_model_desc* md, const r4q_layer_d
   } al[] = {{(void**)&c->h_in, (size_t)B * D * 2},       {(void**)&c->h, (size_t)B * D * 2},
             {(void**)&c->r, (size_t)B * D * 2},          {(void**)&c->qkv, (size_t)B * qkv_n * 2},
             {(void**)&c->attn, (size_t)B * qd * 2},      {(void**)&c->gu, (size_t)B * 2 * I * 2},
-            {(void**)&c->logits, (size_t)B * m.lm_n * 2 + 16}, {(void**)&c->h_out, (size_t)B * D * 2},
+            {(void**)&c->logits, (size_t)B * m.lm_n * tps * 2 + 16}, {(void**)&c->h_out, (size_t)B * D * 2},
             {(void**)&c->ss_post, (size_t)D / 16 * B * 4}, {(void**)&c->ss_h, (size_t)D / 16 * B * 4},
             {(void**)&c->pos_dev, (size_t)B * 8},         {(void**)&c->seq_dev, (size_t)B * 8},
             {&c->gemv_ws, c->gemv_ws_bytes},              {&c->attn_ws, c->attn_ws_bytes}};
@@ -247,7 +303,8 @@ extern "C" int r4q_decode_step(r4q_decode_ctx* c, const void* hidden_in, int pos
     if (e != cudaSuccess) return set_error(R4Q_ERR_CUDA, "decode_step: copy out: %s", cudaGetErrorString(e));
   }
   if (logits_out) {
-    e = cudaMemcpyAsync(logits_out, c->logits, (size_t)B * c->m.lm_n * 2, cudaMemcpyDeviceToDevice, st);
+    e = cudaMemcpyAsync(logits_out, c->logits, (size_t)B * c->m.lm_n * c->m.tp_size * 2,
+                        cudaMemcpyDeviceToDevice, st);
     if (e != cudaSuccess) return set_error(R4Q_ERR_CUDA, "decode_step: copy logits: %s", cudaGetErrorString(e));
   }
   return R4Q_OK;

@@ -207,7 +207,12 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const GemvParams p) {
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
           const int c = cg * 8 + 2 * t + h;
-          if (c < p.B) {
+          if (c < p.B && p.npush) {
+            for (int q = 0; q < p.npush; ++q) {
+              p.y32p[q][(long)c * p.ldy + row_a] = acc[cg][h];
+              p.y32p[q][(long)c * p.ldy + row_b] = acc[cg][2 + h];
+            }
+          } else if (c < p.B) {
             float va = __half2float(__float2half(acc[cg][h]));
             float vb = __half2float(__float2half(acc[cg][2 + h]));
             if (p.res) {
@@ -247,6 +252,7 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const GemvParams p) {
       }
     }
   }
+  if (p.npush > 1) __threadfence_system();  // peer outputs complete before exit
   if (p.ksplit == 1) return;
 
   // ---- split-K fixup: the last CTA of this row tile sums partials in order ----
@@ -267,6 +273,11 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const GemvParams p) {
     const int r = trow0 + ti * 16 + (lane & 15);
     float v = 0.0f;
     for (int k2 = 0; k2 < p.ksplit; ++k2) v += __ldcg(p.part + ((long)k2 * p.B + col) * p.N + r);
+    if (p.npush) {
+      if (lane < 16)
+        for (int q = 0; q < p.npush; ++q) p.y32p[q][(long)col * p.ldy + r] = v;
+      continue;
+    }
     v = __half2float(__float2half(v));
     if (p.res) v += __half2float(p.res[(long)col * p.ldres + r]);
     if (lane < 16) p.y[(long)col * p.ldy + r] = __float2half(v);
@@ -275,6 +286,7 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const GemvParams p) {
     if (p.ss_out && lane == 0) p.ss_out[(long)((trow0 >> 4) + ti) * p.B + col] = sq;
   }
   if (tid == 0) p.cnt[blockIdx.x] = 0u;  // leave the workspace zeroed for the next launch
+  if (p.npush > 1) __threadfence_system();
 }
 
 // ------------------------------------------------------------- planning ---
@@ -365,6 +377,8 @@ static int launch_gemv_t(const GemvArgs& a) {
   p.res = reinterpret_cast<const __half*>(a.res);
   p.ldres = a.ldres;
   p.ss_out = a.ss_out;
+  p.npush = a.npush;
+  for (int q = 0; q < 8; ++q) p.y32p[q] = q < a.npush ? a.y32p[q] : nullptr;
   p.cnt = reinterpret_cast<unsigned*>(a.ws);
   p.part = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(a.ws) + gemv_cnt_bytes(a.N));
   if (pl.ksplit > 1 && a.ws == nullptr)
@@ -383,8 +397,11 @@ size_t gemv_ws_bytes_for(int B, int N, int ksplit) {
 }
 
 int gemv_validate(const GemvArgs& a, int fmt) {
-  if (!a.x || !a.w || !a.y || (fmt != W_FP16 && !a.s))
+  if (!a.x || !a.w || (!a.y && !a.npush) || (fmt != W_FP16 && !a.s))
     return set_error(R4Q_ERR_ARG, "gemv: null pointer");
+  if (a.npush < 0 || a.npush > 8) return set_error(R4Q_ERR_ARG, "gemv: %d fp32 outputs (max 8)", a.npush);
+  for (int q = 0; q < a.npush; ++q)
+    if (!a.y32p[q] || !aligned(a.y32p[q], 4)) return set_error(R4Q_ERR_ALIGN, "gemv: fp32 output %d null or misaligned", q);
   if (a.B < 1 || a.B > 16) return set_error(R4Q_ERR_ARG, "gemv: B=%d outside 1..16", a.B);
   if (a.N <= 0 || a.N % 16) return set_error(R4Q_ERR_ARG, "gemv: N=%d must be a positive multiple of 16", a.N);
   if (a.N / 16 > kMaxTiles16) return set_error(R4Q_ERR_ARG, "gemv: N=%d above %d", a.N, kMaxTiles16 * 16);
@@ -482,6 +499,10 @@ extern "C" int r4q_gemv(int wfmt, const void* x, long ldx, const void* w, const 
     a.res = f->residual;
     a.ldres = (B > 1) ? f->ldres : N;
     a.ss_out = f->ss_out;
+    if (f->y32) {
+      a.y32p[0] = f->y32;
+      a.npush = 1;
+    }
   }
   if (a.prologue == R4Q_PRO_RMSNORM_FWHT && !f)
     return set_error(R4Q_ERR_ARG, "gemv: RMSNorm prologue needs fused parameters");

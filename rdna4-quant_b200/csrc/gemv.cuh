@@ -27,6 +27,9 @@ struct GemvArgs {
   const void* res;
   long ldres;
   float* ss_out;
+  // fp32 sums to npush arrays (local or peer memory) instead of fp16 y
+  float* y32p[8];
+  int npush;
 };
 
 size_t gemv_cnt_bytes(int N);

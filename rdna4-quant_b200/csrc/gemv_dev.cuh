@@ -35,6 +35,11 @@ struct GemvParams {
   const __half* res;     // [B][ldres] or null
   long ldres;
   float* ss_out;         // [N/16][B] or null
+  // fp32 outputs instead of y (no rounding, no residual): each value goes to
+  // all npush arrays, y32p[q][c * ldy + n] (tensor-parallel partials pushed
+  // straight into the peers' reduce buffers)
+  float* y32p[8];
+  int npush;
 };
 
 __host__ __device__ inline int steps_total(int K, int ck, int u) {

@@ -526,7 +526,12 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
           const int c = cg * 8 + 2 * t + h;
-          if (c < p.B) {
+          if (c < p.B && p.npush) {
+            for (int q = 0; q < p.npush; ++q) {
+              p.y32p[q][(long)c * p.ldy + row_a] = r[cg][h];
+              p.y32p[q][(long)c * p.ldy + row_b] = r[cg][2 + h];
+            }
+          } else if (c < p.B) {
             float va = __half2float(__float2half(r[cg][h]));
             float vb = __half2float(__float2half(r[cg][2 + h]));
             if (p.res) {
@@ -577,6 +582,11 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
         for (int col = 0; col < p.B; ++col) {
           float v = 0.0f;
           for (int k2 = 0; k2 < cur.n; ++k2) v += __ldcg(p.part + ((long)k2 * p.B + col) * p.N + rr);
+          if (p.npush) {
+            if (lane < 16)
+              for (int q = 0; q < p.npush; ++q) p.y32p[q][(long)col * p.ldy + rr] = v;
+            continue;
+          }
           v = __half2float(__float2half(v));
           if (p.res) v += __half2float(p.res[(long)col * p.ldres + rr]);
           if (lane < 16) p.y[(long)col * p.ldy + rr] = __float2half(v);
@@ -589,6 +599,8 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
     }
     if (ctid == 0) TRACE(3, uidx);
   }
+  // outputs pushed into peer memory: complete them system-wide before exit
+  if (p.npush > 1) __threadfence_system();
   if (ctid == 0) TRACE(0, 2);
 }
 
@@ -739,6 +751,8 @@ static int launch_tma_t(const GemvArgs& a) {
   p.res = reinterpret_cast<const __half*>(a.res);
   p.ldres = a.ldres;
   p.ss_out = a.ss_out;
+  p.npush = a.npush;
+  for (int q = 0; q < 8; ++q) p.y32p[q] = q < a.npush ? a.y32p[q] : nullptr;
   p.cnt = reinterpret_cast<unsigned*>(a.ws);
   p.part = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(a.ws) + gemv_cnt_bytes(a.N));
   tp.nstages = (a.K + T::SK - 1) / T::SK;

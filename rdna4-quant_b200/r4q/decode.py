@@ -57,13 +57,17 @@ def _p(t):
 def get_context(qkv_w, qkv_s, o_w, o_s, gu_w, gu_s, down_w, down_s, in_norm_w, post_norm_w,
                 q_norm_w, k_norm_w, rope_cos, rope_sin, num_heads, num_kv_heads, head_dim,
                 hidden_size, intermediate_size, rms_eps, k_caches, v_caches, final_norm_w=None,
-                lm_w=None, lm_s=None, lm_N=0, batch=1, k_scales=None, v_scales=None):
+                lm_w=None, lm_s=None, lm_N=0, batch=1, k_scales=None, v_scales=None, comm=None):
+    """Context for these weights/caches.  With ``comm`` (r4q.tp.Comm of
+    world > 1) the tensors are this rank's shards and the head / intermediate
+    / vocabulary counts are the local ones (r4q.tp.local_cfg)."""
     n = len(qkv_w)
     max_seq = int(k_caches[0].shape[-2]) if n else 1
     key = (tuple(t.data_ptr() for t in (*qkv_w, *o_w, *gu_w, *down_w, *k_caches, *v_caches)),
            _p(final_norm_w), _p(lm_w), int(lm_N), int(batch), int(hidden_size),
            int(intermediate_size), int(num_heads), int(num_kv_heads), int(head_dim), max_seq,
-           float(rms_eps), _p(rope_cos), torch.cuda.current_device())
+           float(rms_eps), _p(rope_cos), torch.cuda.current_device(),
+           None if comm is None else comm.handle.value)
     with _lock:
         ctx = _ctx.get(key)
         if ctx is not None:
@@ -94,7 +98,11 @@ def get_context(qkv_w, qkv_s, o_w, o_s, gu_w, gu_s, down_w, down_s, in_norm_w, p
             m.lm_fmt = weight_format(lm_w)
             m.lm_w, m.lm_s = lm_w.data_ptr(), _p(lm_s) if m.lm_fmt != L.W_FP16 else None
             m.lm_n = int(lm_N)
-        keep = (qkv_w, qkv_s, o_w, o_s, gu_w, gu_s, down_w, down_s, in_norm_w, post_norm_w,
+        if comm is not None and comm.world > 1:
+            m.tp_rank, m.tp_size, m.comm = comm.rank, comm.world, comm.handle.value
+        else:
+            m.tp_rank, m.tp_size, m.comm = 0, 1, None
+        keep = (comm, qkv_w, qkv_s, o_w, o_s, gu_w, gu_s, down_w, down_s, in_norm_w, post_norm_w,
                 q_norm_w, k_norm_w, rope_cos, rope_sin, k_caches, v_caches, final_norm_w, lm_w,
                 lm_s, k_scales, v_scales)
         ctx = DecodeContext(m, layers, keep)

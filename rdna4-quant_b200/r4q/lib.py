@@ -39,7 +39,7 @@ class GemvFused(C.Structure):
     """r4q_gemv_fused (include/r4q.h)."""
     _fields_ = [("norm_w", C.c_void_p), ("eps", C.c_float), ("ss_in", C.c_void_p),
                 ("ss_in_parts", C.c_int), ("residual", C.c_void_p), ("ldres", C.c_long),
-                ("ss_out", C.c_void_p)]
+                ("ss_out", C.c_void_p), ("y32", C.c_void_p)]
 
 vp, i32, i64, sz_t, f32 = C.c_void_p, C.c_int, C.c_long, C.c_size_t, C.c_float
 
@@ -59,7 +59,8 @@ class ModelDesc(C.Structure):
                                         "num_kv_heads", "head_dim", "max_seq")] + [
         ("rms_eps", C.c_float), ("rope_cos", C.c_void_p), ("rope_sin", C.c_void_p),
         ("rope_stride", C.c_long), ("final_norm", C.c_void_p), ("lm_fmt", C.c_int),
-        ("lm_w", C.c_void_p), ("lm_s", C.c_void_p), ("lm_n", C.c_int)]
+        ("lm_w", C.c_void_p), ("lm_s", C.c_void_p), ("lm_n", C.c_int), ("tp_rank", C.c_int),
+        ("tp_size", C.c_int), ("comm", C.c_void_p)]
 
 _SIGS = {
     "r4q_last_error": (C.c_char_p, []),
@@ -80,10 +81,18 @@ _SIGS = {
     "r4q_decode_ctx_create": (i32, [C.POINTER(ModelDesc), C.POINTER(LayerDesc), C.POINTER(C.c_void_p)]),
     "r4q_decode_ctx_destroy": (None, [vp]),
     "r4q_decode_step": (i32, [vp, vp, i32, vp, vp, i32, vp]),
+    "r4q_comm_create": (i32, [i32, i32, i32, i32, i32, i64, C.POINTER(C.c_void_p), vp]),
+    "r4q_comm_open": (i32, [vp, vp]),
+    "r4q_comm_status": (i32, [vp]),
+    "r4q_comm_clear_status": (i32, [vp]),
+    "r4q_comm_allreduce_f32": (i32, [vp, vp, vp, i64, vp]),
+    "r4q_comm_destroy": (None, [vp]),
     "r4q_dequant_int4": (i32, [vp, vp, vp, i32, i32, vp]),
     "r4q_fp16_to_fp8": (i32, [vp, vp, i64, vp]),
     "r4q_fp8_to_fp32": (i32, [vp, vp, i64, vp]),
 }
+
+COMM_HANDLE_BYTES = 64
 
 EXPORTS = []
 for _name, (_res, _args) in _SIGS.items():

@@ -52,13 +52,14 @@ def gemv(fmt: str, x: torch.Tensor, w: torch.Tensor, s: torch.Tensor | None, N: 
          prologue: int = L.PRO_NONE, out: torch.Tensor | None = None, *,
          norm_w: torch.Tensor | None = None, eps: float = 1e-6,
          ss_in: torch.Tensor | None = None, residual: torch.Tensor | None = None,
-         ss_out: torch.Tensor | None = None) -> torch.Tensor:
+         ss_out: torch.Tensor | None = None, out32: torch.Tensor | None = None) -> torch.Tensor:
     """y[B, N] = prologue(x)[B, K] @ dequant(W)^T for fmt in {'int4','int8','fp16'}.
 
     Optional fusions: RMSNorm prologue (``prologue=PRO_RMSNORM_FWHT`` with
     ``norm_w`` and, optionally, ``ss_in`` partial sums of squares [P, B]);
     residual epilogue y = fp16(fp16(acc) + residual) with ``ss_out`` [N/16, B]
-    receiving the sums of squares of the unrounded sums."""
+    receiving the sums of squares of the unrounded sums.  ``out32`` (fp32 [B, N]):
+    write the unrounded fp32 sums there instead (no fp16 output, no residual)."""
     dev = _require_cuda(x, w)
     if x.dtype != torch.float16:
         raise TypeError("x must be float16")
@@ -69,25 +70,27 @@ def gemv(fmt: str, x: torch.Tensor, w: torch.Tensor, s: torch.Tensor | None, N: 
     kin = 2 * K if prologue == L.PRO_SILU_FWHT else K
     if x2.shape[1] < kin:
         raise ValueError(f"x has {x2.shape[1]} columns, need {kin}")
-    if out is None:
+    if out is None and out32 is None:
         out = torch.empty(B, N, dtype=torch.float16, device=dev)
     ws = gemv_workspace(dev, B, N, K)
     st = stream_handle(dev)
     ldx = x2.stride(0) if B > 1 else kin
-    ldy = out.stride(0) if B > 1 else N
+    yt = out if out32 is None else out32
+    ldy = yt.stride(0) if B > 1 else N
     fused = None
-    if norm_w is not None or residual is not None or ss_out is not None or ss_in is not None:
+    if (norm_w is not None or residual is not None or ss_out is not None or ss_in is not None
+            or out32 is not None):
         if residual is not None:
             residual = residual.reshape(B, -1)
         fused = L.GemvFused(
             norm_w=_ptr(norm_w), eps=float(eps), ss_in=_ptr(ss_in),
             ss_in_parts=0 if ss_in is None else int(ss_in.shape[0]),
             residual=_ptr(residual), ldres=N if residual is None else residual.stride(0),
-            ss_out=_ptr(ss_out))
-    L.call("r4q_gemv", _FMT[fmt], x2.data_ptr(), ldx, w.data_ptr(), _ptr(s), out.data_ptr(), ldy,
+            ss_out=_ptr(ss_out), y32=_ptr(out32))
+    L.call("r4q_gemv", _FMT[fmt], x2.data_ptr(), ldx, w.data_ptr(), _ptr(s), _ptr(out), ldy,
            B, N, K, prologue, None if fused is None else C.byref(fused), ws.data_ptr(), ws.numel(),
            st)
-    return out
+    return out if out32 is None else out32
 
 
 def dequant_int4(packed: torch.Tensor, sz: torch.Tensor, N: int, K: int) -> torch.Tensor:

@@ -63,3 +63,26 @@ def test_residual_epilogue_aliasing_in_place():
     ops.gemv('int4', cuda(x), cuda(p), cuda(s), D, K, out=ht, residual=ht)
     ref = (O.gemv_int4(x, p, s).astype(np.float32) + h.astype(np.float32)).astype(np.float16)
     close(ht.cpu().numpy(), ref)
+
+
+@pytest.mark.parametrize("fmt", ['int4', 'int8'])
+@pytest.mark.parametrize("B,N,K", [(1, 5120, 640), (1, 5120, 2176), (2, 5120, 17408), (4, 1024, 5120),
+                                   (16, 5120, 2048)])
+def test_fp32_partial_output(fmt, B, N, K):
+    """fp32 output (tensor-parallel partial): fp16(y32) equals the fp16 output
+    bit for bit on every path (direct and split-K merge), including the
+    o_proj / down_proj column-shard widths of TP=8 (640, 2176)."""
+    from r4q import ops
+    rng = np.random.default_rng(B * 7 + K)
+    x = rng.standard_normal((B, K)).astype(np.float16)
+    if fmt == 'int4':
+        w, s = make_int4(rng, N, K)
+    else:
+        q, s = O.quantize_int8_sym((rng.standard_normal((N, K)) * 0.05).reshape(N, K // 32, 32))
+        w = q.reshape(N, K)
+    y16 = ops.gemv(fmt, cuda(x), cuda(w), cuda(s), N, K)
+    y32 = ops.gemv(fmt, cuda(x), cuda(w), cuda(s), N, K, out32=torch.empty(B, N, device='cuda'))
+    assert y32.dtype == torch.float32
+    assert torch.equal(y32.half(), y16)
+    ref = O.linear(x, (fmt, w, s), acc=True)
+    close(y32.cpu().numpy(), ref)
