@@ -219,6 +219,13 @@ void r4q_decode_ctx_destroy(r4q_decode_ctx* ctx);
 int r4q_decode_step(r4q_decode_ctx* ctx, const void* hidden_in, int pos, void* hidden_out,
                     void* logits_out, int use_graph, void* stream);
 
+/* Exchange timeline of a tensor-parallel context created with the environment
+ * variable R4Q_TP_TRACE set (synchronous; host array of 6 x 256 u64 global-timer
+ * stamps in ns, per exchange index: producer compute start, producer signal,
+ * consumer wait start, consumer wait end, consumer input staged, producer
+ * entry).  A profiling aid; R4Q_ERR_ARG when the context has no trace. */
+int r4q_decode_tp_trace(r4q_decode_ctx* ctx, unsigned long long* host);
+
 /* ------------------------------------------- tensor-parallel exchange --- */
 /* One comm per rank, one process per GPU.  It replaces the torch.distributed
  * all_reduce the reference's TP path runs between per-layer GEMVs: each rank

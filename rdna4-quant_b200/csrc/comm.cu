@@ -24,6 +24,7 @@
 #include <cstring>
 
 #include "comm.cuh"
+#include "tp_exchange.cuh"
 #include "r4q_common.cuh"
 
 struct r4q_comm {
@@ -34,7 +35,9 @@ struct r4q_comm {
   size_t bytes;
   uint8_t* peer[8];     // every rank's allocation as mapped here (peer[rank] = base)
   bool opened;
-  unsigned long long* ctl;  // local: [0] seq, [1] done counter, [2] status bits
+  // local control words: [0] standalone seq, [1] standalone done counter,
+  // [2] status bits, [3] step counter; then u32 done counters [256] at byte 64
+  unsigned long long* ctl;
   size_t off_red, off_gat, off_sa;
   size_t red_slot, sa_slot;  // floats per (parity, src) slot
   int sa_calls;
@@ -52,8 +55,14 @@ struct SyncArgs {
   unsigned long long* flags_local;         // flags[8] of this rank
   unsigned long long* flags_peer[kMaxWorld];  // flags[8] of each rank (mapped)
   unsigned long long* ctl;                 // local control words
+  const unsigned long long* ep_ctr;        // static epochs (step counter) or null
+  int ep_idx;
+  bool signal;
   int rank, world;
 };
+
+constexpr size_t kFlagsX = 0;     // flags of the decode-step exchanges (static epochs)
+constexpr size_t kFlagsSA = 64;   // flags of the standalone all-reduce (sequence epochs)
 
 __device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long* p) {
   unsigned long long v;
@@ -69,15 +78,19 @@ __device__ __forceinline__ unsigned long long globaltimer() {
   return t;
 }
 
-// Signal (block 0) and wait for every rank's signal of this epoch.
+// Signal (block 0) and wait for every rank's signal of this epoch.  Static
+// epochs (ep_ctr set): the epoch comes from the step counter and the exchange
+// index, and the producers have already signalled (signal = false).
 __device__ void comm_sync(const SyncArgs& a, unsigned long long& epoch) {
   __shared__ unsigned long long s_ep;
-  if (threadIdx.x == 0) s_ep = *(volatile unsigned long long*)&a.ctl[0] + 1;
+  if (threadIdx.x == 0)
+    s_ep = a.ep_ctr ? *(volatile unsigned long long*)a.ep_ctr * kTpExchangesPerStep + a.ep_idx + 1
+                    : *(volatile unsigned long long*)&a.ctl[0] + 1;
   __syncthreads();
   const unsigned long long e = s_ep;
   epoch = e;
   const int t = threadIdx.x;
-  if (blockIdx.x == 0 && t < a.world) {
+  if (a.signal && blockIdx.x == 0 && t < a.world) {
     __threadfence_system();  // pushes of earlier kernels are complete; order them first
     st_release_sys(a.flags_peer[t] + a.rank, e);
   }
@@ -89,7 +102,7 @@ __device__ void comm_sync(const SyncArgs& a, unsigned long long& epoch) {
         atomicOr(&a.ctl[2], 1ull << t);
         break;
       }
-      __nanosleep(64);
+      __nanosleep(32);
     }
   }
   __syncthreads();
@@ -97,6 +110,7 @@ __device__ void comm_sync(const SyncArgs& a, unsigned long long& epoch) {
 
 // Last block to finish publishes the epoch as completed.
 __device__ void comm_done(const SyncArgs& a, unsigned long long e) {
+  if (a.ep_ctr) return;
   __syncthreads();
   if (threadIdx.x == 0) {
     const unsigned long long d = atomicAdd(&a.ctl[1], 1ull);
@@ -185,15 +199,21 @@ __global__ void sum_kernel(const SyncArgs s, const float* __restrict__ sa, long 
   comm_done(s, e);
 }
 
-SyncArgs sync_args(r4q_comm* c) {
+SyncArgs sync_args(r4q_comm* c, size_t flags_off, int ep_idx, bool static_epoch) {
   SyncArgs a{};
-  a.flags_local = reinterpret_cast<unsigned long long*>(c->base);
-  for (int r = 0; r < c->world; ++r) a.flags_peer[r] = reinterpret_cast<unsigned long long*>(c->peer[r]);
+  a.flags_local = reinterpret_cast<unsigned long long*>(c->base + flags_off);
+  for (int r = 0; r < c->world; ++r)
+    a.flags_peer[r] = reinterpret_cast<unsigned long long*>(c->peer[r] + flags_off);
   a.ctl = c->ctl;
+  a.ep_ctr = static_epoch ? c->ctl + 3 : nullptr;
+  a.ep_idx = ep_idx;
+  a.signal = !static_epoch;
   a.rank = c->rank;
   a.world = c->world;
   return a;
 }
+
+__global__ void tick_kernel(unsigned long long* ctr) { *ctr += 1ull; }
 
 }  // namespace
 
@@ -210,8 +230,35 @@ int comm_vocab(const r4q_comm* c) { return c->vocab; }
 int comm_max_batch(const r4q_comm* c) { return c->max_batch; }
 int comm_hidden(const r4q_comm* c) { return c->hidden; }
 
-int comm_reduce_residual(r4q_comm* c, int parity, const __half* res, __half* out, float* ss_out, int B,
-                         int D, cudaStream_t st) {
+void comm_fill_signal(r4q_comm* c, TpExchange& x, int idx) {
+  for (int q = 0; q < c->world; ++q)
+    x.sig[q] = reinterpret_cast<unsigned long long*>(c->peer[q] + kFlagsX) + c->rank;
+  x.nsig = c->world;
+  x.sig_idx = idx;
+  x.sig_done = reinterpret_cast<unsigned*>(reinterpret_cast<uint8_t*>(c->ctl) + 64) + idx;
+  x.ep_ctr = c->ctl + 3;
+  x.status = c->ctl + 2;
+}
+
+void comm_fill_wait(r4q_comm* c, TpExchange& x, int idx, int parity, const __half* res, __half* out) {
+  x.wait_flags = reinterpret_cast<const unsigned long long*>(c->base + kFlagsX);
+  x.nwait = c->world;
+  x.wait_idx = idx;
+  x.red = reinterpret_cast<const float*>(c->base + c->off_red) + (size_t)(parity & 1) * c->world * c->red_slot;
+  x.red_slot = (long)c->red_slot;
+  x.red_res = res;
+  x.red_out = out;
+  x.ep_ctr = c->ctl + 3;
+  x.status = c->ctl + 2;
+}
+
+int comm_tick(r4q_comm* c, cudaStream_t st) {
+  tick_kernel<<<1, 1, 0, st>>>(c->ctl + 3);
+  return check_launch("tick_kernel");
+}
+
+int comm_reduce_residual(r4q_comm* c, int idx, int parity, const __half* res, __half* out, float* ss_out,
+                         int B, int D, cudaStream_t st) {
   if (!c->opened) return set_error(R4Q_ERR_ARG, "comm: peers not opened");
   if (B > c->max_batch || D != c->hidden || D % 16)
     return set_error(R4Q_ERR_CAPACITY, "comm reduce: B=%d D=%d exceeds the comm (%d, %d)", B, D,
@@ -221,19 +268,19 @@ int comm_reduce_residual(r4q_comm* c, int parity, const __half* res, __half* out
   const long n = (long)B * D;
   const int thr = 256;
   const int grid = (int)((n / 4 + thr - 1) / thr);
-  reduce_residual_kernel<<<grid, thr, 0, st>>>(sync_args(c), red, (long)c->red_slot, res, out, ss_out,
-                                                B, D);
+  reduce_residual_kernel<<<grid, thr, 0, st>>>(sync_args(c, kFlagsX, idx, true), red, (long)c->red_slot,
+                                                res, out, ss_out, B, D);
   return check_launch("reduce_residual_kernel");
 }
 
-int comm_gather_logits(r4q_comm* c, __half* logits, int B, cudaStream_t st) {
+int comm_gather_logits(r4q_comm* c, int idx, __half* logits, int B, cudaStream_t st) {
   if (!c->opened) return set_error(R4Q_ERR_ARG, "comm: peers not opened");
   if (B > c->max_batch) return set_error(R4Q_ERR_CAPACITY, "comm gather: B=%d > %d", B, c->max_batch);
   const long n = (long)B * c->vocab;
   int grid = (int)((n / 4 + 255) / 256);
   if (grid > 4 * num_sms()) grid = 4 * num_sms();
-  gather_kernel<<<grid, 256, 0, st>>>(sync_args(c), reinterpret_cast<const float*>(c->base + c->off_gat),
-                                      logits, n);
+  gather_kernel<<<grid, 256, 0, st>>>(sync_args(c, kFlagsX, idx, true),
+                                      reinterpret_cast<const float*>(c->base + c->off_gat), logits, n);
   return check_launch("gather_kernel");
 }
 
@@ -263,8 +310,8 @@ extern "C" int r4q_comm_create(int rank, int world, int max_batch, int hidden, i
   c->bytes = c->off_sa + 2 * world * c->sa_slot * 4 + 256;
   cudaError_t e = cudaMalloc(&c->base, c->bytes);
   if (e == cudaSuccess) e = cudaMemset(c->base, 0, c->bytes);
-  if (e == cudaSuccess) e = cudaMalloc(&c->ctl, 256);
-  if (e == cudaSuccess) e = cudaMemset(c->ctl, 0, 256);
+  if (e == cudaSuccess) e = cudaMalloc(&c->ctl, 64 + 4 * kTpExchangesPerStep);
+  if (e == cudaSuccess) e = cudaMemset(c->ctl, 0, 64 + 4 * kTpExchangesPerStep);
   cudaIpcMemHandle_t h;
   if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, c->base);
   if (e == cudaSuccess) e = cudaDeviceSynchronize();
@@ -345,7 +392,7 @@ extern "C" int r4q_comm_allreduce_f32(r4q_comm* c, const float* x, float* y, lon
   int rc = check_launch("push_kernel");
   if (rc) return rc;
   const float* sa = reinterpret_cast<const float*>(c->base + c->off_sa) + (size_t)par * c->world * c->sa_slot;
-  sum_kernel<<<grid, 256, 0, st>>>(sync_args(c), sa, (long)c->sa_slot, y, n);
+  sum_kernel<<<grid, 256, 0, st>>>(sync_args(c, kFlagsSA, 0, false), sa, (long)c->sa_slot, y, n);
   return check_launch("sum_kernel");
 }
 

@@ -16,6 +16,7 @@
 #include <cuda_runtime.h>
 
 #include "../../include/r4q.h"
+#include "tp_exchange.cuh"
 
 namespace r4q {
 
@@ -30,11 +31,21 @@ int comm_vocab(const r4q_comm* c);
 int comm_max_batch(const r4q_comm* c);
 int comm_hidden(const r4q_comm* c);
 
-// out[b, d] = fp16(fp16(sum_src red[parity][src][b, d]) + res[b, d]) (res may
-// alias out), ss_out[d/16][b] = sum of squares of the unrounded values.
-int comm_reduce_residual(r4q_comm* c, int parity, const __half* res, __half* out, float* ss_out,
+// Decode-step exchanges use static epochs (step counter * 256 + index + 1);
+// the producer GEMVs signal (comm_fill_signal), consumers wait.
+void comm_fill_signal(r4q_comm* c, TpExchange& x, int idx);
+// Consumer GEMV prologue: wait for exchange idx, read reduce slots of `parity`,
+// r = fp16(fp16(sum) + res) (res [B][hidden]); CTA 0 stores r to out.
+void comm_fill_wait(r4q_comm* c, TpExchange& x, int idx, int parity, const __half* res, __half* out);
+// Advance the step counter (once at the start of every decode step).
+int comm_tick(r4q_comm* c, cudaStream_t st);
+// Stand-alone consumer of exchange idx: out[b, d] = fp16(fp16(sum_src
+// red[parity][src][b, d]) + res[b, d]) (res may alias out), ss_out[d/16][b] =
+// sum of squares of the unrounded values.
+int comm_reduce_residual(r4q_comm* c, int idx, int parity, const __half* res, __half* out, float* ss_out,
                          int B, int D, cudaStream_t st);
-// logits[b, v] = fp16(gat[b, v]) once every rank has pushed its vocabulary slice.
-int comm_gather_logits(r4q_comm* c, __half* logits, int B, cudaStream_t st);
+// logits[b, v] = fp16(gat[b, v]) once exchange idx (every rank's vocabulary
+// slice) has arrived.
+int comm_gather_logits(r4q_comm* c, int idx, __half* logits, int B, cudaStream_t st);
 
 }  // namespace r4q

@@ -17,6 +17,7 @@
 // (positions come from a device scalar, so one graph serves every token) and
 // replayed.
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <vector>
 
@@ -40,6 +41,7 @@ struct r4q_decode_ctx {
   // graph cache
   cudaStream_t cap_stream;
   cudaGraphExec_t graph[2];  // [without lm_head, with lm_head]
+  unsigned long long* tp_trace;  // R4Q_TP_TRACE: exchange timeline u64 [6][256]
 };
 
 namespace r4q {
@@ -55,7 +57,7 @@ __global__ void set_positions(long long* pos, long long* seq, int B, int p) {
 static int gemv_call(r4q_decode_ctx* c, int fmt, const void* w, const void* s, const void* x, void* y,
                      int N, int K, int prologue, const void* norm_w, const float* ss_in, int ss_parts,
                      const void* res, float* ss_out, cudaStream_t st, float* const* push = nullptr,
-                     int npush = 0, long ld_push = 0) {
+                     int npush = 0, long ld_push = 0, const TpExchange* tpx = nullptr) {
   GemvArgs a{};
   a.x = x;
   a.ldx = (prologue == R4Q_PRO_SILU_FWHT) ? 2L * K : K;
@@ -82,7 +84,20 @@ static int gemv_call(r4q_decode_ctx* c, int fmt, const void* w, const void* s, c
     for (int q = 0; q < npush; ++q) a.y32p[q] = push[q];
     a.ldy = ld_push;
   }
+  if (tpx) {
+    a.tpx = *tpx;
+    a.tpx.trace = c->tp_trace;
+
+  }
   return launch_gemv(a, fmt);
+}
+
+static bool getenv_ldg() {
+  static const bool v = [] {
+    const char* e = getenv("R4Q_GEMV_PATH");
+    return e && e[0] == 'l';
+  }();
+  return v;
 }
 
 // Push targets of this rank's slot in every rank's all-reduce buffer.
@@ -96,14 +111,105 @@ static PushSet push_slots(r4q_decode_ctx* c, int parity) {
   return s;
 }
 
-static int enqueue_step(r4q_decode_ctx* c, bool with_logits, cudaStream_t st) {
+// One rank of a tensor-parallel step.  Exchange 2*li is layer li's o_proj,
+// 2*li + 1 its down_proj (reduce slots of parity idx & 1), 2*L the lm_head
+// vocabulary gather.  Producers push fp32 partials into every rank's slot and
+// signal; the next GEMV (gate_up / next qkv / lm_head) waits and reduces in
+// its RMSNorm+FWHT prologue, its CTA 0 storing the residual stream.  When
+// that GEMV cannot take the TMA path, a reduce kernel materialises r and its
+// sums of squares and the GEMV normalises from those.
+static int consume(r4q_decode_ctx* c, int idx, const __half* res, __half* out, float* ss, int fmt,
+                   const void* w, const void* s, void* y, int N, const void* norm_w, cudaStream_t st,
+                   float* const* push = nullptr, int npush = 0, long ld_push = 0, int sig_idx = -1) {
+  const r4q_model_desc& m = c->m;
+  const int D = m.hidden;
+  GemvArgs probe{};
+  probe.K = D; probe.N = N; probe.B = m.batch; probe.w = w; probe.s = s;
+  const bool fused = gemv_tma_supported(probe, fmt) && !getenv_ldg();
+  TpExchange x{};
+  int rc = 0;
+  if (fused) {
+    comm_fill_wait(m.comm, x, idx, idx & 1, res, out);
+  } else {
+    rc = comm_reduce_residual(m.comm, idx, idx & 1, res, out, ss, m.batch, D, st);
+    if (rc) return rc;
+  }
+  if (sig_idx >= 0) comm_fill_signal(m.comm, x, sig_idx);
+  // x = out (fallback: the materialised r; fused: a valid dummy, the prologue
+  // reads the exchange buffer)
+  return gemv_call(c, fmt, w, s, fused ? res : out, y, N, D, R4Q_PRO_RMSNORM_FWHT, norm_w,
+                   fused ? nullptr : ss, D / 16, nullptr, nullptr, st, push, npush, ld_push, &x);
+}
+
+static int enqueue_step_tp(r4q_decode_ctx* c, bool with_logits, cudaStream_t st) {
   const r4q_model_desc& m = c->m;
   const int B = m.batch, D = m.hidden, I = m.intermediate, H = m.num_heads, Hk = m.num_kv_heads,
             hd = m.head_dim;
   const int qd = H * hd, kvd = Hk * hd, qkv_n = qd + 2 * kvd;
   const int L = m.num_layers;
-  const bool tp = m.tp_size > 1;
-  int par = 0;  // exchange-buffer parity: 2 exchanges per layer, every step starts at 0
+  int rc = comm_tick(m.comm, st);
+  for (int li = 0; li < L && !rc; ++li) {
+    const r4q_layer_desc& ly = c->layers[li];
+    const int xo = 2 * li, xd = 2 * li + 1;
+    // 1. qkv: layer 0 from the input; later layers consume the previous down exchange
+    if (li == 0)
+      rc = gemv_call(c, ly.qkv_fmt, ly.qkv_w, ly.qkv_s, c->h_in, c->qkv, qkv_n, D, R4Q_PRO_RMSNORM_FWHT,
+                     ly.in_norm, nullptr, 0, nullptr, nullptr, st);
+    else
+      rc = consume(c, xd - 2, c->r, c->h, c->ss_h, ly.qkv_fmt, ly.qkv_w, ly.qkv_s, c->qkv, qkv_n,
+                   ly.in_norm, st);
+    if (rc) break;
+    const __half* hin = (li == 0) ? c->h_in : c->h;
+    rc = r4q_head_norm_rope(c->qkv, c->qkv + qd, c->qkv + qd + kvd, ly.q_norm, ly.k_norm, m.rope_cos,
+                            m.rope_sin, m.rope_stride, 0, c->pos_dev, c->qkv, c->qkv + qd, ly.k_cache,
+                            ly.v_cache, ly.k_scale, ly.v_scale, B, H, Hk, hd, qkv_n, qkv_n,
+                            m.max_seq, m.rms_eps, R4Q_HEAD_NORM | R4Q_HEAD_ROPE | R4Q_HEAD_KV, st);
+    if (rc) break;
+    rc = r4q_flash_decode(c->qkv, qkv_n, ly.k_cache, ly.v_cache, ly.k_scale, ly.v_scale, c->attn, qd,
+                          B, H, Hk, hd, m.max_seq, 0, c->seq_dev, R4Q_ATTN_FWHT, c->attn_ws,
+                          c->attn_ws_bytes, st);
+    if (rc) break;
+    // 4. o_proj over this rank's heads -> pushed + signalled (exchange xo)
+    {
+      TpExchange x{};
+      comm_fill_signal(m.comm, x, xo);
+      rc = gemv_call(c, ly.o_fmt, ly.o_w, ly.o_s, c->attn, nullptr, D, qd, R4Q_PRO_NONE, nullptr, nullptr,
+                     0, nullptr, nullptr, st, push_slots(c, xo & 1), m.tp_size, D, &x);
+    }
+    if (rc) break;
+    // 5. gate_up consumes exchange xo: r = o + h
+    rc = consume(c, xo, hin, c->r, c->ss_post, ly.gate_up_fmt, ly.gate_up_w, ly.gate_up_s, c->gu, 2 * I,
+                 ly.post_norm, st);
+    if (rc) break;
+    // 6. down over this rank's intermediate slice -> pushed + signalled (xd)
+    {
+      TpExchange x{};
+      comm_fill_signal(m.comm, x, xd);
+      rc = gemv_call(c, ly.down_fmt, ly.down_w, ly.down_s, c->gu, nullptr, D, I, R4Q_PRO_SILU_FWHT,
+                     nullptr, nullptr, 0, nullptr, nullptr, st, push_slots(c, xd & 1), m.tp_size, D, &x);
+    }
+  }
+  if (rc) return rc;
+  const int xl = 2 * L - 1;
+  if (!with_logits)  // final hidden h = down + r
+    return comm_reduce_residual(m.comm, xl, xl & 1, c->r, c->h, nullptr, B, D, st);
+  // lm_head: consumes the last down exchange (writes h), pushes its vocabulary
+  // slice into every rank's gather buffer, signals exchange 2L
+  float* gp[8];
+  for (int q = 0; q < m.tp_size; ++q) gp[q] = comm_gather_base(m.comm, q) + (long)m.tp_rank * m.lm_n;
+  rc = consume(c, xl, c->r, c->h, c->ss_h, m.lm_fmt, m.lm_w, m.lm_s, nullptr, m.lm_n, m.final_norm, st, gp,
+               m.tp_size, (long)m.lm_n * m.tp_size, 2 * L);
+  if (rc) return rc;
+  return comm_gather_logits(m.comm, 2 * L, c->logits, B, st);
+}
+
+static int enqueue_step(r4q_decode_ctx* c, bool with_logits, cudaStream_t st) {
+  if (c->m.tp_size > 1) return enqueue_step_tp(c, with_logits, st);
+  const r4q_model_desc& m = c->m;
+  const int B = m.batch, D = m.hidden, I = m.intermediate, H = m.num_heads, Hk = m.num_kv_heads,
+            hd = m.head_dim;
+  const int qd = H * hd, kvd = Hk * hd, qkv_n = qd + 2 * kvd;
+  const int L = m.num_layers;
   int rc = 0;
   for (int li = 0; li < L && !rc; ++li) {
     const r4q_layer_desc& ly = c->layers[li];
@@ -124,44 +230,20 @@ static int enqueue_step(r4q_decode_ctx* c, bool with_logits, cudaStream_t st) {
                           c->attn_ws_bytes, st);
     if (rc) break;
     // 4. o_proj + residual -> r, sums of squares for the post-attention norm
-    if (tp) {
-      // partial over this rank's heads, pushed to every rank; reduce + residual
-      rc = gemv_call(c, ly.o_fmt, ly.o_w, ly.o_s, c->attn, nullptr, D, qd, R4Q_PRO_NONE, nullptr,
-                     nullptr, 0, nullptr, nullptr, st, push_slots(c, par), m.tp_size, D);
-      if (!rc) rc = comm_reduce_residual(m.comm, par, hin, c->r, c->ss_post, B, D, st);
-      par ^= 1;
-    } else {
-      rc = gemv_call(c, ly.o_fmt, ly.o_w, ly.o_s, c->attn, c->r, D, qd, R4Q_PRO_NONE, nullptr, nullptr,
-                     0, hin, c->ss_post, st);
-    }
+    rc = gemv_call(c, ly.o_fmt, ly.o_w, ly.o_s, c->attn, c->r, D, qd, R4Q_PRO_NONE, nullptr, nullptr, 0,
+                   hin, c->ss_post, st);
     if (rc) break;
     // 5. gate_up with RMSNorm + FWHT of r
     rc = gemv_call(c, ly.gate_up_fmt, ly.gate_up_w, ly.gate_up_s, c->r, c->gu, 2 * I, D,
                    R4Q_PRO_RMSNORM_FWHT, ly.post_norm, c->ss_post, D / 16, nullptr, nullptr, st);
     if (rc) break;
     // 6. down with SiLU*up + FWHT, + residual r -> h, sums of squares for the next norm
-    if (tp) {
-      rc = gemv_call(c, ly.down_fmt, ly.down_w, ly.down_s, c->gu, nullptr, D, I, R4Q_PRO_SILU_FWHT,
-                     nullptr, nullptr, 0, nullptr, nullptr, st, push_slots(c, par), m.tp_size, D);
-      if (!rc) rc = comm_reduce_residual(m.comm, par, c->r, c->h, c->ss_h, B, D, st);
-      par ^= 1;
-    } else {
-      rc = gemv_call(c, ly.down_fmt, ly.down_w, ly.down_s, c->gu, c->h, D, I, R4Q_PRO_SILU_FWHT, nullptr,
-                     nullptr, 0, c->r, c->ss_h, st);
-    }
+    rc = gemv_call(c, ly.down_fmt, ly.down_w, ly.down_s, c->gu, c->h, D, I, R4Q_PRO_SILU_FWHT, nullptr,
+                   nullptr, 0, c->r, c->ss_h, st);
   }
   if (rc || !with_logits) return rc;
-  const __half* hl = L > 0 ? c->h : c->h_in;
-  if (!tp)
-    return gemv_call(c, m.lm_fmt, m.lm_w, m.lm_s, hl, c->logits, m.lm_n, D, R4Q_PRO_RMSNORM_FWHT,
-                     m.final_norm, nullptr, 0, nullptr, nullptr, st);
-  // vocabulary slice of this rank pushed into every rank's gather buffer
-  float* gp[8];
-  for (int q = 0; q < m.tp_size; ++q) gp[q] = comm_gather_base(m.comm, q) + (long)m.tp_rank * m.lm_n;
-  rc = gemv_call(c, m.lm_fmt, m.lm_w, m.lm_s, hl, nullptr, m.lm_n, D, R4Q_PRO_RMSNORM_FWHT, m.final_norm,
-                 nullptr, 0, nullptr, nullptr, st, gp, m.tp_size, (long)m.lm_n * m.tp_size);
-  if (rc) return rc;
-  return comm_gather_logits(m.comm, c->logits, B, st);
+  return gemv_call(c, m.lm_fmt, m.lm_w, m.lm_s, L > 0 ? c->h : c->h_in, c->logits, m.lm_n, D,
+                   R4Q_PRO_RMSNORM_FWHT, m.final_norm, nullptr, 0, nullptr, nullptr, st);
 }
 
 static void free_ctx(r4q_decode_ctx* c) {
@@ -169,7 +251,7 @@ static void free_ctx(r4q_decode_ctx* c) {
     if (c->graph[i]) cudaGraphExecDestroy(c->graph[i]);
   if (c->cap_stream) cudaStreamDestroy(c->cap_stream);
   void* bufs[] = {c->h_in, c->h, c->r, c->qkv, c->attn, c->gu, c->logits, c->h_out, c->ss_post,
-                  c->ss_h, c->pos_dev, c->seq_dev, c->gemv_ws, c->attn_ws};
+                  c->ss_h, c->pos_dev, c->seq_dev, c->gemv_ws, c->attn_ws, c->tp_trace};
   for (void* b : bufs)
     if (b) cudaFree(b);
   delete c;
@@ -194,7 +276,7 @@ extern "C" int r4q_decode_ctx_create(const r4q_model_desc* md, const r4q_layer_d
         comm_rank(m.comm) != m.tp_rank)
       return set_error(R4Q_ERR_ARG, "decode_ctx_create: tp_size %d / tp_rank %d do not match the comm",
                        m.tp_size, m.tp_rank);
-    if (m.num_layers < 1 || m.batch > comm_max_batch(m.comm) || m.hidden != comm_hidden(m.comm) ||
+    if (m.num_layers < 1 || 2 * m.num_layers + 1 > kTpExchangesPerStep || m.batch > comm_max_batch(m.comm) || m.hidden != comm_hidden(m.comm) ||
         (m.lm_w && (long)m.lm_n * tps != comm_vocab(m.comm)))
       return set_error(R4Q_ERR_ARG, "decode_ctx_create: comm sized for B %d D %d V %d",
                        comm_max_batch(m.comm), comm_hidden(m.comm), comm_vocab(m.comm));
@@ -228,6 +310,13 @@ extern "C" int r4q_decode_ctx_create(const r4q_model_desc* md, const r4q_layer_d
     if (e != cudaSuccess) {
       free_ctx(c);
       return set_error(R4Q_ERR_CUDA, "decode_ctx_create: %s", cudaGetErrorString(e));
+    }
+  }
+  if (tps > 1 && getenv("R4Q_TP_TRACE")) {
+    if (cudaMalloc(&c->tp_trace, 6 * kTpExchangesPerStep * 8) != cudaSuccess ||
+        cudaMemset(c->tp_trace, 0, 6 * kTpExchangesPerStep * 8) != cudaSuccess) {
+      free_ctx(c);
+      return set_error(R4Q_ERR_CUDA, "decode_ctx_create: trace buffer");
     }
   }
   cudaError_t e = cudaStreamCreateWithFlags(&c->cap_stream, cudaStreamNonBlocking);
@@ -308,4 +397,11 @@ extern "C" int r4q_decode_step(r4q_decode_ctx* c, const void* hidden_in, int pos
     if (e != cudaSuccess) return set_error(R4Q_ERR_CUDA, "decode_step: copy logits: %s", cudaGetErrorString(e));
   }
   return R4Q_OK;
+}
+
+extern "C" int r4q_decode_tp_trace(r4q_decode_ctx* c, unsigned long long* host) {
+  if (!c || !host) return set_error(R4Q_ERR_ARG, "decode_tp_trace: null argument");
+  if (!c->tp_trace) return set_error(R4Q_ERR_ARG, "decode_tp_trace: context built without R4Q_TP_TRACE");
+  cudaError_t e = cudaMemcpy(host, c->tp_trace, 6 * kTpExchangesPerStep * 8, cudaMemcpyDeviceToHost);
+  return e == cudaSuccess ? R4Q_OK : set_error(R4Q_ERR_CUDA, "decode_tp_trace: %s", cudaGetErrorString(e));
 }

@@ -58,6 +58,14 @@ __device__ __forceinline__ void load_chunk(const GemvParams& p, int row, int chu
 }
 
 // --------------------------------------------------------------- kernel ---
+// CTA exit of a tensor-parallel producer: the last CTA signals every rank
+// (called by all threads of the CTA; tp_signal_cta fences at system scope).
+__device__ __forceinline__ void tp_exit(const GemvParams& p) {
+  if (!p.tpx.nsig) return;
+  __syncthreads();
+  if (threadIdx.x == 0) tp_signal_cta(p.tpx);
+}
+
 template <int FMT, int NG>
 __global__ void __launch_bounds__(kThreads) gemv_kernel(const GemvParams p) {
   using F = Fmt<FMT>;
@@ -252,8 +260,11 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const GemvParams p) {
       }
     }
   }
-  if (p.npush > 1) __threadfence_system();  // peer outputs complete before exit
-  if (p.ksplit == 1) return;
+  if (p.npush > 1 && !p.tpx.nsig) __threadfence_system();  // peer outputs complete before exit
+  if (p.ksplit == 1) {
+    tp_exit(p);
+    return;
+  }
 
   // ---- split-K fixup: the last CTA of this row tile sums partials in order ----
   __threadfence();
@@ -263,7 +274,10 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const GemvParams p) {
     s_last = (old == (unsigned)p.ksplit - 1) ? 1u : 0u;
   }
   __syncthreads();
-  if (!s_last) return;
+  if (!s_last) {
+    tp_exit(p);
+    return;
+  }
   __threadfence();
   const int trow0 = blockIdx.x * p.mt * 16;
   const int tiles16 = min(p.mt, (p.N - trow0) >> 4);
@@ -286,7 +300,8 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const GemvParams p) {
     if (p.ss_out && lane == 0) p.ss_out[(long)((trow0 >> 4) + ti) * p.B + col] = sq;
   }
   if (tid == 0) p.cnt[blockIdx.x] = 0u;  // leave the workspace zeroed for the next launch
-  if (p.npush > 1) __threadfence_system();
+  if (p.npush > 1 && !p.tpx.nsig) __threadfence_system();
+  tp_exit(p);
 }
 
 // ------------------------------------------------------------- planning ---
@@ -379,6 +394,7 @@ static int launch_gemv_t(const GemvArgs& a) {
   p.ss_out = a.ss_out;
   p.npush = a.npush;
   for (int q = 0; q < 8; ++q) p.y32p[q] = q < a.npush ? a.y32p[q] : nullptr;
+  p.tpx = a.tpx;
   p.cnt = reinterpret_cast<unsigned*>(a.ws);
   p.part = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(a.ws) + gemv_cnt_bytes(a.N));
   if (pl.ksplit > 1 && a.ws == nullptr)
@@ -436,6 +452,8 @@ int launch_gemv(const GemvArgs& a, int fmt) {
     st = launch_gemv_tma(a, fmt);
     if (st != R4Q_ERR_CAPACITY) return st;  // no TMA plan fits: take the LDG kernel
   }
+  if (a.tpx.nwait)
+    return set_error(R4Q_ERR_ARG, "gemv: the tensor-parallel reduce prologue needs the TMA path");
   const bool two = a.B > 8;
   switch (fmt) {
     case W_INT4: return two ? launch_gemv_t<W_INT4, 2>(a) : launch_gemv_t<W_INT4, 1>(a);

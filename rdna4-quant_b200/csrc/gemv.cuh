@@ -3,6 +3,8 @@
 #include <cuda_runtime.h>
 #include <stddef.h>
 
+#include "tp_exchange.cuh"
+
 namespace r4q {
 
 enum WFmt { W_INT4 = 0, W_INT8 = 1, W_FP16 = 2 };
@@ -30,6 +32,8 @@ struct GemvArgs {
   // fp32 sums to npush arrays (local or peer memory) instead of fp16 y
   float* y32p[8];
   int npush;
+  // tensor-parallel exchange: signal after the pushes / reduce-on-read prologue
+  TpExchange tpx;
 };
 
 size_t gemv_cnt_bytes(int N);

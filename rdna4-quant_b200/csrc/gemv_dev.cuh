@@ -40,7 +40,30 @@ struct GemvParams {
   // straight into the peers' reduce buffers)
   float* y32p[8];
   int npush;
+  TpExchange tpx;  // tensor-parallel exchange (zero outside TP)
 };
+
+// Tensor-parallel consumer input: 8 fp16 values r = fp16(fp16(sum over src of
+// the fp32 partials) + residual) of row `col`, elements k..k+7 (K = hidden).
+__device__ __forceinline__ uint4 tp_row8(const GemvParams& p, int col, int k) {
+  const float* rb = p.tpx.red + (long)col * p.K + k;
+  float4 a0 = __ldcg(reinterpret_cast<const float4*>(rb));
+  float4 a1 = __ldcg(reinterpret_cast<const float4*>(rb + 4));
+  for (int s = 1; s < p.tpx.nwait; ++s) {
+    const float4 b0 = __ldcg(reinterpret_cast<const float4*>(rb + s * p.tpx.red_slot));
+    const float4 b1 = __ldcg(reinterpret_cast<const float4*>(rb + s * p.tpx.red_slot + 4));
+    a0.x += b0.x; a0.y += b0.y; a0.z += b0.z; a0.w += b0.w;
+    a1.x += b1.x; a1.y += b1.y; a1.z += b1.z; a1.w += b1.w;
+  }
+  const uint4 rr = *reinterpret_cast<const uint4*>(p.tpx.red_res + (long)col * p.K + k);
+  const __half* hr = reinterpret_cast<const __half*>(&rr);
+  const float a[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+  uint4 out;
+  __half* ho = reinterpret_cast<__half*>(&out);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) ho[j] = __float2half(__half2float(__float2half(a[j])) + __half2float(hr[j]));
+  return out;
+}
 
 __host__ __device__ inline int steps_total(int K, int ck, int u) {
   const int nch = K / ck;
@@ -266,7 +289,7 @@ __device__ __forceinline__ void stage_quad(const GemvParams& p, int col, int k0,
   } else {
     float f[8];
     if (in) {
-      const uint4 raw = *reinterpret_cast<const uint4*>(xr);
+      const uint4 raw = p.tpx.nwait ? tp_row8(p, col, k0 + 8 * q) : *reinterpret_cast<const uint4*>(xr);
       const __half* h = reinterpret_cast<const __half*>(&raw);
       if (p.prologue == R4Q_PRO_SILU_FWHT) {
         const uint4 ru = *reinterpret_cast<const uint4*>(xr + p.K);

@@ -225,6 +225,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
   SegIter iter0{tp.tiles, tp.gt, cta_in_split, st0, st1, ks, S};
 
   if (tid == 0) TRACE(0, 0);
+  if (tid == 0 && blockIdx.x == 0 && p.tpx.nsig) tp_stamp(p.tpx, 5, p.tpx.sig_idx);
   if (tid == 0) {
     for (int i = 0; i < NS; ++i) {
       mbar_init(&full[i], 1);
@@ -274,7 +275,52 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
   const int nch_pad = nst * T::CPS;
   const int colstride = tp.x_bytes / (ncolx > 0 ? ncolx : 1);
 
-  if (p.prologue == R4Q_PRO_RMSNORM_FWHT) {
+  const bool stamp = blockIdx.x == 0 && ctid == 0;
+  if (stamp && p.tpx.nsig) tp_stamp(p.tpx, 0, p.tpx.sig_idx);
+  if (p.tpx.nwait) {
+    // tensor-parallel consumer: wait for every rank's partials, then r and
+    // its sum of squares straight from the exchange buffer (CTA 0 stores r)
+    if (stamp) tp_stamp(p.tpx, 2, p.tpx.wait_idx);
+    if (warp == 0) tp_wait_lane(p.tpx, lane);
+    consumer_sync();
+    if (stamp) tp_stamp(p.tpx, 3, p.tpx.wait_idx);
+    // every consumer thread takes 4 consecutive k of every column; partial
+    // sums of squares per (warp, column) meet in shared memory
+    __shared__ float s_ssp[kTmaConsumers][16];
+    for (int c = 0; c < ncolx; ++c) {
+      const float* rb = p.tpx.red + (long)c * p.K;
+      const __half* hr = p.tpx.red_res + (long)c * p.K;
+      __half* ro = (blockIdx.x == 0 && p.tpx.red_out) ? p.tpx.red_out + (long)c * p.K : nullptr;
+      float ss = 0.0f;
+      for (int k = ctid * 4; k < p.K; k += kTmaConsumers * 128) {
+        float4 a = __ldcg(reinterpret_cast<const float4*>(rb + k));
+        for (int s2 = 1; s2 < p.tpx.nwait; ++s2) {
+          const float4 b = __ldcg(reinterpret_cast<const float4*>(rb + s2 * p.tpx.red_slot + k));
+          a.x += b.x; a.y += b.y; a.z += b.z; a.w += b.w;
+        }
+        const uint2 rr = *reinterpret_cast<const uint2*>(hr + k);
+        const __half* h4 = reinterpret_cast<const __half*>(&rr);
+        const float a4[4] = {a.x, a.y, a.z, a.w};
+        __half o4[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float v = __half2float(__float2half(a4[j])) + __half2float(h4[j]);
+          ss += v * v;
+          o4[j] = __float2half(v);
+        }
+        if (ro) *reinterpret_cast<uint2*>(ro + k) = *reinterpret_cast<const uint2*>(o4);
+      }
+      ss = warp_sum(ss);
+      if (lane == 0) s_ssp[warp][c] = ss;
+    }
+    consumer_sync();
+    if (warp == 0 && lane < ncolx) {
+      float ss = 0.0f;
+      for (int w2 = 0; w2 < kTmaConsumers; ++w2) ss += s_ssp[w2][lane];
+      s_rrms[lane] = rsqrtf(ss / (float)p.K + p.eps);
+    }
+    consumer_sync();
+  } else if (p.prologue == R4Q_PRO_RMSNORM_FWHT) {
     for (int c = warp; c < ncolx; c += kTmaConsumers) {
       float ss = 0.0f;
       if (p.ss_in) {
@@ -310,6 +356,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
   }
   consumer_sync();
   if (ctid == 0) TRACE(0, 1);
+  if (stamp && p.tpx.nwait) tp_stamp(p.tpx, 4, p.tpx.wait_idx);
 
   // warp -> (k quarter, m-tile); every stage is consumed by all 16 warps
   const int g = lane >> 2, t = lane & 3;
@@ -599,8 +646,14 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
     }
     if (ctid == 0) TRACE(3, uidx);
   }
-  // outputs pushed into peer memory: complete them system-wide before exit
-  if (p.npush > 1) __threadfence_system();
+  // outputs pushed into peer memory: the last CTA signals the exchange to
+  // every rank once all CTAs' pushes are fenced at system scope
+  if (p.tpx.nsig) {
+    consumer_sync();
+    if (ctid == 0) tp_signal_cta(p.tpx);
+  } else if (p.npush > 1) {
+    __threadfence_system();
+  }
   if (ctid == 0) TRACE(0, 2);
 }
 
@@ -753,6 +806,7 @@ static int launch_tma_t(const GemvArgs& a) {
   p.ss_out = a.ss_out;
   p.npush = a.npush;
   for (int q = 0; q < 8; ++q) p.y32p[q] = q < a.npush ? a.y32p[q] : nullptr;
+  p.tpx = a.tpx;
   p.cnt = reinterpret_cast<unsigned*>(a.ws);
   p.part = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(a.ws) + gemv_cnt_bytes(a.N));
   tp.nstages = (a.K + T::SK - 1) / T::SK;

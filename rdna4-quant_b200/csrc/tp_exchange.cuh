@@ -1,0 +1,109 @@
+// Tensor-parallel exchange fused into the GEMVs (device side).
+//
+// Producer GEMV (o_proj, down_proj, lm_head under TP): its epilogue pushes the
+// fp32 partial sums into every rank's exchange buffer (GemvParams::y32p); at
+// kernel exit every CTA fences its pushes at system scope and the last CTA to
+// finish stores the exchange's epoch into flags[rank] of every rank.
+//
+// Consumer GEMV (gate_up after o_proj, the next layer's qkv or the lm_head
+// after down_proj): after griddepcontrol.wait — i.e. while its producer warp
+// already streams weights — it waits (bounded) until flags[src] >= epoch for
+// every src, then builds its RMSNorm+FWHT input straight from the exchange
+// buffer: r = fp16(fp16(sum over src in rank order) + residual), every CTA
+// computing the sum of squares itself; CTA 0 also stores r (the residual
+// stream).  The separate all-reduce kernel disappears from the step.
+//
+// Epochs are static: epoch = step_counter * 256 + exchange index + 1, where
+// the step counter (one per comm, shared by every context on it) is ticked
+// once at the start of each step, so epochs only grow and a stale flag can
+// never satisfy a wait.
+#pragma once
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+namespace r4q {
+
+constexpr int kTpMaxWorld = 8;
+constexpr int kTpExchangesPerStep = 256;
+
+struct TpExchange {
+  // producer side
+  unsigned long long* sig[kTpMaxWorld];  // &flags[rank] inside every rank's buffer
+  unsigned* sig_done;                    // CTA-completion counter of this exchange (left zero)
+  int nsig;                              // ranks to signal (0: no signal)
+  int sig_idx;
+  // consumer side
+  const unsigned long long* wait_flags;  // this rank's flags[world]
+  int nwait;                             // ranks to wait for (0: not a TP consumer)
+  int wait_idx;
+  const float* red;                      // reduce slots of this parity: [world][red_slot]
+  long red_slot;                         // floats per slot; row b of a slot at b * K
+  const __half* red_res;                 // residual added to the reduced sum ([B][K])
+  __half* red_out;                       // fp16(sum) + residual, written by CTA 0 (or null)
+  // both
+  const unsigned long long* ep_ctr;      // step counter
+  unsigned long long* status;            // timeout bits (one per rank waited for)
+  // optional timeline (R4Q_TP_TRACE): u64 [6][256] global-timer stamps per
+  // exchange index: 0 producer compute start, 1 producer signal, 2 consumer
+  // wait start, 3 consumer wait end, 4 consumer input staged, 5 producer entry
+  unsigned long long* trace;
+};
+
+#ifdef __CUDACC__
+__device__ __forceinline__ unsigned long long tp_now() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ void tp_stamp(const TpExchange& x, int ev, int idx) {
+  if (x.trace && idx >= 0 && idx < kTpExchangesPerStep) x.trace[ev * kTpExchangesPerStep + idx] = tp_now();
+}
+
+__device__ __forceinline__ unsigned long long tp_epoch(const TpExchange& x, int idx) {
+  const unsigned long long c = *reinterpret_cast<const volatile unsigned long long*>(x.ep_ctr);
+  return c * (unsigned long long)kTpExchangesPerStep + (unsigned long long)idx + 1ull;
+}
+
+// Lanes 0..nwait-1 of one warp each wait for one rank; bounded by ~2 s of
+// wall time, after which the missing rank is recorded in `status`.
+__device__ __forceinline__ void tp_wait_lane(const TpExchange& x, int lane) {
+  if (lane >= x.nwait) return;
+  const unsigned long long e = tp_epoch(x, x.wait_idx);
+  unsigned long long t0;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+  unsigned it = 0;
+  for (;;) {
+    unsigned long long v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(x.wait_flags + lane) : "memory");
+    if (v >= e) break;
+    if ((++it & 63) == 0) {
+      unsigned long long t;
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+      if (t - t0 > 2000000000ull) {
+        atomicOr(x.status, 1ull << lane);
+        break;
+      }
+    }
+    __nanosleep(32);
+  }
+}
+
+// One thread per CTA, after a CTA-wide barrier that follows every thread's
+// pushes: a system-scope fence (cumulative over the writes the barrier made
+// visible to this thread — the grid-barrier pattern at system scope), then
+// the last CTA to arrive publishes the epoch to all ranks.
+__device__ __forceinline__ void tp_signal_cta(const TpExchange& x) {
+  __threadfence_system();
+  unsigned old;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(old) : "l"(x.sig_done) : "memory");
+  if (old != gridDim.x * gridDim.y * gridDim.z - 1) return;
+  *x.sig_done = 0u;
+  const unsigned long long e = tp_epoch(x, x.sig_idx);
+  __threadfence_system();
+  for (int q = 0; q < x.nsig; ++q)
+    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(x.sig[q]), "l"(e) : "memory");
+  tp_stamp(x, 1, x.sig_idx);
+}
+#endif
+
+}  // namespace r4q

@@ -81,6 +81,7 @@ _SIGS = {
     "r4q_decode_ctx_create": (i32, [C.POINTER(ModelDesc), C.POINTER(LayerDesc), C.POINTER(C.c_void_p)]),
     "r4q_decode_ctx_destroy": (None, [vp]),
     "r4q_decode_step": (i32, [vp, vp, i32, vp, vp, i32, vp]),
+    "r4q_decode_tp_trace": (i32, [vp, vp]),
     "r4q_comm_create": (i32, [i32, i32, i32, i32, i32, i64, C.POINTER(C.c_void_p), vp]),
     "r4q_comm_open": (i32, [vp, vp]),
     "r4q_comm_status": (i32, [vp]),
