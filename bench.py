@@ -375,14 +375,13 @@ def decode_tok_s(a, dev, peak, ws=1, rank=0):
     """40-layer Qwen3-14B-shaped decode (random-init,
     80 % INT4 / 20 % INT8 groups by seed, fp16 embedding + lm_head), KV cache
     pre-filled for `ctx` prompt positions, greedy decode of `tokens` tokens,
-    each one decode step with logits (CUDA-graph replay) + argmax + embedding
-    lookup on the device.  TP=1: through int4_hip.decode_step_logits.  TP=ws>1
+    each one CUDA-graph launch of step + device argmax + embedding lookup
+    (r4q_decode_loop, the engine of int4_hip.decode_loop).  TP=ws>1
     (torchrun, one rank per GPU): each rank holds its shard (r4q.tp) and the
     step's exchanges run over NVLink peer memory (r4q_comm); time is the max
     over ranks."""
     import torch
     import torch.distributed as dist
-    import int4_hip
     from r4q import synth, tp
     cfg = synth.qwen3_14b_config()
     ctxs = [int(c) for c in a.decode_ctx.split(",") if c]
@@ -398,33 +397,29 @@ def decode_tok_s(a, dev, peak, ws=1, rank=0):
         comm = tp.Comm(rank, ws, max_batch=1, hidden=cfg['hidden'], vocab=cfg['vocab'])
         dec = tp.TPDecoder(m, cfg, comm, batch=1)
     res = []
+    from r4q import decode as rdec
     for ctx in ctxs:
         synth.fill_kv_synthetic(m, ctx, seed=ctx)
         gen = torch.Generator(device=dev).manual_seed(ctx)
         tok = torch.randint(0, cfg['vocab'], (1,), generator=gen, device=dev)
-
-        def step(pos, tok):
-            h = m['embed'][tok].reshape(1, 1, -1)
-            if dec is not None:
-                lg = dec.step(h, pos)
-            else:
-                lg = int4_hip.decode_step_logits(
-                    h, m['qkv_w'], m['qkv_s'], 0, m['o_w'], m['o_s'], 0, m['gu_w'], m['gu_s'], 0,
-                    m['down_w'], m['down_s'], 0, m['in_norm_w'], m['post_norm_w'], m['q_norm_w'],
-                    m['k_norm_w'], m['rope_cos'], m['rope_sin'], pos, cfg['num_heads'],
-                    cfg['num_kv_heads'], cfg['head_dim'], cfg['hidden'], cfg['intermediate'],
-                    cfg['rms_eps'], m['k_caches'], m['v_caches'], m['final_norm_w'], m['lm_w'],
-                    m['lm_s'], cfg['vocab'], cfg['hidden'], None)
-            return lg.reshape(-1).argmax().reshape(1)
-        for w in range(3):                         # warm-up (graph capture on the first)
-            tok = step(ctx + w, tok)
+        h0 = m['embed'][tok].reshape(1, -1).contiguous()
+        if dec is not None:
+            loop = lambda start, n: dec.loop(m['embed'], h0, start, n)
+        else:
+            c1 = rdec.get_context(
+                m['qkv_w'], m['qkv_s'], m['o_w'], m['o_s'], m['gu_w'], m['gu_s'], m['down_w'], m['down_s'],
+                m['in_norm_w'], m['post_norm_w'], m['q_norm_w'], m['k_norm_w'], m['rope_cos'], m['rope_sin'],
+                cfg['num_heads'], cfg['num_kv_heads'], cfg['head_dim'], cfg['hidden'], cfg['intermediate'],
+                cfg['rms_eps'], m['k_caches'], m['v_caches'], m['final_norm_w'], m['lm_w'], m['lm_s'],
+                cfg['vocab'], batch=1)
+            loop = lambda start, n: c1.loop(m['embed'], h0, start, n)
+        loop(ctx, 3)                                   # warm-up (graph capture)
         torch.cuda.synchronize()
         if ws > 1:
             dist.barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
-        for t in range(a.decode_tokens):
-            tok = step(ctx + t, tok)
+        toks = loop(ctx, a.decode_tokens)
         e1.record()
         torch.cuda.synchronize()
         ms = e0.elapsed_time(e1) / a.decode_tokens
@@ -448,9 +443,10 @@ def decode_tok_s(a, dev, peak, ws=1, rank=0):
     return {"model": "Qwen3-14B shape, random init", "int8_groups": int8_groups,
             "lm_head": "fp16", "batch": 1, "tokens": a.decode_tokens, "tp": ws,
             "kv": "prompt K/V pre-filled with seeded FP8 values (no prefill compute)",
-            "api": ("int4_hip.decode_step_logits per token (graph replay) + argmax + embedding"
-                    if ws == 1 else "r4q.tp.TPDecoder.step per token (graph replay, NVLink P2P "
-                    "exchanges fused into the GEMV epilogues) + argmax + embedding"),
+            "api": ("r4q decode_loop (int4_hip.decode_loop's engine): one CUDA-graph launch per token "
+                    "= step + device argmax + embedding lookup" if ws == 1 else
+                    "r4q.tp.TPDecoder.loop: one CUDA-graph launch per token per rank (NVLink P2P "
+                    "exchanges fused into the GEMVs) + device argmax + embedding lookup"),
             "results": res}
 
 

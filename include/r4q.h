@@ -219,6 +219,24 @@ void r4q_decode_ctx_destroy(r4q_decode_ctx* ctx);
 int r4q_decode_step(r4q_decode_ctx* ctx, const void* hidden_in, int pos, void* hidden_out,
                     void* logits_out, int use_graph, void* stream);
 
+/* Greedy decode of num_tokens tokens entirely on the device: token t runs the
+ * step at position start_pos + t with logits, takes the argmax (first maximum,
+ * NaN skipped) and feeds the embedding row of that token (embed fp16
+ * [vocab, hidden]) into step t + 1.  hidden_first fp16 [batch, hidden] is the
+ * first step's input.  tokens_out: device int64 [num_tokens, batch].  With
+ * use_graph each token is one CUDA-graph launch (step + argmax + embedding,
+ * captured once per context and table); no host synchronisation.  Replaces
+ * decode_loop / decode_bench / decode_bench_graph
+ * (int4_decode_step.hip:2601-2795, 2801-3041, 3284-3466). */
+int r4q_decode_loop(r4q_decode_ctx* ctx, const void* embed, const void* hidden_first, int start_pos,
+                    int num_tokens, long long* tokens_out, int use_graph, void* stream);
+
+/* One eager step with logits at `pos`, timed with events per kernel group:
+ * out5 (host) = [total, gemv, attention, norm, rest] in ms, as decode_profile
+ * (int4_decode_step.hip:3047-3281).  Synchronous.  Single-GPU contexts time
+ * every group; tensor-parallel contexts report the total (rest = total). */
+int r4q_decode_profile(r4q_decode_ctx* ctx, const void* hidden_in, int pos, float* out5, void* stream);
+
 /* Exchange timeline of a tensor-parallel context created with the environment
  * variable R4Q_TP_TRACE set (synchronous; host array of 6 x 256 u64 global-timer
  * stamps in ns, per exchange index: producer compute start, producer signal,

@@ -40,7 +40,18 @@ struct r4q_decode_ctx {
   size_t attn_ws_bytes;
   // graph cache
   cudaStream_t cap_stream;
-  cudaGraphExec_t graph[2];  // [without lm_head, with lm_head]
+  cudaGraphExec_t graph[3];  // [without lm_head, with lm_head, greedy token (+ argmax, embedding)]
+  // greedy loop state
+  long long* tok_hist;       // [B][max_seq] token chosen at each position
+  void* am_ws;               // argmax partials [B][kArgmaxBlocks] + counters
+  const void* loop_embed;    // embedding table the token graph was captured with
+  // decode_profile: events around kernel groups (cat 0 gemv, 1 attention, 2 norm)
+  struct ProfEv {
+    cudaEvent_t a, b;
+    int cat;
+  };
+  bool prof;
+  std::vector<ProfEv> prof_ev;
   unsigned long long* tp_trace;  // R4Q_TP_TRACE: exchange timeline u64 [6][256]
 };
 
@@ -90,6 +101,105 @@ static int gemv_call(r4q_decode_ctx* c, int fmt, const void* w, const void* s, c
 
   }
   return launch_gemv(a, fmt);
+}
+
+// decode_profile: events around one kernel group when the context profiles
+struct ProfScope {
+  r4q_decode_ctx* c;
+  cudaStream_t st;
+  cudaEvent_t a = nullptr;
+  int cat;
+  ProfScope(r4q_decode_ctx* c_, int cat_, cudaStream_t st_) : c(c_), st(st_), cat(cat_) {
+    if (!c->prof) return;
+    cudaEventCreate(&a);
+    cudaEventRecord(a, st);
+  }
+  ~ProfScope() {
+    if (!a) return;
+    cudaEvent_t b;
+    cudaEventCreate(&b);
+    cudaEventRecord(b, st);
+    c->prof_ev.push_back({a, b, cat});
+  }
+};
+
+// ------------------------------------------------------------ greedy loop
+// argmax over fp16 logits [B][V] (first index of the maximum, NaN skipped —
+// torch.argmax on the logits the reference's decode_loop takes), then the
+// embedding row of the chosen token becomes the next step's input.
+constexpr int kArgmaxBlocks = 64;
+
+__device__ __forceinline__ bool am_better(float v, int i, float bv, int bi) {
+  return v > bv || (v == bv && i < bi);
+}
+
+__global__ void argmax_kernel(const __half* __restrict__ logits, int V, float2* part, unsigned* cnt,
+                              long long* tok_hist, int max_seq, const long long* pos_dev) {
+  const int b = blockIdx.y;
+  const __half* lr = logits + (long)b * V;
+  const int per = (V + gridDim.x - 1) / gridDim.x;
+  const int lo = blockIdx.x * per, hi = min(V, lo + per);
+  float bv = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int i = lo + threadIdx.x; i < hi; i += blockDim.x) {
+    const float v = __half2float(lr[i]);
+    if (v == v && am_better(v, i, bv, bi)) {
+      bv = v;
+      bi = i;
+    }
+  }
+  for (int o = 16; o; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (am_better(ov, oi, bv, bi)) {
+      bv = ov;
+      bi = oi;
+    }
+  }
+  __shared__ float sv[32];
+  __shared__ int si[32];
+  __shared__ bool s_last;
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  if (l == 0) {
+    sv[w] = bv;
+    si[w] = bi;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int k = 1; k < (int)(blockDim.x >> 5); ++k)
+      if (am_better(sv[k], si[k], bv, bi)) {
+        bv = sv[k];
+        bi = si[k];
+      }
+    part[b * gridDim.x + blockIdx.x] = make_float2(bv, __int_as_float(bi));
+    __threadfence();
+    s_last = atomicAdd(&cnt[b], 1u) == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (!s_last || threadIdx.x != 0) return;
+  __threadfence();
+  float gv = -INFINITY;
+  int gi = 0x7fffffff;
+  for (int k = 0; k < (int)gridDim.x; ++k) {
+    const float2 pk = __ldcg(&part[b * gridDim.x + k]);
+    if (am_better(pk.x, __float_as_int(pk.y), gv, gi)) {
+      gv = pk.x;
+      gi = __float_as_int(pk.y);
+    }
+  }
+  if (gi == 0x7fffffff) gi = 0;  // every logit NaN
+  const long long pos = pos_dev[b];
+  tok_hist[(long)b * max_seq + pos] = gi;
+  cnt[b] = 0u;
+}
+
+__global__ void embed_kernel(const __half* __restrict__ embed, int D, const long long* tok_hist, int max_seq,
+                             const long long* pos_dev, __half* __restrict__ h) {
+  const int b = blockIdx.x;
+  const long long tok = tok_hist[(long)b * max_seq + pos_dev[b]];
+  const uint4* src = reinterpret_cast<const uint4*>(embed + tok * D);
+  uint4* dst = reinterpret_cast<uint4*>(h + (long)b * D);
+  for (int i = threadIdx.x; i < D / 8; i += blockDim.x) dst[i] = src[i];
 }
 
 static bool getenv_ldg() {
@@ -215,20 +325,30 @@ static int enqueue_step(r4q_decode_ctx* c, bool with_logits, cudaStream_t st) {
     const r4q_layer_desc& ly = c->layers[li];
     const __half* hin = (li == 0) ? c->h_in : c->h;
     // 1. qkv projection, RMSNorm + FWHT prologue
+    {
+    ProfScope ps(c, 0, st);
     rc = gemv_call(c, ly.qkv_fmt, ly.qkv_w, ly.qkv_s, hin, c->qkv, qkv_n, D, R4Q_PRO_RMSNORM_FWHT,
                    ly.in_norm, li == 0 ? nullptr : c->ss_h, D / 16, nullptr, nullptr, st);
+    }
     if (rc) break;
     // 2. QK norm + RoPE in place, K/V to the FP8 cache
+    {
+    ProfScope ps(c, 2, st);
     rc = r4q_head_norm_rope(c->qkv, c->qkv + qd, c->qkv + qd + kvd, ly.q_norm, ly.k_norm, m.rope_cos,
                             m.rope_sin, m.rope_stride, 0, c->pos_dev, c->qkv, c->qkv + qd, ly.k_cache,
                             ly.v_cache, ly.k_scale, ly.v_scale, B, H, Hk, hd, qkv_n, qkv_n,
                             m.max_seq, m.rms_eps, R4Q_HEAD_NORM | R4Q_HEAD_ROPE | R4Q_HEAD_KV, st);
+    }
     if (rc) break;
     // 3. attention over [0, pos], FWHT on the output (feeds o_proj)
+    {
+    ProfScope ps(c, 1, st);
     rc = r4q_flash_decode(c->qkv, qkv_n, ly.k_cache, ly.v_cache, ly.k_scale, ly.v_scale, c->attn, qd,
                           B, H, Hk, hd, m.max_seq, 0, c->seq_dev, R4Q_ATTN_FWHT, c->attn_ws,
                           c->attn_ws_bytes, st);
+    }
     if (rc) break;
+    ProfScope ps(c, 0, st);  // o, gate_up, down
     // 4. o_proj + residual -> r, sums of squares for the post-attention norm
     rc = gemv_call(c, ly.o_fmt, ly.o_w, ly.o_s, c->attn, c->r, D, qd, R4Q_PRO_NONE, nullptr, nullptr, 0,
                    hin, c->ss_post, st);
@@ -247,11 +367,12 @@ static int enqueue_step(r4q_decode_ctx* c, bool with_logits, cudaStream_t st) {
 }
 
 static void free_ctx(r4q_decode_ctx* c) {
-  for (int i = 0; i < 2; ++i)
+  for (int i = 0; i < 3; ++i)
     if (c->graph[i]) cudaGraphExecDestroy(c->graph[i]);
   if (c->cap_stream) cudaStreamDestroy(c->cap_stream);
   void* bufs[] = {c->h_in, c->h, c->r, c->qkv, c->attn, c->gu, c->logits, c->h_out, c->ss_post,
-                  c->ss_h, c->pos_dev, c->seq_dev, c->gemv_ws, c->attn_ws, c->tp_trace};
+                  c->ss_h, c->pos_dev, c->seq_dev, c->gemv_ws, c->attn_ws, c->tp_trace, c->tok_hist,
+                  c->am_ws};
   for (void* b : bufs)
     if (b) cudaFree(b);
   delete c;
@@ -303,7 +424,9 @@ extern "C" int r4q_decode_ctx_create(const r4q_model_desc* md, const r4q_layer_d
             {(void**)&c->logits, (size_t)B * m.lm_n * tps * 2 + 16}, {(void**)&c->h_out, (size_t)B * D * 2},
             {(void**)&c->ss_post, (size_t)D / 16 * B * 4}, {(void**)&c->ss_h, (size_t)D / 16 * B * 4},
             {(void**)&c->pos_dev, (size_t)B * 8},         {(void**)&c->seq_dev, (size_t)B * 8},
-            {&c->gemv_ws, c->gemv_ws_bytes},              {&c->attn_ws, c->attn_ws_bytes}};
+            {&c->gemv_ws, c->gemv_ws_bytes},              {&c->attn_ws, c->attn_ws_bytes},
+            {(void**)&c->tok_hist, (size_t)B * m.max_seq * 8},
+            {&c->am_ws, (size_t)B * kArgmaxBlocks * 8 + (size_t)B * 4 + 16}};
   for (auto& a : al) {
     cudaError_t e = cudaMalloc(a.p, a.n);
     if (e == cudaSuccess) e = cudaMemset(*a.p, 0, a.n);
@@ -335,6 +458,70 @@ extern "C" void r4q_decode_ctx_destroy(r4q_decode_ctx* c) {
   }
 }
 
+// kind 0: step without lm_head, 1: with logits, 2: greedy token (logits,
+// argmax into tok_hist at pos, embedding of the token into h_in)
+static int enqueue_kind(r4q_decode_ctx* c, int kind, cudaStream_t st) {
+  int rc = enqueue_step(c, kind >= 1, st);
+  if (rc || kind < 2) return rc;
+  const int B = c->m.batch;
+  const int V = c->m.lm_n * c->m.tp_size;
+  float2* part = reinterpret_cast<float2*>(c->am_ws);
+  unsigned* cnt = reinterpret_cast<unsigned*>(part + (size_t)B * kArgmaxBlocks);
+  argmax_kernel<<<dim3(kArgmaxBlocks, B), 256, 0, st>>>(c->logits, V, part, cnt, c->tok_hist, c->m.max_seq,
+                                                         c->pos_dev);
+  rc = check_launch("argmax_kernel");
+  if (rc) return rc;
+  embed_kernel<<<B, 256, 0, st>>>(reinterpret_cast<const __half*>(c->loop_embed), c->m.hidden, c->tok_hist,
+                                  c->m.max_seq, c->pos_dev, c->h_in);
+  return check_launch("embed_kernel");
+}
+
+// Run one step of `kind` at the position already set on the device: eagerly,
+// or through the context's CUDA graph for that kind (captured on first use).
+static int run_kind(r4q_decode_ctx* c, int kind, bool use_graph, cudaStream_t st) {
+  if (!use_graph) return enqueue_kind(c, kind, st);
+  cudaGraphExec_t& ge = c->graph[kind];
+  if (!ge) {
+    // one eager step first: it initialises every per-kernel setting (shared
+    // memory limits, tensor-map entry point) outside the capture; running the
+    // step twice is harmless (same inputs, same cache bytes at pos).  The
+    // token kind warms up without its argmax/embedding tail, which would
+    // replace the step's input.
+    int rc = enqueue_kind(c, kind < 2 ? kind : 1, st);
+    if (rc) return rc;
+    // capture on the context's stream, ordered after the caller's stream
+    cudaEvent_t ev;
+    cudaEventCreateWithFlags(&ev, cudaEventDisableTiming);
+    cudaEventRecord(ev, st);
+    cudaStreamWaitEvent(c->cap_stream, ev, 0);
+    cudaEventDestroy(ev);
+    cudaGraph_t g = nullptr;
+    cudaError_t e = cudaStreamBeginCapture(c->cap_stream, cudaStreamCaptureModeThreadLocal);
+    if (e != cudaSuccess) return set_error(R4Q_ERR_CUDA, "decode: begin capture: %s", cudaGetErrorString(e));
+    rc = enqueue_kind(c, kind, c->cap_stream);
+    e = cudaStreamEndCapture(c->cap_stream, &g);
+    if (rc) {
+      if (g) cudaGraphDestroy(g);
+      return rc;
+    }
+    if (e != cudaSuccess) return set_error(R4Q_ERR_CUDA, "decode: end capture: %s", cudaGetErrorString(e));
+    e = cudaGraphInstantiate(&ge, g, 0);
+    cudaGraphDestroy(g);
+    if (e != cudaSuccess) {
+      ge = nullptr;
+      return set_error(R4Q_ERR_CUDA, "decode: instantiate: %s", cudaGetErrorString(e));
+    }
+  }
+  cudaError_t e = cudaGraphLaunch(ge, st);
+  if (e != cudaSuccess) return set_error(R4Q_ERR_CUDA, "decode: graph launch: %s", cudaGetErrorString(e));
+  return R4Q_OK;
+}
+
+static int set_pos(r4q_decode_ctx* c, int pos, cudaStream_t st) {
+  set_positions<<<1, 32, 0, st>>>(c->pos_dev, c->seq_dev, c->m.batch, pos);
+  return check_launch("set_positions");
+}
+
 extern "C" int r4q_decode_step(r4q_decode_ctx* c, const void* hidden_in, int pos, void* hidden_out,
                                void* logits_out, int use_graph, void* stream) {
   if (!c || !hidden_in) return set_error(R4Q_ERR_ARG, "decode_step: null argument");
@@ -346,46 +533,9 @@ extern "C" int r4q_decode_step(r4q_decode_ctx* c, const void* hidden_in, int pos
   const bool with_logits = logits_out != nullptr;
   cudaError_t e = cudaMemcpyAsync(c->h_in, hidden_in, (size_t)B * D * 2, cudaMemcpyDeviceToDevice, st);
   if (e != cudaSuccess) return set_error(R4Q_ERR_CUDA, "decode_step: copy in: %s", cudaGetErrorString(e));
-  set_positions<<<1, 32, 0, st>>>(c->pos_dev, c->seq_dev, B, pos);
-  int rc = check_launch("set_positions");
+  int rc = set_pos(c, pos, st);
+  if (!rc) rc = run_kind(c, with_logits ? 1 : 0, use_graph != 0, st);
   if (rc) return rc;
-  if (use_graph) {
-    cudaGraphExec_t& ge = c->graph[with_logits ? 1 : 0];
-    if (!ge) {
-      // one eager run first: it initialises every per-kernel setting (shared
-      // memory limits, tensor-map entry point) outside the capture; running the
-      // step twice is harmless (same inputs, same cache bytes at pos)
-      rc = enqueue_step(c, with_logits, st);
-      if (rc) return rc;
-      // capture on the context's stream, ordered after the caller's stream
-      cudaEvent_t ev;
-      cudaEventCreateWithFlags(&ev, cudaEventDisableTiming);
-      cudaEventRecord(ev, st);
-      cudaStreamWaitEvent(c->cap_stream, ev, 0);
-      cudaEventDestroy(ev);
-      cudaGraph_t g = nullptr;
-      e = cudaStreamBeginCapture(c->cap_stream, cudaStreamCaptureModeThreadLocal);
-      if (e != cudaSuccess) return set_error(R4Q_ERR_CUDA, "decode_step: begin capture: %s", cudaGetErrorString(e));
-      rc = enqueue_step(c, with_logits, c->cap_stream);
-      e = cudaStreamEndCapture(c->cap_stream, &g);
-      if (rc) {
-        if (g) cudaGraphDestroy(g);
-        return rc;
-      }
-      if (e != cudaSuccess) return set_error(R4Q_ERR_CUDA, "decode_step: end capture: %s", cudaGetErrorString(e));
-      e = cudaGraphInstantiate(&ge, g, 0);
-      cudaGraphDestroy(g);
-      if (e != cudaSuccess) {
-        ge = nullptr;
-        return set_error(R4Q_ERR_CUDA, "decode_step: instantiate: %s", cudaGetErrorString(e));
-      }
-    }
-    e = cudaGraphLaunch(ge, st);
-    if (e != cudaSuccess) return set_error(R4Q_ERR_CUDA, "decode_step: graph launch: %s", cudaGetErrorString(e));
-  } else {
-    rc = enqueue_step(c, with_logits, st);
-    if (rc) return rc;
-  }
   const __half* hfinal = c->m.num_layers > 0 ? c->h : c->h_in;
   if (hidden_out) {
     e = cudaMemcpyAsync(hidden_out, hfinal, (size_t)B * D * 2, cudaMemcpyDeviceToDevice, st);
@@ -396,6 +546,89 @@ extern "C" int r4q_decode_step(r4q_decode_ctx* c, const void* hidden_in, int pos
                         cudaMemcpyDeviceToDevice, st);
     if (e != cudaSuccess) return set_error(R4Q_ERR_CUDA, "decode_step: copy logits: %s", cudaGetErrorString(e));
   }
+  return R4Q_OK;
+}
+
+__global__ void gather_tokens(const long long* tok_hist, int max_seq, int B, int start, int n, long long* out) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n * B) return;
+  const int t = i / B, b = i - t * B;
+  out[i] = tok_hist[(long)b * max_seq + start + t];
+}
+
+extern "C" int r4q_decode_loop(r4q_decode_ctx* c, const void* embed, const void* hidden_first, int start_pos,
+                               int num_tokens, long long* tokens_out, int use_graph, void* stream) {
+  if (!c || !embed || !hidden_first || !tokens_out || num_tokens < 0)
+    return set_error(R4Q_ERR_ARG, "decode_loop: bad arguments");
+  if (!c->m.lm_w) return set_error(R4Q_ERR_ARG, "decode_loop: the context has no lm_head");
+  if (start_pos < 0 || start_pos + num_tokens > c->m.max_seq)
+    return set_error(R4Q_ERR_CAPACITY, "decode_loop: positions %d..%d outside the KV cache (max_seq %d)",
+                     start_pos, start_pos + num_tokens - 1, c->m.max_seq);
+  if (num_tokens == 0) return R4Q_OK;
+  cudaStream_t st = (cudaStream_t)stream;
+  const int B = c->m.batch, D = c->m.hidden;
+  if (c->loop_embed != embed && c->graph[2]) {  // the token graph holds the table pointer
+    cudaGraphExecDestroy(c->graph[2]);
+    c->graph[2] = nullptr;
+  }
+  c->loop_embed = embed;
+  cudaError_t e = cudaMemcpyAsync(c->h_in, hidden_first, (size_t)B * D * 2, cudaMemcpyDeviceToDevice, st);
+  if (e != cudaSuccess) return set_error(R4Q_ERR_CUDA, "decode_loop: copy in: %s", cudaGetErrorString(e));
+  for (int t = 0; t < num_tokens; ++t) {
+    int rc = set_pos(c, start_pos + t, st);
+    if (!rc) rc = run_kind(c, 2, use_graph != 0, st);
+    if (rc) return rc;
+  }
+  const int n = num_tokens * B;
+  gather_tokens<<<(n + 255) / 256, 256, 0, st>>>(c->tok_hist, c->m.max_seq, B, start_pos, num_tokens, tokens_out);
+  return check_launch("gather_tokens");
+}
+
+// One eager step of kind 1 with events between the kernel groups:
+// [total, gemv, attention, norm (head norm/RoPE/KV write), rest] in ms
+// (decode_profile, int4_decode_step.hip:3047-3281).  Synchronous.
+extern "C" int r4q_decode_profile(r4q_decode_ctx* c, const void* hidden_in, int pos, float* out5, void* stream) {
+  if (!c || !hidden_in || !out5) return set_error(R4Q_ERR_ARG, "decode_profile: null argument");
+  if (pos < 0 || pos >= c->m.max_seq) return set_error(R4Q_ERR_CAPACITY, "decode_profile: pos %d", pos);
+  cudaStream_t st = (cudaStream_t)stream;
+  const int B = c->m.batch, D = c->m.hidden;
+  cudaError_t e = cudaMemcpyAsync(c->h_in, hidden_in, (size_t)B * D * 2, cudaMemcpyDeviceToDevice, st);
+  if (e != cudaSuccess) return set_error(R4Q_ERR_CUDA, "decode_profile: copy in: %s", cudaGetErrorString(e));
+  int rc = set_pos(c, pos, st);
+  if (rc) return rc;
+  c->prof = true;
+  c->prof_ev.clear();
+  cudaEvent_t e0, e1;
+  cudaEventCreate(&e0);
+  cudaEventCreate(&e1);
+  cudaEventRecord(e0, st);
+  rc = enqueue_step(c, c->m.lm_w != nullptr, st);
+  cudaEventRecord(e1, st);
+  c->prof = false;
+  if (!rc) e = cudaStreamSynchronize(st);
+  float total = 0.f, cat[3] = {0.f, 0.f, 0.f};
+  if (!rc && e == cudaSuccess) {
+    cudaEventElapsedTime(&total, e0, e1);
+    for (auto& pe : c->prof_ev) {
+      float ms = 0.f;
+      cudaEventElapsedTime(&ms, pe.a, pe.b);
+      cat[pe.cat] += ms;
+    }
+  }
+  for (auto& pe : c->prof_ev) {
+    cudaEventDestroy(pe.a);
+    cudaEventDestroy(pe.b);
+  }
+  c->prof_ev.clear();
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  if (rc) return rc;
+  if (e != cudaSuccess) return set_error(R4Q_ERR_CUDA, "decode_profile: %s", cudaGetErrorString(e));
+  out5[0] = total;
+  out5[1] = cat[0];
+  out5[2] = cat[1];
+  out5[3] = cat[2];
+  out5[4] = total - cat[0] - cat[1] - cat[2];
   return R4Q_OK;
 }
 

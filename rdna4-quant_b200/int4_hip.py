@@ -116,3 +116,73 @@ def decode_step_logits(hidden_in, qkv_w, qkv_s, qkv_N, o_w, o_s, o_N, gu_w, gu_s
     logits = torch.empty(B, 1, int(lm_N), dtype=torch.float16, device=h.device)
     ctx.step(h, pos, logits_out=logits, use_graph=USE_GRAPH)
     return logits
+
+
+def _logits_ctx(hidden, qkv_w, qkv_s, o_w, o_s, gu_w, gu_s, down_w, down_s, in_norm_w, post_norm_w,
+                q_norm_w, k_norm_w, rope_cos, rope_sin, num_heads, num_kv_heads, head_dim, hidden_size,
+                intermediate_size, rms_eps, k_caches, v_caches, final_norm_w, lm_w, lm_s, lm_N):
+    B = hidden.numel() // int(hidden_size)
+    ctx = _dec.get_context(qkv_w, qkv_s, o_w, o_s, gu_w, gu_s, down_w, down_s, in_norm_w,
+                           post_norm_w, q_norm_w, k_norm_w, rope_cos, rope_sin, num_heads,
+                           num_kv_heads, head_dim, hidden_size, intermediate_size, rms_eps,
+                           k_caches, v_caches, final_norm_w, lm_w, lm_s, lm_N, batch=B)
+    return ctx, hidden.reshape(B, int(hidden_size)).contiguous()
+
+
+def decode_loop(embed_weight, final_norm_w, lm_w, lm_s, lm_N, lm_K, first_token_hidden, num_tokens,
+                qkv_w, qkv_s, qkv_N, o_w, o_s, o_N, gu_w, gu_s, gu_N, down_w, down_s, down_N,
+                in_norm_w, post_norm_w, q_norm_w, k_norm_w, rope_cos, rope_sin, start_pos,
+                num_heads, num_kv_heads, head_dim, hidden_size, intermediate_size, rms_eps,
+                k_caches, v_caches, hadamard_mat=None):
+    """Greedy decode of ``num_tokens`` tokens starting at ``start_pos`` from
+    the first token's hidden state; token ids int64 on the CPU
+    (int4_decode_step.hip:3284-3466): every token is one device-side step +
+    argmax + embedding lookup, no host synchronisation until the end.
+    Returns [num_tokens] for one row, [num_tokens, B] for a batch."""
+    ctx, h = _logits_ctx(first_token_hidden, qkv_w, qkv_s, o_w, o_s, gu_w, gu_s, down_w, down_s,
+                         in_norm_w, post_norm_w, q_norm_w, k_norm_w, rope_cos, rope_sin, num_heads,
+                         num_kv_heads, head_dim, hidden_size, intermediate_size, rms_eps, k_caches,
+                         v_caches, final_norm_w, lm_w, lm_s, lm_N)
+    toks = ctx.loop(embed_weight, h, start_pos, num_tokens, use_graph=USE_GRAPH)
+    toks = toks.cpu()
+    return toks.reshape(-1) if toks.shape[1] == 1 else toks
+
+
+def _bench(hidden_in, embed_weight, num_tokens, layer_args, use_graph):
+    (qkv_w, qkv_s, qkv_N, o_w, o_s, o_N, gu_w, gu_s, gu_N, down_w, down_s, down_N, in_norm_w,
+     post_norm_w, q_norm_w, k_norm_w, rope_cos, rope_sin, start_pos, num_heads, num_kv_heads,
+     head_dim, hidden_size, intermediate_size, rms_eps, k_caches, v_caches, final_norm_w, lm_w,
+     lm_s, lm_N, lm_K, hadamard_mat) = layer_args
+    ctx, h = _logits_ctx(hidden_in, qkv_w, qkv_s, o_w, o_s, gu_w, gu_s, down_w, down_s, in_norm_w,
+                         post_norm_w, q_norm_w, k_norm_w, rope_cos, rope_sin, num_heads, num_kv_heads,
+                         head_dim, hidden_size, intermediate_size, rms_eps, k_caches, v_caches,
+                         final_norm_w, lm_w, lm_s, lm_N)
+    ctx.loop(embed_weight, h, start_pos, num_tokens, use_graph=use_graph)
+
+
+def decode_bench(hidden_in, embed_weight, num_tokens, *layer_args):
+    """Greedy decode of ``num_tokens`` tokens with per-kernel launches (no
+    graph), as the reference's C++ benchmark loop (int4_decode_step.hip:
+    2601-2795).  Returns None; the caller times it."""
+    _bench(hidden_in, embed_weight, num_tokens, layer_args, False)
+
+
+def decode_bench_graph(hidden_in, embed_weight, num_tokens, *layer_args):
+    """The same with one CUDA-graph launch per token (int4_decode_step.hip:
+    2801-3041); unlike the reference it keeps the argmax and the embedding
+    lookup inside the graph.  Returns None; the caller times it."""
+    _bench(hidden_in, embed_weight, num_tokens, layer_args, True)
+
+
+def decode_profile(hidden_in, embed_weight, qkv_w, qkv_s, qkv_N, o_w, o_s, o_N, gu_w, gu_s, gu_N,
+                   down_w, down_s, down_N, in_norm_w, post_norm_w, q_norm_w, k_norm_w, rope_cos,
+                   rope_sin, start_pos, num_heads, num_kv_heads, head_dim, hidden_size,
+                   intermediate_size, rms_eps, k_caches, v_caches, final_norm_w, lm_w, lm_s, lm_N,
+                   lm_K, hadamard_mat=None):
+    """[total_ms, gemv_ms, attn_ms, norm_ms, rest_ms] of one eager decode step
+    at ``start_pos`` (int4_decode_step.hip:3047-3281)."""
+    ctx, h = _logits_ctx(hidden_in, qkv_w, qkv_s, o_w, o_s, gu_w, gu_s, down_w, down_s, in_norm_w,
+                         post_norm_w, q_norm_w, k_norm_w, rope_cos, rope_sin, num_heads, num_kv_heads,
+                         head_dim, hidden_size, intermediate_size, rms_eps, k_caches, v_caches,
+                         final_norm_w, lm_w, lm_s, lm_N)
+    return ctx.profile(h, start_pos)

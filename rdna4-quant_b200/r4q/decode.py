@@ -42,6 +42,22 @@ class DecodeContext:
                None if logits_out is None else logits_out.data_ptr(), 1 if use_graph else 0,
                ops.stream_handle(dev))
 
+    def loop(self, embed, hidden_first, start_pos, num_tokens, use_graph=True):
+        """Greedy tokens [num_tokens, batch] int64 on the device (r4q_decode_loop)."""
+        dev = hidden_first.device
+        out = torch.empty(int(num_tokens), self.model.batch, dtype=torch.int64, device=dev)
+        if num_tokens:
+            L.call("r4q_decode_loop", self.handle, embed.data_ptr(), hidden_first.data_ptr(), int(start_pos),
+                   int(num_tokens), out.data_ptr(), 1 if use_graph else 0, ops.stream_handle(dev))
+        return out
+
+    def profile(self, hidden_in, pos):
+        """[total, gemv, attention, norm, rest] ms of one eager step (r4q_decode_profile)."""
+        out = (C.c_float * 5)()
+        L.call("r4q_decode_profile", self.handle, hidden_in.data_ptr(), int(pos), out,
+               ops.stream_handle(hidden_in.device))
+        return [float(v) for v in out]
+
     def __del__(self):
         try:
             if getattr(self, "handle", None):

@@ -82,6 +82,8 @@ _SIGS = {
     "r4q_decode_ctx_destroy": (None, [vp]),
     "r4q_decode_step": (i32, [vp, vp, i32, vp, vp, i32, vp]),
     "r4q_decode_tp_trace": (i32, [vp, vp]),
+    "r4q_decode_loop": (i32, [vp, vp, vp, i32, i32, vp, i32, vp]),
+    "r4q_decode_profile": (i32, [vp, vp, i32, vp, vp]),
     "r4q_comm_create": (i32, [i32, i32, i32, i32, i32, i64, C.POINTER(C.c_void_p), vp]),
     "r4q_comm_open": (i32, [vp, vp]),
     "r4q_comm_status": (i32, [vp]),

@@ -235,6 +235,10 @@ class TPDecoder:
             shard['final_norm_w'], shard['lm_w'], shard['lm_s'], self.vocab // w, batch=batch,
             comm=comm)
 
+    def loop(self, embed, h, start_pos: int, num_tokens: int, use_graph: bool = True):
+        """Greedy tokens [num_tokens, batch] (device int64), identical on every rank."""
+        return self.ctx.loop(embed, h.reshape(self.batch, self.hidden), start_pos, num_tokens, use_graph)
+
     def step(self, h, pos: int, logits: bool = True, out=None, use_graph: bool = True):
         import torch
         h2 = h.reshape(self.batch, self.hidden)

@@ -162,3 +162,80 @@ def test_decode_graph_equals_eager_and_consecutive_tokens():
                                     final, lm, write_kv=False)
     close(b.cpu().numpy().reshape(1, V), ref_b, STEP_TOL)
     decode.clear_contexts()
+
+
+def _layer_args(g, norms, kcs, vcs, t_final, lm_w, lm_s, t_cos, t_sin, pos):
+    return (g['qkv_w'], g['qkv_s'], 0, g['o_w'], g['o_s'], 0, g['gu_w'], g['gu_s'], 0,
+            g['down_w'], g['down_s'], 0, *norms, t_cos, t_sin, pos, H, HK, HD, D, I, EPS, kcs, vcs,
+            t_final, lm_w, lm_s, V, D, None)
+
+
+@pytest.mark.parametrize("use_graph", [True, False])
+def test_decode_loop_matches_stepwise_greedy(use_graph):
+    """decode_loop (device argmax + embedding, one graph per token) picks the
+    same tokens as decode_step_logits + torch.argmax + embedding lookup, and
+    leaves the same KV cache bytes."""
+    import int4_hip
+    from r4q import decode
+    rng = np.random.default_rng(21)
+    layers, final, lm = make_model(31, ('int4', 'int8'), 'fp16')
+    kc, vc = caches(rng, 1, 12)
+    cos, sin = O.rope_tables(HD, MAXS + 8, 1e6)
+    embed = cuda((rng.standard_normal((V, D)) * 0.5).astype(np.float16))
+    h0 = cuda((rng.standard_normal((1, 1, D)) * 0.5).astype(np.float16))
+    n, start = 6, 12
+    int4_hip.USE_GRAPH = use_graph
+    g, norms, kcs, vcs, t_final, lm_w, lm_s, t_cos, t_sin = gpu_args(layers, final, lm, kc, vc, cos, sin)
+    toks = int4_hip.decode_loop(embed, t_final, lm_w, lm_s, V, D, h0, n, g['qkv_w'], g['qkv_s'], 0, g['o_w'],
+                                g['o_s'], 0, g['gu_w'], g['gu_s'], 0, g['down_w'], g['down_s'], 0, *norms,
+                                t_cos, t_sin, start, H, HK, HD, D, I, EPS, kcs, vcs, None)
+    kl = [k.clone() for k in kcs]
+    decode.clear_contexts()
+    g, norms, kcs, vcs, t_final, lm_w, lm_s, t_cos, t_sin = gpu_args(layers, final, lm, kc, vc, cos, sin)
+    h = h0
+    ref = []
+    for t in range(n):
+        lg = run_gpu(int4_hip, h, start + t, g, norms, kcs, vcs, t_final, lm_w, lm_s, t_cos, t_sin)
+        tok = int(lg.reshape(-1).argmax())
+        ref.append(tok)
+        h = embed[tok].reshape(1, 1, D)
+    torch.cuda.synchronize()
+    int4_hip.USE_GRAPH = True
+    assert toks.dtype == torch.int64 and toks.device.type == 'cpu'
+    assert toks.tolist() == ref
+    for a, b in zip(kl, kcs):
+        assert torch.equal(a, b)
+    # decode_bench / decode_bench_graph run the same loop and return None
+    assert int4_hip.decode_bench(h0, embed, 3, *_layer_args(g, norms, kcs, vcs, t_final, lm_w, lm_s, t_cos,
+                                                            t_sin, start)) is None
+    assert int4_hip.decode_bench_graph(h0, embed, 3, *_layer_args(g, norms, kcs, vcs, t_final, lm_w, lm_s,
+                                                                  t_cos, t_sin, start)) is None
+    prof = int4_hip.decode_profile(h0, embed, *_layer_args(g, norms, kcs, vcs, t_final, lm_w, lm_s, t_cos,
+                                                           t_sin, start))
+    assert len(prof) == 5 and prof[0] > 0 and all(p >= 0 for p in prof[1:4])
+    assert abs(sum(prof[1:]) - prof[0]) < 1e-3 * max(1.0, prof[0]) + 1e-3
+    decode.clear_contexts()
+
+
+def test_argmax_first_maximum_and_ties():
+    """The device argmax takes the first index of the maximum (torch.argmax)."""
+    import int4_hip
+    from r4q import decode
+    rng = np.random.default_rng(2)
+    layers, final, lm = make_model(4, ('int4', 'int4'), 'fp16')
+    # rows 7 and 900 identical: equal logits, whichever value they take
+    w = lm[1].copy()
+    w[7] = w[900] = np.abs(w[7]) * 0 + 0.5
+    lm = ('fp16', w)
+    kc, vc = caches(rng, 1, 4)
+    cos, sin = O.rope_tables(HD, MAXS + 8, 1e6)
+    embed = cuda((rng.standard_normal((V, D)) * 0.5).astype(np.float16))
+    g, norms, kcs, vcs, t_final, lm_w, lm_s, t_cos, t_sin = gpu_args(layers, final, lm, kc, vc, cos, sin)
+    h0 = cuda(np.abs(rng.standard_normal((1, 1, D))).astype(np.float16))
+    lg = run_gpu(int4_hip, h0, 4, g, norms, kcs, vcs, t_final, lm_w, lm_s, t_cos, t_sin)
+    want = int(lg.reshape(-1).argmax())
+    toks = int4_hip.decode_loop(embed, t_final, lm_w, lm_s, V, D, h0, 1, g['qkv_w'], g['qkv_s'], 0, g['o_w'],
+                                g['o_s'], 0, g['gu_w'], g['gu_s'], 0, g['down_w'], g['down_s'], 0, *norms,
+                                t_cos, t_sin, 4, H, HK, HD, D, I, EPS, kcs, vcs, None)
+    assert toks.tolist() == [want]
+    decode.clear_contexts()
