@@ -163,6 +163,21 @@ int r4q_flash_decode(const void* q, long ldq, const void* k_cache, const void* v
                      int Hk, int D, int max_seq, int seq_len, const long long* seq_dev, int flags,
                      void* workspace, size_t ws_bytes, void* stream);
 
+/* r4q_head_norm_rope (NORM | ROPE | KV) and r4q_flash_decode in one launch:
+ * qkv fp16 [B, ld] holds the new token's raw q (H heads), k, v (Hk heads each)
+ * side by side; q and k are RMS-normalised (q_norm_w / k_norm_w) and rotated
+ * at pos = seq - 1, K and V are encoded to FP8 at cache row pos (divided by the
+ * optional per-head scales), and o = attention over [0, seq) (R4Q_ATTN_FWHT as
+ * in r4q_flash_decode).  The cache and o equal the two-call sequence.
+ * Replaces head_rmsnorm_rope_kv + flash_decode (int4_decode_step.hip:
+ * 1326-1593, 1620-1683) on the decode path. */
+int r4q_attn_decode_fused(const void* qkv, long ld, const void* q_norm_w, const void* k_norm_w,
+                          const void* cos_tab, const void* sin_tab, long tab_stride, float eps,
+                          void* k_cache, void* v_cache, const float* k_scale, const float* v_scale,
+                          void* o, long ldo, int B, int H, int Hk, int D, int max_seq, int seq_len,
+                          const long long* seq_dev, int flags, void* workspace, size_t ws_bytes,
+                          void* stream);
+
 /* ------------------------------------------------------------- decode step --- */
 /* One transformer layer's weights and caches (device pointers).  *_fmt is
  * R4Q_W_INT4 (packed [N, K/2] + (scale, zero) pairs [N, K/16]) or R4Q_W_INT8

@@ -21,6 +21,7 @@
 #include <cstring>
 #include <vector>
 
+#include "attention.cuh"
 #include "comm.cuh"
 #include "gemv.cuh"
 #include "r4q_common.cuh"
@@ -221,6 +222,30 @@ static PushSet push_slots(r4q_decode_ctx* c, int parity) {
   return s;
 }
 
+// Head norm + RoPE + KV write of the new token and attention over [0, pos]
+// with the FWHT epilogue: one fused launch (R4Q_ATTN_FUSED=0: the two kernels).
+static int attn_step(r4q_decode_ctx* c, const r4q_layer_desc& ly, cudaStream_t st) {
+  const r4q_model_desc& m = c->m;
+  const int B = m.batch, H = m.num_heads, Hk = m.num_kv_heads, hd = m.head_dim;
+  const int qd = H * hd, kvd = Hk * hd, qkv_n = qd + 2 * kvd;
+  static const bool fused = [] {
+    const char* e = getenv("R4Q_ATTN_FUSED");
+    return !(e && e[0] == '0');
+  }();
+  if (fused)
+    return r4q_attn_decode_fused_ex(c->qkv, qkv_n, ly.q_norm, ly.k_norm, m.rope_cos, m.rope_sin, m.rope_stride,
+                                    m.rms_eps, ly.k_cache, ly.v_cache, ly.k_scale, ly.v_scale, c->attn, qd, B, H,
+                                    Hk, hd, m.max_seq, 0, c->seq_dev, R4Q_ATTN_FWHT, 1, c->attn_ws,
+                                    c->attn_ws_bytes, st);
+  int rc = r4q_head_norm_rope(c->qkv, c->qkv + qd, c->qkv + qd + kvd, ly.q_norm, ly.k_norm, m.rope_cos,
+                              m.rope_sin, m.rope_stride, 0, c->pos_dev, c->qkv, c->qkv + qd, ly.k_cache,
+                              ly.v_cache, ly.k_scale, ly.v_scale, B, H, Hk, hd, qkv_n, qkv_n, m.max_seq,
+                              m.rms_eps, R4Q_HEAD_NORM | R4Q_HEAD_ROPE | R4Q_HEAD_KV, st);
+  if (rc) return rc;
+  return r4q_flash_decode(c->qkv, qkv_n, ly.k_cache, ly.v_cache, ly.k_scale, ly.v_scale, c->attn, qd, B, H, Hk,
+                          hd, m.max_seq, 0, c->seq_dev, R4Q_ATTN_FWHT, c->attn_ws, c->attn_ws_bytes, st);
+}
+
 // One rank of a tensor-parallel step.  Exchange 2*li is layer li's o_proj,
 // 2*li + 1 its down_proj (reduce slots of parity idx & 1), 2*L the lm_head
 // vocabulary gather.  Producers push fp32 partials into every rank's slot and
@@ -270,14 +295,7 @@ static int enqueue_step_tp(r4q_decode_ctx* c, bool with_logits, cudaStream_t st)
                    ly.in_norm, st);
     if (rc) break;
     const __half* hin = (li == 0) ? c->h_in : c->h;
-    rc = r4q_head_norm_rope(c->qkv, c->qkv + qd, c->qkv + qd + kvd, ly.q_norm, ly.k_norm, m.rope_cos,
-                            m.rope_sin, m.rope_stride, 0, c->pos_dev, c->qkv, c->qkv + qd, ly.k_cache,
-                            ly.v_cache, ly.k_scale, ly.v_scale, B, H, Hk, hd, qkv_n, qkv_n,
-                            m.max_seq, m.rms_eps, R4Q_HEAD_NORM | R4Q_HEAD_ROPE | R4Q_HEAD_KV, st);
-    if (rc) break;
-    rc = r4q_flash_decode(c->qkv, qkv_n, ly.k_cache, ly.v_cache, ly.k_scale, ly.v_scale, c->attn, qd,
-                          B, H, Hk, hd, m.max_seq, 0, c->seq_dev, R4Q_ATTN_FWHT, c->attn_ws,
-                          c->attn_ws_bytes, st);
+    rc = attn_step(c, ly, st);
     if (rc) break;
     // 4. o_proj over this rank's heads -> pushed + signalled (exchange xo)
     {
@@ -331,21 +349,11 @@ static int enqueue_step(r4q_decode_ctx* c, bool with_logits, cudaStream_t st) {
                    ly.in_norm, li == 0 ? nullptr : c->ss_h, D / 16, nullptr, nullptr, st);
     }
     if (rc) break;
-    // 2. QK norm + RoPE in place, K/V to the FP8 cache
-    {
-    ProfScope ps(c, 2, st);
-    rc = r4q_head_norm_rope(c->qkv, c->qkv + qd, c->qkv + qd + kvd, ly.q_norm, ly.k_norm, m.rope_cos,
-                            m.rope_sin, m.rope_stride, 0, c->pos_dev, c->qkv, c->qkv + qd, ly.k_cache,
-                            ly.v_cache, ly.k_scale, ly.v_scale, B, H, Hk, hd, qkv_n, qkv_n,
-                            m.max_seq, m.rms_eps, R4Q_HEAD_NORM | R4Q_HEAD_ROPE | R4Q_HEAD_KV, st);
-    }
-    if (rc) break;
-    // 3. attention over [0, pos], FWHT on the output (feeds o_proj)
+    // 2-3. QK norm + RoPE, K/V to the FP8 cache, attention over [0, pos] with
+    //      the FWHT on the output (feeds o_proj)
     {
     ProfScope ps(c, 1, st);
-    rc = r4q_flash_decode(c->qkv, qkv_n, ly.k_cache, ly.v_cache, ly.k_scale, ly.v_scale, c->attn, qd,
-                          B, H, Hk, hd, m.max_seq, 0, c->seq_dev, R4Q_ATTN_FWHT, c->attn_ws,
-                          c->attn_ws_bytes, st);
+    rc = attn_step(c, ly, st);
     }
     if (rc) break;
     ProfScope ps(c, 0, st);  // o, gate_up, down

@@ -176,3 +176,21 @@ def flash_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, 
            _ptr(seq_dev), L.ATTN_FWHT if fwht else 0, ws.data_ptr(), ws.numel(),
            stream_handle(dev))
     return o
+
+
+def attn_decode_fused(qkv, k_cache, v_cache, q_w, k_w, cos, sin, H, Hk, seq_len, *, k_scale=None,
+                      v_scale=None, fwht=False, eps=1e-6, out=None, seq_dev=None):
+    """Head norm + RoPE + FP8 KV write of the new token and attention in one
+    launch (r4q_attn_decode_fused).  qkv fp16 [B, (H + 2 Hk) * 128]; caches
+    uint8 [B, Hk, max_seq, 128] (row seq_len - 1 is written) -> o [B, H, 128]."""
+    dev = _require_cuda(qkv, k_cache, v_cache)
+    B = qkv.shape[0]
+    D = 128
+    max_seq = int(k_cache.shape[2])
+    o = out if out is not None else torch.empty(B, H, D, dtype=torch.float16, device=dev)
+    ws = attn_workspace(dev, B, H, Hk, max_seq)
+    L.call("r4q_attn_decode_fused", qkv.data_ptr(), qkv.stride(0), q_w.data_ptr(), k_w.data_ptr(),
+           cos.data_ptr(), sin.data_ptr(), cos.stride(0), float(eps), k_cache.data_ptr(), v_cache.data_ptr(),
+           _ptr(k_scale), _ptr(v_scale), o.data_ptr(), H * D, B, H, Hk, D, max_seq, int(seq_len),
+           _ptr(seq_dev), L.ATTN_FWHT if fwht else 0, ws.data_ptr(), ws.numel(), stream_handle(dev))
+    return o

@@ -79,3 +79,40 @@ def test_flash_decode_repeatable_and_workspace_clean():
     b = ops.flash_decode(q, cuda(kc), cuda(vc), 500)
     torch.cuda.synchronize()
     assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("B,ctx,scaled", [(1, 1, False), (1, 64, False), (1, 65, True), (2, 300, False),
+                                          (1, 2048, True), (4, 4097, False), (1, 9000, False)])
+def test_fused_head_ops_attention_equals_two_kernels(B, ctx, scaled):
+    """r4q_attn_decode_fused (q/k norm + RoPE + FP8 write of row ctx-1 +
+    attention) leaves the same cache bytes and the same output, bit for bit,
+    as r4q_head_norm_rope followed by r4q_flash_decode; and matches the oracle."""
+    from r4q import lib as L, ops
+    rng = np.random.default_rng(B * 31 + ctx)
+    max_seq = ctx + 9
+    kc, vc, ks, vs = make_cache(rng, B, ctx - 1, max_seq, scaled)
+    qkv = (rng.standard_normal((B, (H + 2 * HK) * D)) * 2).astype(np.float16)
+    qw = (1 + 0.1 * rng.standard_normal(D)).astype(np.float16)
+    kw = (1 + 0.1 * rng.standard_normal(D)).astype(np.float16)
+    cos, sin = O.rope_tables(D, max_seq + 4, 1e6)
+    t = cuda
+    tks, tvs = (None, None) if ks is None else (t(ks), t(vs))
+    pos = ctx - 1
+    # two kernels
+    q1 = t(qkv)
+    kc1, vc1 = t(kc), t(vc)
+    ops.head_norm_rope(q1[:, :H * D], q1[:, H * D:], v=q1[:, (H + HK) * D:], q_w=t(qw), k_w=t(kw), cos=t(cos),
+                       sin=t(sin), pos=pos, q_out=q1[:, :H * D], k_out=q1[:, H * D:], k_cache=kc1, v_cache=vc1,
+                       k_scale=tks, v_scale=tvs, B=B, H=H, Hk=HK, D=D,
+                       flags=L.HEAD_NORM | L.HEAD_ROPE | L.HEAD_KV)
+    qn = q1[:, :H * D].reshape(B, H, D).contiguous()
+    o1 = ops.flash_decode(qn, kc1, vc1, ctx, k_scale=tks, v_scale=tvs, fwht=True)
+    # fused
+    kc2, vc2 = t(kc), t(vc)
+    o2 = ops.attn_decode_fused(t(qkv), kc2, vc2, t(qw), t(kw), t(cos), t(sin), H, HK, ctx, k_scale=tks,
+                               v_scale=tvs, fwht=True)
+    torch.cuda.synchronize()
+    assert torch.equal(kc1, kc2) and torch.equal(vc1, vc2)
+    assert torch.equal(o1, o2)
+    ref = O.attention_decode(qn.cpu().numpy(), kc2.cpu().numpy(), vc2.cpu().numpy(), ctx, ks, vs, fwht_out=True)
+    close(o2.cpu().numpy(), ref)
