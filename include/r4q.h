@@ -178,6 +178,21 @@ int r4q_attn_decode_fused(const void* qkv, long ld, const void* q_norm_w, const 
                           const long long* seq_dev, int flags, void* workspace, size_t ws_bytes,
                           void* stream);
 
+/* ------------------------------------------------------------ prefill GEMM --- */
+/* y[M, N] fp16 = x[M, K] fp16 · w[N, K]ᵀ on the tcgen05 tensor cores (fp32
+ * accumulation in tensor memory).  x row stride ldx, y row stride ldy
+ * (elements); K % 8 == 0, 16-byte aligned x and w.  workspace: >= 4 bytes,
+ * zeroed, receives 1 if a bounded wait gave up.  Replaces the rocBLAS GEMM of
+ * the reference prefill (int4_decode_step.hip:2127-2320). */
+int r4q_gemm_fp16(const void* x, long ldx, const void* w, void* y, long ldy, int M, int N, int K,
+                  void* workspace, size_t ws_bytes, void* stream);
+/* The same with INT4 weights in the runtime layout (nibbles [N, K/2], (scale,
+ * zero) pairs [N, K/16]), dequantised in the kernel to the exact reference
+ * value fp16((q - z) · s) (dequant_int4, :3568-3603) — dequant + GEMM of the
+ * reference prefill (:1973-1988) in one pass over the weights.  K % 64 == 0. */
+int r4q_gemm_int4(const void* x, long ldx, const void* w, const void* sz, void* y, long ldy, int M, int N,
+                  int K, void* workspace, size_t ws_bytes, void* stream);
+
 /* ------------------------------------------------------------- decode step --- */
 /* One transformer layer's weights and caches (device pointers).  *_fmt is
  * R4Q_W_INT4 (packed [N, K/2] + (scale, zero) pairs [N, K/16]) or R4Q_W_INT8

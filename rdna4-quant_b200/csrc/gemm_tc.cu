@@ -1,0 +1,370 @@
+// Prefill / batched GEMM on the 5th-generation tensor cores (tcgen05).
+//
+// Replaces the prefill projections of the reference, which dequantise the
+// INT4 weights to fp16 (dequant_int4, int4_decode_step.hip:1973-1988, 3568-3603)
+// and call rocBLAS (int4_prefill_logits, :2127-2320; int4_engine_v5.py:
+// 214-266):  Y[M, N] = X[M, K] · W[N, K]ᵀ, fp16 in, fp32 accumulate, fp16 out.
+//
+// B200 design (one 128 x 256 output tile per CTA, 4 warps):
+//  * warp 0, one lane: TMA producer.  X tiles [128 x 64] and W tiles
+//    [256 x 64] (fp16, K-major, 128-byte swizzle) into a 4-stage ring with
+//    mbarrier transaction counts;
+//  * INT4 weights (`w4` set): warps 2-3 dequantise instead of TMA-loading W:
+//    the nibbles come in by TMA, the (scale, zero) pairs by plain loads (8 bytes
+//    per row and stage, below TMA's 16-byte box minimum), the exact reference value
+//    fp16((q - z) · s) is written into the same swizzled fp16 layout, then
+//    fence.proxy.async makes it visible to the tensor cores;
+//  * warp 1, one lane: issues tcgen05.mma.cta_group::1.kind::f16 (M = 128,
+//    N = 256, K = 16 per instruction, 4 per stage) from shared-memory matrix
+//    descriptors into a 128 x 256 fp32 accumulator in tensor memory, and
+//    tcgen05.commit releases each stage back to the producer;
+//  * all 4 warps: epilogue, tcgen05.ld of their 32 accumulator lanes (= rows),
+//    fp16 conversion, stores.
+// Every mbarrier wait is bounded; a timeout sets the status word and the
+// kernel drains.  No multicast anywhere.
+#include <cuda.h>
+
+#include <mutex>
+
+#include "r4q_common.cuh"
+
+namespace r4q {
+namespace {
+
+constexpr int kBM = 128, kBN = 256, kBK = 64;
+constexpr int kStages = 4;
+constexpr int kABytes = kBM * kBK * 2;             // 16 KB
+constexpr int kBBytes = kBN * kBK * 2;             // 32 KB
+constexpr int kW4Bytes = kBN * kBK / 2;            // 8 KB of nibbles per stage
+constexpr int kGemmThreads = 128;
+constexpr long kGemmSpin = 1L << 26;
+
+struct GemmParams {
+  const uint8_t* sz;   // INT4: (scale, zero) fp16 pairs [N][K/16]
+  __half* y;
+  long ldy;
+  int M, N, K;
+  int w4;          // 1: W is INT4 (nibbles + pairs), dequantised in the kernel
+  int* status;
+};
+
+__device__ __forceinline__ uint32_t sm_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void g_mbar_init(uint64_t* b, unsigned n) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(sm_u32(b)), "r"(n));
+}
+__device__ __forceinline__ void g_expect_tx(uint64_t* b, unsigned bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(sm_u32(b)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void g_arrive(uint64_t* b) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(sm_u32(b)) : "memory");
+}
+__device__ __forceinline__ bool g_wait(uint64_t* b, unsigned parity, int* status) {
+  const uint32_t a = sm_u32(b);
+  for (long i = 0; i < kGemmSpin; ++i) {
+    uint32_t ok;
+    asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+                 " selp.u32 %0, 1, 0, p;\n}\n" : "=r"(ok) : "r"(a), "r"(parity) : "memory");
+    if (ok) return true;
+  }
+  if (status) atomicExch(status, 1);
+  return false;
+}
+__device__ __forceinline__ void g_tma2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(sm_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(sm_u32(bar))
+      : "memory");
+}
+
+// Shared-memory matrix descriptor, K-major, 128-byte swizzle: rows of 128
+// bytes (64 fp16), 8-row groups 1024 bytes apart (stride byte offset), no
+// leading byte offset, descriptor version 1, layout type 2 (SWIZZLE_128B).
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFF);
+  d |= (uint64_t)(1024 >> 4) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;
+  return d;
+}
+
+// Instruction descriptor of kind::f16: fp32 accumulator, fp16 A and B, both
+// K-major, N = 256, M = 128.
+constexpr uint32_t kIdesc = (1u << 4) | (uint32_t(kBN >> 3) << 17) | (uint32_t(kBM >> 4) << 24);
+
+__device__ __forceinline__ void umma_f16(uint32_t tmem, uint64_t da, uint64_t db, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}\n"
+      ::"r"(tmem), "l"(da), "l"(db), "r"(kIdesc), "r"(accumulate), "r"(0), "r"(0), "r"(0), "r"(0));
+}
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(sm_u32(bar))
+               : "memory");
+}
+
+// One INT4 stage: 256 rows x 64 k.  Nibbles [256][32 B] (plain TMA box) and
+// the rows' (scale, zero) pairs of blocks 2 kt, 2 kt + 1 (8 bytes in global
+// memory) -> fp16 in the 128-byte swizzled K-major layout TMA would have
+// produced: element (r, k) at r * 128 + (((k >> 3) ^ (r & 7)) << 4) + (k & 7) * 2.
+// Thread t of the 64 dequant threads takes rows t, t + 64, ...; each row is 8
+// chunks of 8 k.  Rows past N (zero nibbles) get zero pairs.
+__device__ __forceinline__ void dequant_stage(const uint8_t* w4, const uint8_t* sz, long ld_sz, int n0, int N,
+                                              int kt, uint8_t* bdst, int t) {
+  for (int r = t; r < kBN; r += 64) {
+    const uint4 q0 = *reinterpret_cast<const uint4*>(w4 + r * 32);
+    const uint4 q1 = *reinterpret_cast<const uint4*>(w4 + r * 32 + 16);
+    const uint32_t qw[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+    const uint2 pz = (n0 + r < N) ? __ldg(reinterpret_cast<const uint2*>(sz + (long)(n0 + r) * ld_sz + kt * 8))
+                                  : make_uint2(0u, 0u);
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {                        // 8 k per chunk = 4 bytes of nibbles
+      const uint32_t pair = (c < 4) ? pz.x : pz.y;        // block 0: k 0..31, block 1: k 32..63
+      const __half2 szh = u32_as_h2(pair);
+      const __half s = __low2half(szh), z = __high2half(szh);
+      const uint32_t wq = qw[c];
+      uint32_t o[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const uint32_t byte = (wq >> (8 * j)) & 0xFFu;
+        const __half lo = __ushort2half_rn((unsigned short)(byte & 0xFu));
+        const __half hi = __ushort2half_rn((unsigned short)(byte >> 4));
+        o[j] = h2_as_u32(__halves2half2(__hmul(__hsub(lo, z), s), __hmul(__hsub(hi, z), s)));
+      }
+      *reinterpret_cast<uint4*>(bdst + r * 128 + ((c ^ (r & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tma, const __grid_constant__ CUtensorMap tmb,
+                   const GemmParams p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sa = smem;                                        // [stage][16 KB]
+  uint8_t* sb = sa + kStages * kABytes;                      // [stage][32 KB] fp16 W
+  uint8_t* sw4 = sb + kStages * kBBytes;                     // [stage][8 KB]  INT4 nibbles
+  uint64_t* full = reinterpret_cast<uint64_t*>(sw4 + kStages * kW4Bytes);
+  uint64_t* empty = full + kStages;
+  uint64_t* w4full = empty + kStages;                        // INT4 bytes landed
+  uint64_t* bready = w4full + kStages;                       // dequantised W ready
+  uint64_t* accum = bready + kStages;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int n0 = blockIdx.x * kBN, m0 = blockIdx.y * kBM;
+  const int KT = (p.K + kBK - 1) / kBK;
+
+  if (tid == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      g_mbar_init(&full[s], 1);
+      g_mbar_init(&empty[s], 1);
+      g_mbar_init(&w4full[s], 1);
+      g_mbar_init(&bready[s], 64);
+    }
+    g_mbar_init(accum, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 2) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(sm_u32(tmem_slot)),
+                 "r"(kBN));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;");
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0 && lane == 0) {
+    // ---- producer
+    bool ok = true;
+    for (int kt = 0; kt < KT && ok; ++kt) {
+      const int s = kt % kStages;
+      if (kt >= kStages) ok = g_wait(&empty[s], ((kt / kStages) - 1) & 1, p.status);
+      if (!ok) break;
+      if (p.w4) {
+        g_expect_tx(&full[s], kABytes);
+        g_tma2d(sa + s * kABytes, &tma, kt * kBK, m0, &full[s]);
+        g_expect_tx(&w4full[s], kW4Bytes);
+        g_tma2d(sw4 + s * kW4Bytes, &tmb, kt * (kBK / 2), n0, &w4full[s]);
+      } else {
+        g_expect_tx(&full[s], kABytes + kBBytes);
+        g_tma2d(sa + s * kABytes, &tma, kt * kBK, m0, &full[s]);
+        g_tma2d(sb + s * kBBytes, &tmb, kt * kBK, n0, &full[s]);
+      }
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ---- MMA issuer
+    bool ok = true;
+    for (int kt = 0; kt < KT; ++kt) {
+      const int s = kt % kStages;
+      const unsigned ph = (kt / kStages) & 1;
+      if (ok) ok = g_wait(&full[s], ph, p.status);
+      if (ok && p.w4) ok = g_wait(&bready[s], ph, p.status);
+      asm volatile("tcgen05.fence::after_thread_sync;");
+      if (ok) {
+        const uint32_t a0 = sm_u32(sa + s * kABytes), b0 = sm_u32(sb + s * kBBytes);
+#pragma unroll
+        for (int kk = 0; kk < kBK / 16; ++kk)
+          umma_f16(tmem, sw128_desc(a0 + kk * 32), sw128_desc(b0 + kk * 32), (kt | kk) ? 1u : 0u);
+      }
+      umma_commit(&empty[s]);               // the stage is free once these MMAs have read it
+    }
+    umma_commit(accum);
+  } else if (warp >= 2 && p.w4) {
+    // ---- INT4 dequantisers (64 threads)
+    const int t = tid - 64;
+    bool ok = true;
+    for (int kt = 0; kt < KT; ++kt) {
+      const int s = kt % kStages;
+      const unsigned ph = (kt / kStages) & 1;
+      if (ok) ok = g_wait(&w4full[s], ph, p.status);
+      // the fp16 slot was last read by the MMAs of stage kt - kStages
+      if (ok && kt >= kStages) ok = g_wait(&empty[s], ((kt / kStages) - 1) & 1, p.status);
+      if (ok) dequant_stage(sw4 + s * kW4Bytes, p.sz, p.K / 8, n0, p.N, kt, sb + s * kBBytes, t);
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      g_arrive(&bready[s]);
+    }
+  }
+
+  // ---- epilogue: warp w owns accumulator lanes (rows) 32w..32w+31
+  __syncwarp();
+  const bool ok = g_wait(accum, 0, p.status);
+  asm volatile("tcgen05.fence::after_thread_sync;");
+  const int row = m0 + warp * 32 + lane;
+#pragma unroll 1
+  for (int c0 = 0; c0 < kBN; c0 += 32) {
+    uint32_t v[32];
+    const uint32_t taddr = tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0;
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]),
+          "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]),
+          "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+    if (!ok || row >= p.M) continue;
+    __half* yr = p.y + (long)row * p.ldy + n0 + c0;
+    const int nvalid = min(32, p.N - (n0 + c0));
+    if (nvalid == 32 && (p.ldy % 8) == 0 && (reinterpret_cast<uintptr_t>(p.y) & 15) == 0) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        uint4 o;
+        o.x = h2_as_u32(__floats2half2_rn(__uint_as_float(v[8 * q]), __uint_as_float(v[8 * q + 1])));
+        o.y = h2_as_u32(__floats2half2_rn(__uint_as_float(v[8 * q + 2]), __uint_as_float(v[8 * q + 3])));
+        o.z = h2_as_u32(__floats2half2_rn(__uint_as_float(v[8 * q + 4]), __uint_as_float(v[8 * q + 5])));
+        o.w = h2_as_u32(__floats2half2_rn(__uint_as_float(v[8 * q + 6]), __uint_as_float(v[8 * q + 7])));
+        reinterpret_cast<uint4*>(yr)[q] = o;
+      }
+    } else {
+      for (int j = 0; j < nvalid; ++j) yr[j] = __float2half(__uint_as_float(v[j]));
+    }
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;");
+  __syncthreads();
+  if (warp == 2) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kBN));
+}
+
+typedef CUresult (*EncodeTiledFnG)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFnG encode_g() {
+  static EncodeTiledFnG fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFnG>(f);
+  });
+  return fn;
+}
+
+// 2-D map over [rows, cols] elements of `esize` bytes, row stride ld elements.
+int map2d(CUtensorMap* m, const void* base, CUtensorMapDataType dt, int esize, long rows, long cols, long ld,
+          int box_cols, int box_rows, CUtensorMapSwizzle sw) {
+  EncodeTiledFnG fn = encode_g();
+  if (!fn) return set_error(R4Q_ERR_CUDA, "gemm: cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(ld * esize)};
+  cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
+  cuuint32_t es[2] = {1, 1};
+  CUresult r = fn(m, dt, 2, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(R4Q_ERR_CUDA, "gemm: tensor map encode failed (%d)", (int)r);
+  return R4Q_OK;
+}
+
+size_t gemm_smem() {
+  return 1024 + (size_t)kStages * (kABytes + kBBytes + kW4Bytes) + (4 * kStages + 1) * 8 + 16;
+}
+
+int launch_gemm(const void* x, long ldx, const void* w, const void* s, void* y, long ldy, int M, int N, int K,
+                int w4, int* status, cudaStream_t st) {
+  CUtensorMap ta, tb;
+  int rc = map2d(&ta, x, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, M, K, ldx, kBK, kBM, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  if (w4) {
+    // nibbles [N, K/2] bytes, box 32 B x 256 rows (plain layout)
+    rc = map2d(&tb, w, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, N, K / 2, K / 2, kBK / 2, kBN, CU_TENSOR_MAP_SWIZZLE_NONE);
+  } else {
+    rc = map2d(&tb, w, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, N, K, K, kBK, kBN, CU_TENSOR_MAP_SWIZZLE_128B);
+  }
+  if (rc) return rc;
+  GemmParams p{};
+  p.sz = (const uint8_t*)s;
+  p.y = (__half*)y;
+  p.ldy = ldy;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.w4 = w4;
+  p.status = status;
+  const size_t smem = gemm_smem();
+  static std::mutex mu;
+  static bool done[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    if (dev < 64 && !done[dev]) {
+      cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      cudaGetLastError();
+      done[dev] = true;
+    }
+  }
+  dim3 grid((N + kBN - 1) / kBN, (M + kBM - 1) / kBM);
+  gemm_tc_kernel<<<grid, kGemmThreads, smem, st>>>(ta, tb, p);
+  return check_launch("gemm_tc_kernel");
+}
+
+}  // namespace
+}  // namespace r4q
+
+using namespace r4q;
+
+extern "C" int r4q_gemm_fp16(const void* x, long ldx, const void* w, void* y, long ldy, int M, int N, int K,
+                             void* ws, size_t ws_bytes, void* stream) {
+  if (!x || !w || !y || M < 1 || N < 1 || K < 1) return set_error(R4Q_ERR_ARG, "gemm_fp16: bad arguments");
+  if (K % 8 || ldx % 8 || ldx < K || ldy < N || !aligned(x, 16) || !aligned(w, 16) || !aligned(y, 2))
+    return set_error(R4Q_ERR_ALIGN, "gemm_fp16: K, ldx multiples of 8 and 16-byte aligned x, w required");
+  if (!ws || ws_bytes < 4) return set_error(R4Q_ERR_CAPACITY, "gemm_fp16: workspace (status word) required");
+  return launch_gemm(x, ldx, w, nullptr, y, ldy, M, N, K, 0, (int*)ws, (cudaStream_t)stream);
+}
+
+extern "C" int r4q_gemm_int4(const void* x, long ldx, const void* w, const void* sz, void* y, long ldy, int M,
+                             int N, int K, void* ws, size_t ws_bytes, void* stream) {
+  if (!x || !w || !sz || !y || M < 1 || N < 1 || K < 1) return set_error(R4Q_ERR_ARG, "gemm_int4: bad arguments");
+  if (K % 64 || ldx % 8 || ldx < K || ldy < N || !aligned(x, 16) || !aligned(w, 16) || !aligned(sz, 16) ||
+      !aligned(y, 2))
+    return set_error(R4Q_ERR_ALIGN, "gemm_int4: K % 64 == 0, ldx % 8 == 0 and 16-byte aligned x, w, sz required");
+  if (!ws || ws_bytes < 4) return set_error(R4Q_ERR_CAPACITY, "gemm_int4: workspace (status word) required");
+  return launch_gemm(x, ldx, w, sz, y, ldy, M, N, K, 1, (int*)ws, (cudaStream_t)stream);
+}

@@ -194,3 +194,39 @@ def attn_decode_fused(qkv, k_cache, v_cache, q_w, k_w, cos, sin, H, Hk, seq_len,
            _ptr(k_scale), _ptr(v_scale), o.data_ptr(), H * D, B, H, Hk, D, max_seq, int(seq_len),
            _ptr(seq_dev), L.ATTN_FWHT if fwht else 0, ws.data_ptr(), ws.numel(), stream_handle(dev))
     return o
+
+
+_gws: dict = {}
+
+
+def _status_ws(dev):
+    key = (dev.index, stream_handle(dev))
+    with _ws_lock:
+        cur = _gws.get(key)
+        if cur is None:
+            cur = torch.zeros(256, dtype=torch.uint8, device=dev)
+            _gws[key] = cur
+    return cur
+
+
+def gemm(x: torch.Tensor, w: torch.Tensor, s: torch.Tensor | None = None, N: int | None = None,
+         out: torch.Tensor | None = None) -> torch.Tensor:
+    """y[M, N] = x[M, K] @ W[N, K]^T on the tcgen05 tensor cores.  W is fp16
+    [N, K], or INT4 nibbles [N, K/2] with (scale, zero) pairs ``s`` [N, K/16]
+    (dequantised in the kernel, bit-exact to dequant_int4)."""
+    dev = _require_cuda(x, w)
+    x2 = x.reshape(-1, x.shape[-1])
+    if x2.stride(-1) != 1:
+        x2 = x2.contiguous()
+    M, K = x2.shape
+    N = int(w.shape[0]) if N is None else N
+    y = out if out is not None else torch.empty(M, N, dtype=torch.float16, device=dev)
+    ws = _status_ws(dev)
+    st = stream_handle(dev)
+    if s is None:
+        L.call("r4q_gemm_fp16", x2.data_ptr(), x2.stride(0), w.data_ptr(), y.data_ptr(), y.stride(0), M, N, K,
+               ws.data_ptr(), ws.numel(), st)
+    else:
+        L.call("r4q_gemm_int4", x2.data_ptr(), x2.stride(0), w.data_ptr(), s.data_ptr(), y.data_ptr(),
+               y.stride(0), M, N, K, ws.data_ptr(), ws.numel(), st)
+    return y
