@@ -5,11 +5,11 @@
 // and call rocBLAS (int4_prefill_logits, :2127-2320; int4_engine_v5.py:
 // 214-266):  Y[M, N] = X[M, K] · W[N, K]ᵀ, fp16 in, fp32 accumulate, fp16 out.
 //
-// B200 design (one 128 x 256 output tile per CTA, 4 warps):
+// B200 design (one 128 x 256 output tile per CTA, 8 warps):
 //  * warp 0, one lane: TMA producer.  X tiles [128 x 64] and W tiles
 //    [256 x 64] (fp16, K-major, 128-byte swizzle) into a 4-stage ring with
 //    mbarrier transaction counts;
-//  * INT4 weights (`w4` set): warps 2-3 dequantise instead of TMA-loading W:
+//  * INT4 weights (`w4` set): warps 2-7 dequantise instead of TMA-loading W:
 //    the nibbles come in by TMA, the (scale, zero) pairs by plain loads (8 bytes
 //    per row and stage, below TMA's 16-byte box minimum), the exact reference value
 //    fp16((q - z) · s) is written into the same swizzled fp16 layout, then
@@ -18,8 +18,8 @@
 //    N = 256, K = 16 per instruction, 4 per stage) from shared-memory matrix
 //    descriptors into a 128 x 256 fp32 accumulator in tensor memory, and
 //    tcgen05.commit releases each stage back to the producer;
-//  * all 4 warps: epilogue, tcgen05.ld of their 32 accumulator lanes (= rows),
-//    fp16 conversion, stores.
+//  * all 8 warps: epilogue, tcgen05.ld of their 32 accumulator lanes (= rows)
+//    and half of the columns, fp16 conversion, stores.
 // Every mbarrier wait is bounded; a timeout sets the status word and the
 // kernel drains.  No multicast anywhere.
 #include <cuda.h>
@@ -36,7 +36,8 @@ constexpr int kStages = 4;
 constexpr int kABytes = kBM * kBK * 2;             // 16 KB
 constexpr int kBBytes = kBN * kBK * 2;             // 32 KB
 constexpr int kW4Bytes = kBN * kBK / 2;            // 8 KB of nibbles per stage
-constexpr int kGemmThreads = 128;
+constexpr int kGemmThreads = 256;   // 8 warps
+constexpr int kDequantThreads = kGemmThreads - 64;
 constexpr long kGemmSpin = 1L << 26;
 
 struct GemmParams {
@@ -110,32 +111,47 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
 // the rows' (scale, zero) pairs of blocks 2 kt, 2 kt + 1 (8 bytes in global
 // memory) -> fp16 in the 128-byte swizzled K-major layout TMA would have
 // produced: element (r, k) at r * 128 + (((k >> 3) ^ (r & 7)) << 4) + (k & 7) * 2.
-// Thread t of the 64 dequant threads takes rows t, t + 64, ...; each row is 8
-// chunks of 8 k.  Rows past N (zero nibbles) get zero pairs.
+// The dequant threads take (row, 8-k chunk) items.  Exact reference value:
+// OR-ing a nibble into 0x6400 gives the fp16 1024 + q; subtracting the fp16
+// 1024 + z is exact (both integers below 2048), and the one fp16 multiply by s
+// rounds (q - z) · s once, as dequantize_int4_asym does.  Rows past N get
+// zero pairs.
 __device__ __forceinline__ void dequant_stage(const uint8_t* w4, const uint8_t* sz, long ld_sz, int n0, int N,
-                                              int kt, uint8_t* bdst, int t) {
-  for (int r = t; r < kBN; r += 64) {
-    const uint4 q0 = *reinterpret_cast<const uint4*>(w4 + r * 32);
-    const uint4 q1 = *reinterpret_cast<const uint4*>(w4 + r * 32 + 16);
-    const uint32_t qw[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
-    const uint2 pz = (n0 + r < N) ? __ldg(reinterpret_cast<const uint2*>(sz + (long)(n0 + r) * ld_sz + kt * 8))
-                                  : make_uint2(0u, 0u);
+                                              int kt, uint8_t* bdst, int t, int nthr) {
+  // all loads of this thread's items first (the pair loads go to L2: issuing
+  // them together keeps one round trip per stage instead of one per item)
+  constexpr int kItems = (kBN * 8 + kDequantThreads - 1) / kDequantThreads;
+  uint32_t wqs[kItems], prs[kItems];
 #pragma unroll
-    for (int c = 0; c < 8; ++c) {                        // 8 k per chunk = 4 bytes of nibbles
-      const uint32_t pair = (c < 4) ? pz.x : pz.y;        // block 0: k 0..31, block 1: k 32..63
-      const __half2 szh = u32_as_h2(pair);
-      const __half s = __low2half(szh), z = __high2half(szh);
-      const uint32_t wq = qw[c];
-      uint32_t o[4];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const uint32_t byte = (wq >> (8 * j)) & 0xFFu;
-        const __half lo = __ushort2half_rn((unsigned short)(byte & 0xFu));
-        const __half hi = __ushort2half_rn((unsigned short)(byte >> 4));
-        o[j] = h2_as_u32(__halves2half2(__hmul(__hsub(lo, z), s), __hmul(__hsub(hi, z), s)));
-      }
-      *reinterpret_cast<uint4*>(bdst + r * 128 + ((c ^ (r & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+  for (int i = 0; i < kItems; ++i) {
+    const int item = t + i * nthr;
+    const int r = item >> 3, c = item & 7;
+    wqs[i] = 0u;
+    prs[i] = 0u;
+    if (item < kBN * 8) {
+      wqs[i] = *reinterpret_cast<const uint32_t*>(w4 + r * 32 + c * 4);
+      if (n0 + r < N)
+        prs[i] = __ldg(reinterpret_cast<const uint32_t*>(sz + (long)(n0 + r) * ld_sz + kt * 8 + (c >> 2) * 4));
     }
+  }
+#pragma unroll
+  for (int i = 0; i < kItems; ++i) {
+    const int item = t + i * nthr;
+    if (item >= kBN * 8) break;
+    const int r = item >> 3, c = item & 7;               // chunk c: k = 8c .. 8c+7
+    const uint32_t wq = wqs[i];
+    const uint32_t pair = prs[i];
+    const __half2 szh = u32_as_h2(pair);
+    const __half2 s2 = __half2half2(__low2half(szh));
+    const __half2 z2 = __hadd2(__half2half2(__high2half(szh)), __float2half2_rn(1024.0f));
+    // (k0, k4), (k1, k5), (k2, k6), (k3, k7) as 1024 + q
+    const __half2 a = __hmul2(__hsub2(u32_as_h2(lop3_and_or(wq, 0x000F000Fu, 0x64006400u)), z2), s2);
+    const __half2 b = __hmul2(__hsub2(u32_as_h2(lop3_and_or(wq >> 4, 0x000F000Fu, 0x64006400u)), z2), s2);
+    const __half2 cc = __hmul2(__hsub2(u32_as_h2(lop3_and_or(wq >> 8, 0x000F000Fu, 0x64006400u)), z2), s2);
+    const __half2 d = __hmul2(__hsub2(u32_as_h2(lop3_and_or(wq >> 12, 0x000F000Fu, 0x64006400u)), z2), s2);
+    const uint4 o = make_uint4(h2_as_u32(__lows2half2(a, b)), h2_as_u32(__lows2half2(cc, d)),
+                               h2_as_u32(__highs2half2(a, b)), h2_as_u32(__highs2half2(cc, d)));
+    *reinterpret_cast<uint4*>(bdst + r * 128 + ((c ^ (r & 7)) << 4)) = o;
   }
 }
 
@@ -163,7 +179,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       g_mbar_init(&full[s], 1);
       g_mbar_init(&empty[s], 1);
       g_mbar_init(&w4full[s], 1);
-      g_mbar_init(&bready[s], 64);
+      g_mbar_init(&bready[s], kDequantThreads);
     }
     g_mbar_init(accum, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -215,7 +231,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     umma_commit(accum);
   } else if (warp >= 2 && p.w4) {
-    // ---- INT4 dequantisers (64 threads)
+    // ---- INT4 dequantisers (warps 2-7)
     const int t = tid - 64;
     bool ok = true;
     for (int kt = 0; kt < KT; ++kt) {
@@ -224,21 +240,23 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       if (ok) ok = g_wait(&w4full[s], ph, p.status);
       // the fp16 slot was last read by the MMAs of stage kt - kStages
       if (ok && kt >= kStages) ok = g_wait(&empty[s], ((kt / kStages) - 1) & 1, p.status);
-      if (ok) dequant_stage(sw4 + s * kW4Bytes, p.sz, p.K / 8, n0, p.N, kt, sb + s * kBBytes, t);
+      if (ok) dequant_stage(sw4 + s * kW4Bytes, p.sz, p.K / 8, n0, p.N, kt, sb + s * kBBytes, t, kDequantThreads);
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       g_arrive(&bready[s]);
     }
   }
 
-  // ---- epilogue: warp w owns accumulator lanes (rows) 32w..32w+31
+  // ---- epilogue: warp w owns accumulator lanes (rows) 32 (w % 4) .. + 31
+  //      and columns 128 (w / 4) .. + 127
   __syncwarp();
   const bool ok = g_wait(accum, 0, p.status);
   asm volatile("tcgen05.fence::after_thread_sync;");
-  const int row = m0 + warp * 32 + lane;
+  const int quarter = warp & 3, half = warp >> 2;
+  const int row = m0 + quarter * 32 + lane;
 #pragma unroll 1
-  for (int c0 = 0; c0 < kBN; c0 += 32) {
+  for (int c0 = half * (kBN / 2); c0 < (half + 1) * (kBN / 2); c0 += 32) {
     uint32_t v[32];
-    const uint32_t taddr = tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0;
+    const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)c0;
     asm volatile(
         "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
         "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
