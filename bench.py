@@ -54,6 +54,8 @@ def parse():
     ap.add_argument("--decode-ctx", default="128,2048",
                     help="prompt lengths for the Qwen3-14B decode tok/s measurement ('' skips it)")
     ap.add_argument("--decode-tokens", type=int, default=256)
+    ap.add_argument("--prefill-tokens", type=int, default=512,
+                    help="prompt length of the prefill tok/s measurement (0 skips it)")
     ap.add_argument("--decode-probe", action="store_true",
                     help="build the 40-layer model, decode 3 tokens eagerly and exit (for ncu)")
     ap.add_argument("--kernel-probe", default=None, choices=[n for n, *_ in LAYER_SHAPES],
@@ -434,6 +436,9 @@ def decode_tok_s(a, dev, peak, ws=1, rank=0):
                     "bytes_per_token_per_gpu": byt, "GBps_per_gpu": round(byt / ms / 1e6, 1),
                     "roofline_tok_s": round(peak * 1e9 / byt, 1),
                     "frac": round((byt / ms / 1e6) / peak, 4)})
+    pre = None
+    if ws == 1 and a.prefill_tokens:
+        pre = prefill_tok_s(a, dev, m, cfg)
     if dec is not None:
         dec = None
         from r4q import decode
@@ -447,7 +452,43 @@ def decode_tok_s(a, dev, peak, ws=1, rank=0):
                     "= step + device argmax + embedding lookup" if ws == 1 else
                     "r4q.tp.TPDecoder.loop: one CUDA-graph launch per token per rank (NVLink P2P "
                     "exchanges fused into the GEMVs) + device argmax + embedding lookup"),
-            "results": res}
+            "results": res, "prefill": pre}
+
+
+def prefill_tok_s(a, dev, m, cfg):
+    """Prompt processing (pp) of `prefill_tokens` tokens through
+    int4_hip.prefill_logits (tcgen05 GEMM for every projection, logits for
+    every position as the reference returns), timed with CUDA events."""
+    import torch
+    from r4q import prefill
+    M = a.prefill_tokens
+    gen = torch.Generator(device=dev).manual_seed(5)
+    ids = torch.randint(0, cfg['vocab'], (M,), generator=gen, device=dev)
+
+    def run():
+        x = m['embed'][ids]
+        return prefill.prefill_logits(x, m['qkv_w'], m['qkv_s'], m['o_w'], m['o_s'], m['gu_w'], m['gu_s'],
+                                      m['down_w'], m['down_s'], m['in_norm_w'], m['post_norm_w'], m['q_norm_w'],
+                                      m['k_norm_w'], m['rope_cos'], m['rope_sin'], cfg['num_heads'],
+                                      cfg['num_kv_heads'], cfg['head_dim'], cfg['hidden'], cfg['intermediate'],
+                                      cfg['rms_eps'], m['final_norm_w'], m['lm_w'], m['lm_s'], cfg['vocab'])
+    for _ in range(2):
+        run()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 3
+    e0.record()
+    for _ in range(reps):
+        run()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    L, D, I, H, Hk, hd = (cfg['num_layers'], cfg['hidden'], cfg['intermediate'], cfg['num_heads'],
+                          cfg['num_kv_heads'], cfg['head_dim'])
+    flops = 2 * M * (L * (D * (H + 2 * Hk) * hd + H * hd * D + D * 2 * I + I * D) + D * cfg['vocab'])
+    return {"tokens": M, "ms": round(ms, 3), "tok_s": round(M * 1e3 / ms, 1),
+            "gemm_TFLOPs": round(flops / ms / 1e9, 1),
+            "api": "int4_hip.prefill_logits (r4q.prefill): tcgen05 GEMM per projection, torch SDPA attention"}
 
 
 def kernel_probe(a):

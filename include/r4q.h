@@ -193,6 +193,13 @@ int r4q_gemm_fp16(const void* x, long ldx, const void* w, void* y, long ldy, int
 int r4q_gemm_int4(const void* x, long ldx, const void* w, const void* sz, void* y, long ldy, int M, int N,
                   int K, void* workspace, size_t ws_bytes, void* stream);
 
+/* Row kernels of the batched prefill (int4_decode_step.hip:766-792, 2112-2124):
+ * y = fp16(H32 x) on every 32-block of rows x K; y = fp16(silu(g) * u) with
+ * g = x[:, :I], u = x[:, I:2I]; INT8 weights to fp16 (int8_quant.py:52-69). */
+int r4q_fwht_rows(const void* x, long ldx, void* y, long ldy, int rows, int K, void* stream);
+int r4q_silu_mul(const void* x, long ldx, void* y, long ldy, int rows, int I, void* stream);
+int r4q_dequant_int8(const void* w, const void* s, void* out, int N, int K, void* stream);
+
 /* ------------------------------------------------------------- decode step --- */
 /* One transformer layer's weights and caches (device pointers).  *_fmt is
  * R4Q_W_INT4 (packed [N, K/2] + (scale, zero) pairs [N, K/16]) or R4Q_W_INT8

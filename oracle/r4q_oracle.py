@@ -532,3 +532,74 @@ def decode_step_logits(h, layers, cfg, kcs, vcs, pos, cos, sin, final_norm, lm, 
     h = decode_step(h, layers, cfg, kcs, vcs, pos, cos, sin, write_kv)
     rot = rmsnorm_fwht(h, final_norm, cfg['rms_eps'])
     return linear(rot, lm), h
+
+
+# --------------------------------------------------------------------------
+# Batched prefill  (int4_prefill_logits, int4_decode_step.hip:2127-2320)
+# --------------------------------------------------------------------------
+def causal_attention(q, k, v):
+    """softmax(q kᵀ / sqrt(D)) v over positions <= the query's, GQA; q fp16
+    [M, H, D], k/v fp16 [M, Hk, D] -> fp16 [M, H, D] (float64 inside): the
+    role SDPA(is_causal=True, enable_gqa=True) plays at :2268-2277."""
+    qf = np.asarray(q, np.float16).astype(np.float64)
+    kf = np.asarray(k, np.float16).astype(np.float64)
+    vf = np.asarray(v, np.float16).astype(np.float64)
+    M, H, D = qf.shape
+    G = H // kf.shape[1]
+    kf = np.repeat(kf, G, axis=1)
+    vf = np.repeat(vf, G, axis=1)
+    s = np.einsum('mhd,nhd->hmn', qf, kf) / np.sqrt(D)
+    mask = np.triu(np.ones((M, M), bool), 1)
+    s[:, mask] = -np.inf
+    s = s - s.max(-1, keepdims=True)
+    p = np.exp(s)
+    p /= p.sum(-1, keepdims=True)
+    return np.einsum('hmn,nhd->mhd', p, vf).astype(np.float16)
+
+
+def prefill_logits(x, layers, cfg, cos, sin, final_norm, lm):
+    """``int4_prefill_logits`` for hidden rows x fp16 [M, D] (the embedding of
+    the prompt) at positions 0..M-1: per layer rmsnorm -> H32 -> qkv ->
+    head norm + RoPE -> causal attention -> H32 -> o -> residual + norm ->
+    H32 -> gate_up -> fp16(silu·up) -> H32 -> down -> residual + next norm;
+    every stage rounds to fp16 where the reference's kernels do.  No KV cache
+    is written (the reference prefill writes none).  Returns logits fp16
+    [M, vocab]."""
+    H, Hk, hd, I, eps = (cfg['num_heads'], cfg['num_kv_heads'], cfg['head_dim'],
+                         cfg['intermediate_size'], cfg['rms_eps'])
+    x = np.asarray(x, np.float16)
+    M = x.shape[0]
+    qd, kd = H * hd, Hk * hd
+    normed = rmsnorm(x, layers[0]['in_norm'], eps)
+    for li, ly in enumerate(layers):
+        qkv = linear(fwht32(normed.astype(np.float32)).astype(np.float16), ly['qkv'])
+        q = qkv[:, :qd].reshape(M, H, hd)
+        k = qkv[:, qd:qd + kd].reshape(M, Hk, hd)
+        v = qkv[:, qd + kd:qd + 2 * kd].reshape(M, Hk, hd)
+        qn = np.stack([head_norm_rope(q[m], ly['q_norm'], cos[m], sin[m], eps) for m in range(M)]).astype(np.float16)
+        kn = np.stack([head_norm_rope(k[m], ly['k_norm'], cos[m], sin[m], eps) for m in range(M)]).astype(np.float16)
+        att = causal_attention(qn, kn, v).reshape(M, qd)
+        o = linear(fwht32(att.astype(np.float32)).astype(np.float16), ly['o'])
+        r = (o.astype(np.float32) + x.astype(np.float32))
+        normed = rmsnorm_unrounded(r, ly['post_norm'], eps)
+        r16 = r.astype(np.float16)
+        gu = linear(fwht32(normed.astype(np.float32)).astype(np.float16), ly['gate_up'])
+        g = gu[:, :I].astype(np.float64)
+        act = (g / (1.0 + np.exp(-g)) * gu[:, I:2 * I].astype(np.float64)).astype(np.float32).astype(np.float16)
+        d = linear(fwht32(act.astype(np.float32)).astype(np.float16), ly['down'])
+        xr = d.astype(np.float32) + r16.astype(np.float32)
+        nxt = layers[li + 1]['in_norm'] if li + 1 < len(layers) else layers[0]['in_norm']
+        normed = rmsnorm_unrounded(xr, nxt, eps)
+        x = xr.astype(np.float16)
+    n = rmsnorm(x, final_norm, eps)
+    return linear(fwht32(n.astype(np.float32)).astype(np.float16), lm)
+
+
+def rmsnorm_unrounded(r, w, eps):
+    """fused_res_norm_batched (:2017-2052): rrms from the fp32 sum r (not
+    rounded first), y = fp16(r * rrms * w)."""
+    rf = np.asarray(r, np.float32)
+    D = rf.shape[-1]
+    ss = (rf.astype(np.float64) ** 2).sum(-1, keepdims=True)
+    rrms = (1.0 / np.sqrt(ss / D + eps)).astype(np.float32)
+    return (rf * rrms * np.asarray(w, np.float16).astype(np.float32)).astype(np.float16)

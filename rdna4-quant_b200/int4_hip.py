@@ -186,3 +186,19 @@ def decode_profile(hidden_in, embed_weight, qkv_w, qkv_s, qkv_N, o_w, o_s, o_N, 
                          head_dim, hidden_size, intermediate_size, rms_eps, k_caches, v_caches,
                          final_norm_w, lm_w, lm_s, lm_N)
     return ctx.profile(h, start_pos)
+
+
+def prefill_logits(input_ids, embed_weight, final_norm_w, lm_w, lm_s, lm_N, lm_K, qkv_w, qkv_s, qkv_N,
+                   o_w, o_s, o_N, gu_w, gu_s, gu_N, down_w, down_s, down_N, in_norm_w, post_norm_w,
+                   q_norm_w, k_norm_w, rope_cos, rope_sin, num_heads, num_kv_heads, head_dim,
+                   hidden_size, intermediate_size, rms_eps, hadamard_mat=None):
+    """All layers over the prompt ``input_ids`` [M] -> logits [M, lm_N] fp16
+    (int4_decode_step.hip:2127-2320), projections on the tcgen05 GEMM.
+    Weights per layer may be INT4, INT8 or fp16; ``hadamard_mat`` is accepted
+    and unused, as in the reference."""
+    from r4q import prefill as _pf
+    x = embed_weight[input_ids.reshape(-1).to(embed_weight.device)]
+    return _pf.prefill_logits(x, qkv_w, qkv_s, o_w, o_s, gu_w, gu_s, down_w, down_s, in_norm_w,
+                              post_norm_w, q_norm_w, k_norm_w, rope_cos, rope_sin, num_heads,
+                              num_kv_heads, head_dim, hidden_size, intermediate_size, rms_eps,
+                              final_norm_w, lm_w, lm_s, lm_N)

@@ -230,3 +230,31 @@ def gemm(x: torch.Tensor, w: torch.Tensor, s: torch.Tensor | None = None, N: int
         L.call("r4q_gemm_int4", x2.data_ptr(), x2.stride(0), w.data_ptr(), s.data_ptr(), y.data_ptr(),
                y.stride(0), M, N, K, ws.data_ptr(), ws.numel(), st)
     return y
+
+
+def fwht_rows(x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """fp16(H32 x) on every 32-element block of each row (hadamard_rotate_batched)."""
+    dev = _require_cuda(x)
+    x2 = x.reshape(-1, x.shape[-1])
+    y = out if out is not None else torch.empty_like(x2)
+    L.call("r4q_fwht_rows", x2.data_ptr(), x2.stride(0), y.data_ptr(), y.stride(0), x2.shape[0], x2.shape[1],
+           stream_handle(dev))
+    return y
+
+
+def silu_mul(x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """fp16(silu(x[:, :I]) * x[:, I:]) (silu_mul_batched)."""
+    dev = _require_cuda(x)
+    I = x.shape[-1] // 2
+    y = out if out is not None else torch.empty(x.shape[0], I, dtype=torch.float16, device=dev)
+    L.call("r4q_silu_mul", x.data_ptr(), x.stride(0), y.data_ptr(), y.stride(0), x.shape[0], I,
+           stream_handle(dev))
+    return y
+
+
+def dequant_int8(w: torch.Tensor, s: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    dev = _require_cuda(w, s)
+    N, K = w.shape
+    y = out if out is not None else torch.empty(N, K, dtype=torch.float16, device=dev)
+    L.call("r4q_dequant_int8", w.data_ptr(), s.data_ptr(), y.data_ptr(), N, K, stream_handle(dev))
+    return y
