@@ -58,6 +58,8 @@ def parse():
                     help="prompt length of the prefill tok/s measurement (0 skips it)")
     ap.add_argument("--decode-probe", action="store_true",
                     help="build the 40-layer model, decode 3 tokens eagerly and exit (for ncu)")
+    ap.add_argument("--gemm-probe", action="store_true",
+                    help="run the INT4 tcgen05 prefill GEMM (M=512, qkv shape) 4 times and exit (for ncu)")
     ap.add_argument("--kernel-probe", default=None, choices=[n for n, *_ in LAYER_SHAPES],
                     help="run one GEMV of this shape 4 times and exit (for ncu captures)")
     return ap.parse_args()
@@ -531,9 +533,25 @@ def decode_probe(a):
     print("decode probe ok")
 
 
+def gemm_probe(a):
+    """Four INT4 prefill GEMMs, M = 512, qkv shape (7168 x 5120), for ncu."""
+    import torch
+    from r4q import ops, synth
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(0)
+    _, w, sc = synth.linear_int4(QKV_N, HID, g, dev)
+    x = torch.randn(512, HID, device=dev, generator=g).half()
+    for _ in range(4):
+        ops.gemm(x, w, sc, QKV_N)
+    torch.cuda.synchronize()
+    print("gemm probe ok")
+
+
 if __name__ == "__main__":
     args = parse()
-    if args.decode_probe:
+    if args.gemm_probe:
+        gemm_probe(args)
+    elif args.decode_probe:
         decode_probe(args)
     elif args.kernel_probe:
         kernel_probe(args)
