@@ -58,6 +58,9 @@ def parse():
                     help="prompt length of the prefill tok/s measurement (0 skips it)")
     ap.add_argument("--decode-probe", action="store_true",
                     help="build the 40-layer model, decode 3 tokens eagerly and exit (for ncu)")
+    ap.add_argument("--moe-batches", default="1,16,64",
+                    help="batches of the config-4 MoE decode measurement ('' skips it)")
+    ap.add_argument("--moe-tokens", type=int, default=32)
     ap.add_argument("--gemm-probe", action="store_true",
                     help="run the INT4 tcgen05 prefill GEMM (M=512, qkv shape) 4 times and exit (for ncu)")
     ap.add_argument("--kernel-probe", default=None, choices=[n for n, *_ in LAYER_SHAPES],
@@ -333,6 +336,9 @@ def main_ours(a):
         del layers
         torch.cuda.empty_cache()
         line["decode"] = decode_tok_s(a, dev, peak, ws, rank)
+    if a.moe_batches and ws == 1:
+        torch.cuda.empty_cache()
+        line["moe"] = moe_tok_s(a, dev, peak)
     if rank == 0 and ws == 1 and not a.no_cpu_baseline:
         threads = os.cpu_count() or 1
         setup = cpu_port_setup(B)
@@ -408,9 +414,22 @@ def decode_tok_s(a, dev, peak, ws=1, rank=0):
     res = []
     from r4q import decode as rdec
     for ctx in ctxs:
-        synth.fill_kv_synthetic(m, ctx, seed=ctx)
         gen = torch.Generator(device=dev).manual_seed(ctx)
-        tok = torch.randint(0, cfg['vocab'], (1,), generator=gen, device=dev)
+        if ws == 1:
+            # the prompt through the prefill path: its K/V fill positions 0..ctx-1
+            from r4q import prefill as rpre
+            ids = torch.randint(0, cfg['vocab'], (ctx,), generator=gen, device=dev)
+            last = rpre.prefill_logits(m['embed'][ids], m['qkv_w'], m['qkv_s'], m['o_w'], m['o_s'], m['gu_w'],
+                                       m['gu_s'], m['down_w'], m['down_s'], m['in_norm_w'], m['post_norm_w'],
+                                       m['q_norm_w'], m['k_norm_w'], m['rope_cos'], m['rope_sin'],
+                                       cfg['num_heads'], cfg['num_kv_heads'], cfg['head_dim'], cfg['hidden'],
+                                       cfg['intermediate'], cfg['rms_eps'], m['final_norm_w'], m['lm_w'], m['lm_s'],
+                                       cfg['vocab'], k_caches=m['k_caches'], v_caches=m['v_caches'],
+                                       last_only=True)
+            tok = last.reshape(-1).argmax().reshape(1)
+        else:
+            synth.fill_kv_synthetic(m, ctx, seed=ctx)
+            tok = torch.randint(0, cfg['vocab'], (1,), generator=gen, device=dev)
         h0 = m['embed'][tok].reshape(1, -1).contiguous()
         if dec is not None:
             loop = lambda start, n: dec.loop(m['embed'], h0, start, n)
@@ -454,7 +473,8 @@ def decode_tok_s(a, dev, peak, ws=1, rank=0):
         comm.close()
     return {"model": "Qwen3-14B shape, random init", "int8_groups": int8_groups,
             "lm_head": "fp16", "batch": 1, "tokens": a.decode_tokens, "tp": ws,
-            "kv": "prompt K/V pre-filled with seeded FP8 values (no prefill compute)",
+            "kv": ("prompt of seeded random ids through prefill_logits (writes K/V of positions 0..ctx-1)"
+                   if ws == 1 else "prompt K/V pre-filled with seeded FP8 values (prefill is single-GPU)"),
             "api": ("r4q decode_loop (int4_hip.decode_loop's engine): one CUDA-graph launch per token "
                     "= step + device argmax + embedding lookup" if ws == 1 else
                     "r4q.tp.TPDecoder.loop: one CUDA-graph launch per token per rank (NVLink P2P "
@@ -496,6 +516,47 @@ def prefill_tok_s(a, dev, m, cfg):
     return {"tokens": M, "ms": round(ms, 3), "tok_s": round(M * 1e3 / ms, 1),
             "gemm_TFLOPs": round(flops / ms / 1e9, 1),
             "api": "int4_hip.prefill_logits (r4q.prefill): tcgen05 GEMM per projection, torch SDPA attention"}
+
+
+def moe_tok_s(a, dev, peak):
+    """BASELINE config 4 on one GPU: 48-layer Qwen3-30B-A3B-shaped MoE decode
+    (random init, INT4 experts, top-8 of 128), KV cache of ctx 2048 filled
+    with seeded FP8 values, batches from --moe-batches; each token one
+    CUDA-graph replay of the whole step (routing on the device).  Bytes per
+    step count the dense weights, the router, the lm_head, the KV read and
+    the distinct experts the step's routing selects (expected count for
+    uniform routing: E (1 - (1 - k/E)^B) per layer)."""
+    import torch
+    from r4q import moe, synth
+    cfg = moe.qwen3_30b_a3b_config()
+    bs = [int(b) for b in a.moe_batches.split(",") if b]
+    ctx, steps = 2048, a.moe_tokens
+    m = moe.build_moe_model(cfg, dev, seed=11, max_seq=ctx + steps + 16, batch=max(bs))
+    synth.fill_kv_synthetic(m, ctx, seed=5)
+    E, k, D = cfg['experts'], cfg['topk'], cfg['hidden']
+    res = []
+    for B in bs:
+        dec = moe.MoEDecoder(m, cfg, batch=B)
+        h = m['embed'][torch.arange(B, device=dev) * 31 + 1]
+        for w in range(3):
+            dec.step(h, ctx + w)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for t in range(steps):
+            dec.step(h, ctx + t)
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / steps
+        distinct = E * (1 - (1 - k / E) ** B)
+        byt = int(m['dense_weight_bytes'] + cfg['num_layers'] * (E * D * 2 + moe.expert_bytes(cfg, 1) * distinct)
+                  + 2 * cfg['vocab'] * D + cfg['num_layers'] * 2 * B * cfg['num_kv_heads'] * 128 * (ctx + steps // 2))
+        res.append({"batch": B, "tok_s": round(B * 1e3 / ms, 1), "ms_per_step": round(ms, 4),
+                    "bytes_per_step": byt, "GBps": round(byt / ms / 1e6, 1), "frac": round(byt / ms / 1e6 / peak, 4)})
+        del dec
+    return {"model": "Qwen3-30B-A3B shape (48 layers, 128 experts, top-8), random init, INT4 experts",
+            "ctx": ctx, "tokens": steps, "gpus": 1, "results": res,
+            "api": "r4q.moe.MoEDecoder.step (one CUDA graph per step: router, top-k, grouped expert GEMVs)"}
 
 
 def kernel_probe(a):

@@ -199,6 +199,45 @@ int r4q_gemm_int4(const void* x, long ldx, const void* w, const void* sz, void* 
 int r4q_fwht_rows(const void* x, long ldx, void* y, long ldy, int rows, int K, void* stream);
 int r4q_silu_mul(const void* x, long ldx, void* y, long ldy, int rows, int I, void* stream);
 int r4q_dequant_int8(const void* w, const void* s, void* out, int N, int K, void* stream);
+/* Prompt K/V into the FP8 cache: rows m of k, v (fp16, row stride ld, Hk heads
+ * of D = 128) to cache[batch_row][h][start_pos + m] with the reference encoder
+ * (divided by the optional per-head scales).  The reference prefill writes no
+ * cache; this lets a prefilled prompt feed the decode step. */
+int r4q_kv_write_rows(const void* k, const void* v, long ld, void* k_cache, void* v_cache, int M, int Hk, int D,
+                      int max_seq, int start_pos, int batch_row, const float* k_scale, const float* v_scale,
+                      void* stream);
+
+/* ------------------------------------------------- mixture-of-experts FFN --- */
+/* No counterpart in the reference (its engine is dense); BASELINE config 4.
+ * Routing: per token softmax over router logits fp16 [B, E] (fp32), top-k
+ * (ties to the lower expert), weights renormalised over the k -> ids int32
+ * [B, topk], wts fp32 [B, topk]; entries t * topk + k grouped by expert in
+ * token order: counts [E], offsets [E + 1], list [B * topk], active [E]
+ * (experts with tokens in [e_lo, e_hi), ascending — this GPU's slice under
+ * expert parallelism), n_active [1].  E <= 256, topk <= 16. */
+int r4q_moe_route(const void* logits, int B, int E, int topk, int e_lo, int e_hi, int* ids, float* wts,
+                  int* counts, int* offsets, int* list, int* active, int* n_active, void* stream);
+/* y[b] = fp16(H32(x[b] * rrms * w)) per 32-block, rrms from ss_in partials
+ * ([ss_parts][rows]) or from x: the RMSNorm+FWHT prologue as its own pass. */
+int r4q_norm_fwht_rows(const void* x, const float* ss_in, int ss_parts, const void* w, float eps, void* y,
+                       int rows, int D, void* stream);
+/* Grouped INT4 expert GEMV over the routed entries of experts [e_lo, e_hi)
+ * (the active list of r4q_moe_route).  This GPU's experts stacked: w
+ * [(e_hi - e_lo) * N, K/2], sz [(e_hi - e_lo) * N, K/16].  mode 0: y[j] = W_e · x[j / topk] (x rows of
+ * K); mode 1: y[j] = W_e · fp16(H32(silu(g) u)), g, u = halves of x[j] (rows
+ * of 2K).  y rows of N fp16 (ldy), one per entry j. */
+int r4q_moe_gemv(int mode, const void* w, const void* sz, const void* x, long ldx, void* y, long ldy, int N,
+                 int K, int E, int e_lo, int e_hi, int B, int topk, const int* counts, const int* offsets,
+                 const int* list, const int* active, const int* n_active, void* stream);
+/* Over the entries of experts [e_lo, e_hi): h[b] = fp16(fp16(sum_k wts[b,k]
+ * y[b*topk+k]) + res[b]) in slot order with ss_out [D/16][B] the sums of
+ * squares of the unrounded h (res may alias h); or, with out32, the fp32
+ * partial sum alone (expert parallelism: summed over GPUs, then
+ * r4q_residual_f32). */
+int r4q_moe_combine(const void* y, const float* wts, const int* ids, int e_lo, int e_hi, const void* res, void* h,
+                    float* out32, float* ss_out, int B, int D, int topk, void* stream);
+/* h = fp16(fp16(sum) + res) and its per-16-row sums of squares, sum fp32 [B, D]. */
+int r4q_residual_f32(const float* sum, const void* res, void* h, float* ss_out, int B, int D, void* stream);
 
 /* ------------------------------------------------------------- decode step --- */
 /* One transformer layer's weights and caches (device pointers).  *_fmt is

@@ -603,3 +603,34 @@ def rmsnorm_unrounded(r, w, eps):
     ss = (rf.astype(np.float64) ** 2).sum(-1, keepdims=True)
     rrms = (1.0 / np.sqrt(ss / D + eps)).astype(np.float32)
     return (rf * rrms * np.asarray(w, np.float16).astype(np.float32)).astype(np.float16)
+
+
+# --------------------------------------------------------------------------
+# Mixture-of-experts FFN (no reference counterpart — the
+# composition the B200 MoE kernels implement, built from the dense path's
+# pieces: routing softmax in fp32, top-k, renormalised weights; experts as
+# the dense gate_up / silu·up+FWHT / down chain; weighted sum, residual).
+# --------------------------------------------------------------------------
+def moe_route(logits, topk):
+    """logits fp16 [B, E] -> (ids [B, topk], wts [B, topk]): softmax over E in
+    float64, top-k by value (ties to the lower index), renormalised."""
+    lg = np.asarray(logits, np.float16).astype(np.float64)
+    p = np.exp(lg - lg.max(-1, keepdims=True))
+    p /= p.sum(-1, keepdims=True)
+    order = np.argsort(-lg, axis=-1, kind='stable')[:, :topk]
+    w = np.take_along_axis(p, order, -1)
+    return order, w / w.sum(-1, keepdims=True)
+
+
+def moe_expert(rot_row, gu, down, Ie):
+    """One token through one INT4 expert: fp16(W_d · fp16(H32(silu(g) u)))."""
+    g = linear(rot_row[None], gu)
+    act = silu_fwht(g[:, :Ie], g[:, Ie:2 * Ie])
+    return linear(act, down)[0]
+
+
+def moe_combine(ys, wts, r16):
+    """h = fp16(fp16(sum_k w_k y_k) + r) with y_k fp16 [topk, D]."""
+    s = (np.asarray(wts, np.float64)[:, None] * np.asarray(ys, np.float16).astype(np.float64)).sum(0)
+    return (s.astype(np.float16).astype(np.float32) + np.asarray(r16, np.float16).astype(np.float32)).astype(
+        np.float16)

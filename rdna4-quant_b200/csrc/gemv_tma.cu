@@ -744,7 +744,13 @@ static TmaPlan plan_tma(int B, int N, int K, size_t ws_bytes) {
   const size_t smem_limit = tma_smem_limit<FMT, NG, DIAG>();
   TmaPlan best{1, 1, 0, 0, 0, 0};
   double best_cost = 1e30;
+  // R4Q_GEMV_SPLIT forces the K split count (measurement only)
+  static const int forced_split = [] {
+    const char* e = getenv("R4Q_GEMV_SPLIT");
+    return e ? atoi(e) : 0;
+  }();
   for (int S = 1; S <= kTmaMaxSplit && S <= nst; ++S) {
+    if (forced_split > 0 && S != forced_split && forced_split <= nst) continue;
     const int gt = nsm / S;
     if (gt < 1) break;
     if (S > 1 && gemv_ws_bytes_for(B, N, S) > ws_bytes) break;

@@ -88,3 +88,47 @@ extern "C" int r4q_dequant_int8(const void* w, const void* s, void* out, int N, 
       (const int8_t*)w, (const __half*)s, (__half*)out, n8, K);
   return check_launch("dequant_int8_kernel");
 }
+
+namespace r4q {
+namespace {
+// cache[row b][kv head h][start + m][d] = enc(k[m, h, d] / s) for the M prompt
+// rows of batch row b (k, v: rows m with stride ld, kv heads of 128 contiguous).
+__global__ void kv_write_rows_kernel(const __half* __restrict__ k, const __half* __restrict__ v, long ld,
+                                     uint8_t* __restrict__ kc, uint8_t* __restrict__ vc, int M, int Hk,
+                                     int max_seq, int start, int b, const float* ks, const float* vs) {
+  const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;      // one thread per 4 elements
+  const long n = (long)M * Hk * 32;
+  if (i >= n) return;
+  const int d4 = (int)(i & 31);
+  const long mh = i >> 5;
+  const int h = (int)(mh % Hk);
+  const int m = (int)(mh / Hk);
+  const float sk = ks ? ks[b * Hk + h] : 1.0f, sv = vs ? vs[b * Hk + h] : 1.0f;
+  const long src = (long)m * ld + (long)h * 128 + d4 * 4;
+  const long dst = (((long)b * Hk + h) * max_seq + start + m) * 128 + d4 * 4;
+  uint32_t ko = 0, vo = 0;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float kf = __half2float(k[src + j]), vf = __half2float(v[src + j]);
+    ko |= fp8_encode(ks ? kf / sk : kf) << (8 * j);
+    vo |= fp8_encode(vs ? vf / sv : vf) << (8 * j);
+  }
+  *reinterpret_cast<uint32_t*>(kc + dst) = ko;
+  *reinterpret_cast<uint32_t*>(vc + dst) = vo;
+}
+}  // namespace
+}  // namespace r4q
+
+extern "C" int r4q_kv_write_rows(const void* k, const void* v, long ld, void* k_cache, void* v_cache, int M, int Hk,
+                                 int D, int max_seq, int start_pos, int batch_row, const float* k_scale,
+                                 const float* v_scale, void* stream) {
+  if (!k || !v || !k_cache || !v_cache || M < 0 || Hk < 1 || D != 128 || batch_row < 0 || start_pos < 0 ||
+      start_pos + M > max_seq)
+    return set_error(R4Q_ERR_ARG, "kv_write_rows: bad arguments (M %d start %d max_seq %d)", M, start_pos, max_seq);
+  if (M == 0) return R4Q_OK;
+  const long n = (long)M * Hk * 32;
+  kv_write_rows_kernel<<<(unsigned)((n + 255) / 256), 256, 0, (cudaStream_t)stream>>>(
+      (const __half*)k, (const __half*)v, ld, (uint8_t*)k_cache, (uint8_t*)v_cache, M, Hk, max_seq, start_pos,
+      batch_row, k_scale, v_scale);
+  return check_launch("kv_write_rows_kernel");
+}

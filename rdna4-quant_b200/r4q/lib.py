@@ -85,6 +85,13 @@ _SIGS = {
     "r4q_fwht_rows": (i32, [vp, i64, vp, i64, i32, i32, vp]),
     "r4q_silu_mul": (i32, [vp, i64, vp, i64, i32, i32, vp]),
     "r4q_dequant_int8": (i32, [vp, vp, vp, i32, i32, vp]),
+    "r4q_kv_write_rows": (i32, [vp, vp, i64, vp, vp, i32, i32, i32, i32, i32, i32, vp, vp, vp]),
+    "r4q_moe_route": (i32, [vp, i32, i32, i32, i32, i32, vp, vp, vp, vp, vp, vp, vp, vp]),
+    "r4q_norm_fwht_rows": (i32, [vp, vp, i32, vp, f32, vp, i32, i32, vp]),
+    "r4q_moe_gemv": (i32, [i32, vp, vp, vp, i64, vp, i64, i32, i32, i32, i32, i32, i32, i32, vp, vp, vp, vp, vp,
+                           vp]),
+    "r4q_moe_combine": (i32, [vp, vp, vp, i32, i32, vp, vp, vp, vp, i32, i32, i32, vp]),
+    "r4q_residual_f32": (i32, [vp, vp, vp, vp, i32, i32, vp]),
     "r4q_decode_ctx_create": (i32, [C.POINTER(ModelDesc), C.POINTER(LayerDesc), C.POINTER(C.c_void_p)]),
     "r4q_decode_ctx_destroy": (None, [vp]),
     "r4q_decode_step": (i32, [vp, vp, i32, vp, vp, i32, vp]),

@@ -258,3 +258,70 @@ def dequant_int8(w: torch.Tensor, s: torch.Tensor, out: torch.Tensor | None = No
     y = out if out is not None else torch.empty(N, K, dtype=torch.float16, device=dev)
     L.call("r4q_dequant_int8", w.data_ptr(), s.data_ptr(), y.data_ptr(), N, K, stream_handle(dev))
     return y
+
+
+class MoeRouteBuffers:
+    """Device buffers of one routing: ids, wts and the grouping by expert."""
+
+    def __init__(self, B: int, E: int, topk: int, dev, e_lo: int = 0, e_hi: int | None = None):
+        i32 = dict(dtype=torch.int32, device=dev)
+        self.B, self.E, self.topk = B, E, topk
+        self.e_lo, self.e_hi = e_lo, (E if e_hi is None else e_hi)
+        self.ids = torch.empty(B, topk, **i32)
+        self.wts = torch.empty(B, topk, dtype=torch.float32, device=dev)
+        self.counts = torch.empty(E, **i32)
+        self.offsets = torch.empty(E + 1, **i32)
+        self.list = torch.empty(B * topk, **i32)
+        self.active = torch.empty(E, **i32)
+        self.n_active = torch.empty(1, **i32)
+
+
+def moe_route(logits: torch.Tensor, topk: int, rb: MoeRouteBuffers | None = None) -> MoeRouteBuffers:
+    dev = _require_cuda(logits)
+    B, E = logits.shape
+    rb = rb if rb is not None else MoeRouteBuffers(B, E, topk, dev)
+    L.call("r4q_moe_route", logits.data_ptr(), B, E, topk, rb.e_lo, rb.e_hi, rb.ids.data_ptr(), rb.wts.data_ptr(),
+           rb.counts.data_ptr(), rb.offsets.data_ptr(), rb.list.data_ptr(), rb.active.data_ptr(),
+           rb.n_active.data_ptr(), stream_handle(dev))
+    return rb
+
+
+def norm_fwht_rows(x: torch.Tensor, w: torch.Tensor, eps: float = 1e-6, ss_in: torch.Tensor | None = None,
+                   out: torch.Tensor | None = None) -> torch.Tensor:
+    dev = _require_cuda(x, w)
+    rows, D = x.shape
+    y = out if out is not None else torch.empty_like(x)
+    L.call("r4q_norm_fwht_rows", x.data_ptr(), _ptr(ss_in), 0 if ss_in is None else int(ss_in.shape[0]),
+           w.data_ptr(), float(eps), y.data_ptr(), rows, D, stream_handle(dev))
+    return y
+
+
+def moe_gemv(mode: int, w: torch.Tensor, sz: torch.Tensor, x: torch.Tensor, rb: MoeRouteBuffers, N: int, K: int,
+             out: torch.Tensor | None = None) -> torch.Tensor:
+    """Grouped INT4 expert GEMV (r4q_moe_gemv) over experts [rb.e_lo, rb.e_hi);
+    w [(e_hi-e_lo)*N, K/2], sz [(e_hi-e_lo)*N, K/16]; returns y [B*topk, N]
+    (one row per routed entry; rows of other GPUs' experts untouched)."""
+    dev = _require_cuda(w, sz, x)
+    y = out if out is not None else torch.empty(rb.B * rb.topk, N, dtype=torch.float16, device=dev)
+    L.call("r4q_moe_gemv", mode, w.data_ptr(), sz.data_ptr(), x.data_ptr(), x.stride(0), y.data_ptr(), y.stride(0),
+           N, K, rb.E, rb.e_lo, rb.e_hi, rb.B, rb.topk, rb.counts.data_ptr(), rb.offsets.data_ptr(), rb.list.data_ptr(),
+           rb.active.data_ptr(), rb.n_active.data_ptr(), stream_handle(dev))
+    return y
+
+
+def moe_combine(y: torch.Tensor, rb: MoeRouteBuffers, res: torch.Tensor | None, out: torch.Tensor | None = None,
+                ss_out: torch.Tensor | None = None, out32: torch.Tensor | None = None) -> torch.Tensor:
+    """h = fp16(fp16(sum of this GPU's routed outputs) + res), or with out32 the fp32 partial."""
+    dev = _require_cuda(y)
+    D = y.shape[1]
+    h = out if (out is not None or out32 is not None) else torch.empty(rb.B, D, dtype=torch.float16, device=dev)
+    L.call("r4q_moe_combine", y.data_ptr(), rb.wts.data_ptr(), rb.ids.data_ptr(), rb.e_lo, rb.e_hi, _ptr(res),
+           _ptr(h), _ptr(out32), _ptr(ss_out), rb.B, D, rb.topk, stream_handle(dev))
+    return h if out32 is None else out32
+
+
+def residual_f32(s: torch.Tensor, res: torch.Tensor | None, out: torch.Tensor, ss_out=None) -> torch.Tensor:
+    dev = _require_cuda(s)
+    B, D = s.shape
+    L.call("r4q_residual_f32", s.data_ptr(), _ptr(res), out.data_ptr(), _ptr(ss_out), B, D, stream_handle(dev))
+    return out

@@ -42,8 +42,15 @@ def linear(x: torch.Tensor, w: torch.Tensor, s, N: int) -> torch.Tensor:
 
 def prefill_logits(hidden: torch.Tensor, qkv_w, qkv_s, o_w, o_s, gu_w, gu_s, down_w, down_s, in_norm_w,
                    post_norm_w, q_norm_w, k_norm_w, rope_cos, rope_sin, num_heads, num_kv_heads, head_dim,
-                   hidden_size, intermediate_size, rms_eps, final_norm_w, lm_w, lm_s, lm_N):
-    """hidden fp16 [M, D] (embedded prompt) -> logits fp16 [M, lm_N]."""
+                   hidden_size, intermediate_size, rms_eps, final_norm_w, lm_w, lm_s, lm_N, k_caches=None,
+                   v_caches=None, batch_row: int = 0, k_scales=None, v_scales=None, last_only: bool = False):
+    """hidden fp16 [M, D] (embedded prompt) -> logits fp16 [M, lm_N].
+
+    With ``k_caches`` / ``v_caches`` (uint8 [B, Hk, max_seq, 128] per layer)
+    the prompt's rotated K and V of every layer are written to positions
+    0..M-1 of ``batch_row`` (an extension: the reference prefill writes no
+    cache), so decoding can continue at position M.  ``last_only`` returns
+    the logits of the last position only [1, lm_N]."""
     x = hidden.reshape(-1, int(hidden_size)).contiguous()
     M, D = x.shape
     dev = x.device
@@ -58,6 +65,11 @@ def prefill_logits(hidden: torch.Tensor, qkv_w, qkv_s, o_w, o_s, gu_w, gu_s, dow
         ops.head_norm_rope(qkv, qkv[:, qd:], q_w=q_norm_w[li], k_w=k_norm_w[li], cos=rope_cos, sin=rope_sin,
                            pos_dev=pos, q_out=qkv, k_out=qkv[:, qd:], B=M, H=H, Hk=Hk, D=hd, ld_in=qkv_n,
                            ld_out=qkv_n, eps=rms_eps, flags=L.HEAD_NORM | L.HEAD_ROPE)
+        if k_caches is not None:
+            L.call("r4q_kv_write_rows", qkv[:, qd:].data_ptr(), qkv[:, qd + kvd:].data_ptr(), qkv_n,
+                   k_caches[li].data_ptr(), v_caches[li].data_ptr(), M, Hk, hd, int(k_caches[li].shape[2]), 0,
+                   int(batch_row), ops._ptr(None if k_scales is None else k_scales[li]),
+                   ops._ptr(None if v_scales is None else v_scales[li]), ops.stream_handle(dev))
         q = qkv[:, :qd].view(M, H, hd).transpose(0, 1).unsqueeze(0)
         k = qkv[:, qd:qd + kvd].view(M, Hk, hd).transpose(0, 1).unsqueeze(0)
         v = qkv[:, qd + kvd:].view(M, Hk, hd).transpose(0, 1).unsqueeze(0)
@@ -70,5 +82,7 @@ def prefill_logits(hidden: torch.Tensor, qkv_w, qkv_s, o_w, o_s, gu_w, gu_s, dow
         d = linear(act, down_w[li], down_s[li], D)
         nxt = in_norm_w[li + 1] if li + 1 < nl else in_norm_w[0]
         normed, x = ops.rmsnorm(d, nxt, rms_eps, res=r, want_res=True)
+    if last_only:
+        x = x[-1:].contiguous()
     n = ops.rmsnorm(x, final_norm_w, rms_eps)
     return linear(ops.fwht_rows(n), lm_w, lm_s, int(lm_N))

@@ -63,3 +63,48 @@ def test_row_kernels():
     w = q.reshape(64, 128)
     d = ops.dequant_int8(cuda(w), cuda(s)).cpu().numpy()
     assert np.array_equal(d, O.dequant_int8(w, s))
+
+
+def test_prefill_writes_kv_then_decode_continues():
+    """prefill with caches writes the prompt's K/V (positions 0..M-1, within one
+    FP8 code of the oracle's encoding on >= 95 % of bytes); a decode step at
+    position M over that cache matches the oracle decode over the same bytes."""
+    import int4_hip
+    from r4q import decode, prefill
+    rng = np.random.default_rng(4)
+    M, B = 23, 1
+    layers, final, lm = make_model(29, ('int4', 'int8'), 'int4')
+    embed = (rng.standard_normal((V, D)) * 0.5).astype(np.float16)
+    ids = rng.integers(0, V, M)
+    cos, sin = O.rope_tables(HD, MAXS + 8, 1e6)
+    g, norms = _dev_lists(layers)
+    kcs = [torch.zeros(B, HK, MAXS, HD, dtype=torch.uint8, device='cuda') for _ in range(L)]
+    vcs = [torch.zeros(B, HK, MAXS, HD, dtype=torch.uint8, device='cuda') for _ in range(L)]
+    lm_w, lm_s = cuda(lm[1]), cuda(lm[2])
+    x = cuda(embed)[torch.from_numpy(ids).cuda()]
+    last = prefill.prefill_logits(x, g['qkv_w'], g['qkv_s'], g['o_w'], g['o_s'], g['gu_w'], g['gu_s'], g['down_w'],
+                                  g['down_s'], *norms, cuda(cos), cuda(sin), H, HK, HD, D, I, EPS, cuda(final),
+                                  lm_w, lm_s, V, k_caches=kcs, v_caches=vcs, last_only=True)
+    assert last.shape == (1, V)
+    tok = int(last.reshape(-1).argmax())
+    h = cuda(embed[tok]).reshape(1, 1, D)
+    lg = int4_hip.decode_step_logits(h, g['qkv_w'], g['qkv_s'], 0, g['o_w'], g['o_s'], 0, g['gu_w'], g['gu_s'], 0,
+                                     g['down_w'], g['down_s'], 0, *norms, cuda(cos), cuda(sin), M, H, HK, HD, D, I,
+                                     EPS, kcs, vcs, cuda(final), lm_w, lm_s, V, D, None)
+    torch.cuda.synchronize()
+    O.INT4_MODE['mode'] = 'blockwise'
+    ref, _ = O.decode_step_logits(embed[tok].reshape(1, D), layers, CFG, [k.cpu().numpy() for k in kcs],
+                                  [v.cpu().numpy() for v in vcs], M, cos, sin, final, lm, write_kv=False)
+    close(lg.cpu().numpy().reshape(1, V), ref, 2e-3)
+    # the prompt rows against the oracle's own K (layer 0 is exact up to GEMM rounding)
+    O.INT4_MODE['mode'] = 'dequant'
+    qd, kd = H * HD, HK * HD
+    normed = O.rmsnorm(embed[ids], layers[0]['in_norm'], EPS)
+    qkv = O.linear(O.fwht32(normed.astype(np.float32)).astype(np.float16), layers[0]['qkv'])
+    kn = np.stack([O.head_norm_rope(qkv[m, qd:qd + kd].reshape(HK, HD), layers[0]['k_norm'], cos[m], sin[m], EPS)
+                   for m in range(M)]).astype(np.float16)
+    want = O.fp8_encode(kn.astype(np.float32)).transpose(1, 0, 2)        # [HK, M, HD]
+    got = kcs[0].cpu().numpy()[0, :, :M]
+    dlt = got.astype(np.int32) - want.astype(np.int32)
+    assert (dlt != 0).mean() <= 0.05 and np.abs(dlt).max() <= 1
+    decode.clear_contexts()
