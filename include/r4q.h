@@ -238,6 +238,10 @@ int r4q_moe_combine(const void* y, const float* wts, const int* ids, int e_lo, i
                     float* out32, float* ss_out, int B, int D, int topk, void* stream);
 /* h = fp16(fp16(sum) + res) and its per-16-row sums of squares, sum fp32 [B, D]. */
 int r4q_residual_f32(const float* sum, const void* res, void* h, float* ss_out, int B, int D, void* stream);
+/* The same for an fp16 a: h = fp16(a + res) with the sums of squares of the
+ * unrounded sum (the GEMV residual epilogue as its own pass, for batches the
+ * tensor-core GEMM takes). */
+int r4q_residual_f16(const void* a, const void* res, void* h, float* ss_out, int B, int D, void* stream);
 
 /* ------------------------------------------------------------- decode step --- */
 /* One transformer layer's weights and caches (device pointers).  *_fmt is

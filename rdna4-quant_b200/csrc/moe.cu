@@ -26,7 +26,9 @@ namespace {
 
 constexpr int kMoeTile = 64;
 constexpr int kMoeTokChunk = 16;        // tokens staged per pass (2 n-groups of 8)
-constexpr int kMoeThreads = 256;
+constexpr int kMoeThreads = 512;       // 16 warps: 4 m-tiles x 4 K quarters
+constexpr int kMoeKq = 4;
+constexpr int kMoeBatch = 4;            // 32-k blocks whose loads are in flight together
 
 struct MoeRoute {
   const int* counts;      // [E]
@@ -171,13 +173,13 @@ __global__ void __launch_bounds__(kMoeThreads)
   const int row0 = blockIdx.x * kMoeTile;
   extern __shared__ __align__(16) uint8_t smem[];
   __half* xs = reinterpret_cast<__half*>(smem);                           // [16][K + 8]
-  float* red = reinterpret_cast<float*>(xs + kMoeTokChunk * (K + 8));     // [4][2 n-groups][4][32]
+  float* red = reinterpret_cast<float*>(xs + kMoeTokChunk * (K + 8));     // [3 quarters][4][2 ng][4][32]
   const int ldxs = K + 8;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, t = lane & 3;
-  const int mt = warp & 3, kh = warp >> 2;
+  const int mt = warp & 3, kh = warp >> 2;                // m-tile, K quarter
   const int nblk = K / 32;
-  const int b0 = (nblk * kh) / 2, b1 = (nblk * (kh + 1)) / 2;
+  const int b0 = (nblk * kh) / kMoeKq, b1 = (nblk * (kh + 1)) / kMoeKq;
   const long wrow = (long)K / 2, srow = (long)K / 16;
   const int ra = row0 + mt * 16 + g, rb = ra + 8;
   const long el = e - e_lo;                              // this GPU's expert slice starts at e_lo
@@ -215,56 +217,68 @@ __global__ void __launch_bounds__(kMoeThreads)
     float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
     const bool live = ra < N;
     if (live) {
-#pragma unroll 2
-      for (int blk = b0; blk < b1; ++blk) {
-        const uint4 qa = __ldg(reinterpret_cast<const uint4*>(wa + blk * 16));
-        const uint4 qb = __ldg(reinterpret_cast<const uint4*>(wb + blk * 16));
-        const __half2 pa = __ldg(reinterpret_cast<const __half2*>(sa + blk * 2));
-        const __half2 pb = __ldg(reinterpret_cast<const __half2*>(sb + blk * 2));
-        const uint32_t wa4[4] = {qa.x, qa.y, qa.z, qa.w}, wb4[4] = {qb.x, qb.y, qb.z, qb.w};
-        // this lane's bytes t, t + 4, t + 8, t + 12 of each row: k pairs
-        // (2t, 2t+1), (2t+8, 2t+9), (16+2t, ..), (24+2t, ..)
-        uint32_t fa[4], fb[4];
-        const __half2 s2a = __half2half2(__low2half(pa)), z2a = __hadd2(__half2half2(__high2half(pa)),
-                                                                         __float2half2_rn(1024.0f));
-        const __half2 s2b = __half2half2(__low2half(pb)), z2b = __hadd2(__half2half2(__high2half(pb)),
-                                                                         __float2half2_rn(1024.0f));
+      for (int bb = b0; bb < b1; bb += kMoeBatch) {
+        uint4 qa[kMoeBatch], qb[kMoeBatch];
+        __half2 pa[kMoeBatch], pb[kMoeBatch];
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const uint32_t byte_a = (wa4[q] >> (8 * t)) & 0xFFu;   // byte 4q + t
-          const uint32_t byte_b = (wb4[q] >> (8 * t)) & 0xFFu;
-          const uint32_t ha = (byte_a & 0xFu) | ((byte_a >> 4) << 16);
-          const uint32_t hb = (byte_b & 0xFu) | ((byte_b >> 4) << 16);
-          fa[q] = h2_as_u32(__hmul2(__hsub2(u32_as_h2(ha | 0x64006400u), z2a), s2a));
-          fb[q] = h2_as_u32(__hmul2(__hsub2(u32_as_h2(hb | 0x64006400u), z2b), s2b));
+        for (int u = 0; u < kMoeBatch; ++u) {       // every load of the batch first
+          const int blk = min(bb + u, b1 - 1);
+          qa[u] = __ldg(reinterpret_cast<const uint4*>(wa + blk * 16));
+          qb[u] = __ldg(reinterpret_cast<const uint4*>(wb + blk * 16));
+          pa[u] = __ldg(reinterpret_cast<const __half2*>(sa + blk * 2));
+          pb[u] = __ldg(reinterpret_cast<const __half2*>(sb + blk * 2));
         }
-        const int kb = blk * 32;
 #pragma unroll
-        for (int ks = 0; ks < 2; ++ks) {
-          const uint32_t a0 = fa[2 * ks], a1 = fb[2 * ks], a2 = fa[2 * ks + 1], a3 = fb[2 * ks + 1];
+        for (int u = 0; u < kMoeBatch; ++u) {
+          const int blk = bb + u;
+          if (blk >= b1) break;
+          const uint32_t wa4[4] = {qa[u].x, qa[u].y, qa[u].z, qa[u].w}, wb4[4] = {qb[u].x, qb[u].y, qb[u].z, qb[u].w};
+          // this lane's bytes t, t + 4, t + 8, t + 12 of each row: k pairs
+          // (2t, 2t+1), (2t+8, 2t+9), (16+2t, ..), (24+2t, ..)
+          uint32_t fa[4], fb[4];
+          const __half2 s2a = __half2half2(__low2half(pa[u])),
+                        z2a = __hadd2(__half2half2(__high2half(pa[u])), __float2half2_rn(1024.0f));
+          const __half2 s2b = __half2half2(__low2half(pb[u])),
+                        z2b = __hadd2(__half2half2(__high2half(pb[u])), __float2half2_rn(1024.0f));
 #pragma unroll
-          for (int ng = 0; ng < 2; ++ng) {
-            const __half* xr = xs + (ng * 8 + g) * ldxs + kb + ks * 16 + 2 * t;
-            const uint32_t bb0 = *reinterpret_cast<const uint32_t*>(xr);
-            const uint32_t bb1 = *reinterpret_cast<const uint32_t*>(xr + 8);
-            mma16816(acc[ng], a0, a1, a2, a3, bb0, bb1);
+          for (int q = 0; q < 4; ++q) {
+            const uint32_t byte_a = (wa4[q] >> (8 * t)) & 0xFFu;   // byte 4q + t
+            const uint32_t byte_b = (wb4[q] >> (8 * t)) & 0xFFu;
+            const uint32_t ha = (byte_a & 0xFu) | ((byte_a >> 4) << 16);
+            const uint32_t hb = (byte_b & 0xFu) | ((byte_b >> 4) << 16);
+            fa[q] = h2_as_u32(__hmul2(__hsub2(u32_as_h2(ha | 0x64006400u), z2a), s2a));
+            fb[q] = h2_as_u32(__hmul2(__hsub2(u32_as_h2(hb | 0x64006400u), z2b), s2b));
+          }
+          const int kb = blk * 32;
+#pragma unroll
+          for (int ks = 0; ks < 2; ++ks) {
+            const uint32_t a0 = fa[2 * ks], a1 = fb[2 * ks], a2 = fa[2 * ks + 1], a3 = fb[2 * ks + 1];
+#pragma unroll
+            for (int ng = 0; ng < 2; ++ng) {
+              const __half* xr = xs + (ng * 8 + g) * ldxs + kb + ks * 16 + 2 * t;
+              const uint32_t bb0 = *reinterpret_cast<const uint32_t*>(xr);
+              const uint32_t bb1 = *reinterpret_cast<const uint32_t*>(xr + 8);
+              mma16816(acc[ng], a0, a1, a2, a3, bb0, bb1);
+            }
           }
         }
       }
     }
-    // ---- the two K halves meet in shared memory; half 0 writes
-    if (kh == 1) {
+    // ---- the K quarters meet in shared memory (fixed order); quarter 0 writes
+    if (kh != 0) {
 #pragma unroll
       for (int ng = 0; ng < 2; ++ng)
 #pragma unroll
-        for (int i = 0; i < 4; ++i) red[((mt * 2 + ng) * 4 + i) * 32 + lane] = acc[ng][i];
+        for (int i = 0; i < 4; ++i) red[((((kh - 1) * 4 + mt) * 2 + ng) * 4 + i) * 32 + lane] = acc[ng][i];
     }
     __syncthreads();
     if (kh == 0 && live) {
 #pragma unroll
       for (int ng = 0; ng < 2; ++ng) {
 #pragma unroll
-        for (int i = 0; i < 4; ++i) acc[ng][i] += red[((mt * 2 + ng) * 4 + i) * 32 + lane];
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+          for (int q = 0; q < kMoeKq - 1; ++q) acc[ng][i] += red[(((q * 4 + mt) * 2 + ng) * 4 + i) * 32 + lane];
         // C: (row g, tokens 2t, 2t+1), (row g + 8, tokens 2t, 2t+1)
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
@@ -324,8 +338,9 @@ __global__ void moe_combine_kernel(const __half* __restrict__ yk, const float* _
 }
 
 // h[b] = fp16(fp16(sum[b]) + res[b]) and the sums of squares, for the fp32
-// sum of the expert-parallel partials.
-__global__ void residual_f32_kernel(const float* __restrict__ sum, const __half* res, __half* out,
+// sum of the expert-parallel partials (F16: sum already fp16, a GEMM output).
+template <bool F16>
+__global__ void residual_f32_kernel(const void* __restrict__ sumv, const __half* res, __half* out,
                                     float* __restrict__ ss_out, int B, int D) {
   const long i = ((long)blockIdx.x * blockDim.x + threadIdx.x) * 4;
   const bool ok = i < (long)B * D;
@@ -333,7 +348,8 @@ __global__ void residual_f32_kernel(const float* __restrict__ sum, const __half*
   if (ok) {
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      float v = __half2float(__float2half(sum[i + j]));
+      float v = F16 ? __half2float(reinterpret_cast<const __half*>(sumv)[i + j])
+                    : __half2float(__float2half(reinterpret_cast<const float*>(sumv)[i + j]));
       if (res) v += __half2float(res[i + j]);
       sq += v * v;
       out[i + j] = __float2half(v);
@@ -383,7 +399,7 @@ extern "C" int r4q_moe_gemv(int mode, const void* w, const void* sz, const void*
   if (!aligned(w, 16) || !aligned(sz, 4) || !aligned(x, 16) || ldx % 8)
     return set_error(R4Q_ERR_ALIGN, "moe_gemv: weights / activations misaligned");
   MoeRoute rt{counts, offsets, list, active, n_active};
-  const size_t smem = (size_t)kMoeTokChunk * (K + 8) * 2 + 4 * 2 * 4 * 32 * 4;
+  const size_t smem = (size_t)kMoeTokChunk * (K + 8) * 2 + (kMoeKq - 1) * 4 * 2 * 4 * 32 * 4;
   const int el = e_hi - e_lo;
   const int slots = (el < B * topk) ? el : B * topk;
   dim3 grid((N + kMoeTile - 1) / kMoeTile, slots);
@@ -414,7 +430,16 @@ extern "C" int r4q_residual_f32(const float* sum, const void* res, void* out, fl
                                 void* stream) {
   if (!sum || !out || B < 1 || D < 16 || D % 16) return set_error(R4Q_ERR_ARG, "residual_f32: bad arguments");
   const long n4 = (long)B * D / 4;
-  residual_f32_kernel<<<(unsigned)((n4 + 255) / 256), 256, 0, (cudaStream_t)stream>>>(sum, (const __half*)res,
-                                                                                     (__half*)out, ss_out, B, D);
+  residual_f32_kernel<false><<<(unsigned)((n4 + 255) / 256), 256, 0, (cudaStream_t)stream>>>(
+      sum, (const __half*)res, (__half*)out, ss_out, B, D);
   return check_launch("residual_f32_kernel");
+}
+
+extern "C" int r4q_residual_f16(const void* a, const void* res, void* out, float* ss_out, int B, int D,
+                                void* stream) {
+  if (!a || !out || B < 1 || D < 16 || D % 16) return set_error(R4Q_ERR_ARG, "residual_f16: bad arguments");
+  const long n4 = (long)B * D / 4;
+  residual_f32_kernel<true><<<(unsigned)((n4 + 255) / 256), 256, 0, (cudaStream_t)stream>>>(
+      a, (const __half*)res, (__half*)out, ss_out, B, D);
+  return check_launch("residual_f16_kernel");
 }

@@ -92,6 +92,7 @@ _SIGS = {
                            vp]),
     "r4q_moe_combine": (i32, [vp, vp, vp, i32, i32, vp, vp, vp, vp, i32, i32, i32, vp]),
     "r4q_residual_f32": (i32, [vp, vp, vp, vp, i32, i32, vp]),
+    "r4q_residual_f16": (i32, [vp, vp, vp, vp, i32, i32, vp]),
     "r4q_decode_ctx_create": (i32, [C.POINTER(ModelDesc), C.POINTER(LayerDesc), C.POINTER(C.c_void_p)]),
     "r4q_decode_ctx_destroy": (None, [vp]),
     "r4q_decode_step": (i32, [vp, vp, i32, vp, vp, i32, vp]),

@@ -95,6 +95,7 @@ class MoEDecoder:
         self.attn = torch.zeros(B, H, hd, **f16)
         self.rlog = torch.zeros(B, E, **f16)
         self.xn = torch.zeros(B, D, **f16)
+        self.o16 = torch.zeros(B, D, **f16)
         self.gu = torch.zeros(B * k, 2 * Ie, **f16)
         self.yk = torch.zeros(B * k, D, **f16)
         self.ss_post = torch.zeros(D // 16, B, dtype=torch.float32, device=dev)
@@ -122,20 +123,31 @@ class MoEDecoder:
         D, H, Hk, hd = c['hidden'], c['num_heads'], c['num_kv_heads'], c['head_dim']
         Ie, eps = c['expert_inter'], c['rms_eps']
         qkv_n = (H + 2 * Hk) * hd
+        big = self.B > 16          # the GEMV takes up to 16 rows: larger batches use the tensor-core GEMM
         for li in range(c['num_layers']):
             hin = self.h_in if li == 0 else self.h
-            ops.gemv('int4', hin, m['qkv_w'][li], m['qkv_s'][li], qkv_n, D, prologue=L.PRO_RMSNORM_FWHT,
-                     out=self.qkv, norm_w=m['in_norm_w'][li], eps=eps, ss_in=None if li == 0 else self.ss_h)
+            if big:
+                ops.norm_fwht_rows(hin, m['in_norm_w'][li], eps, ss_in=None if li == 0 else self.ss_h, out=self.xn)
+                ops.gemm(self.xn, m['qkv_w'][li], m['qkv_s'][li], qkv_n, out=self.qkv)
+            else:
+                ops.gemv('int4', hin, m['qkv_w'][li], m['qkv_s'][li], qkv_n, D, prologue=L.PRO_RMSNORM_FWHT,
+                         out=self.qkv, norm_w=m['in_norm_w'][li], eps=eps, ss_in=None if li == 0 else self.ss_h)
             ops.attn_decode_fused(self.qkv, m['k_caches'][li], m['v_caches'][li], m['q_norm_w'][li],
                                   m['k_norm_w'][li], m['rope_cos'], m['rope_sin'], H, Hk, 0, fwht=True, eps=eps,
                                   out=self.attn, seq_dev=self.seq)
-            ops.gemv('int4', self.attn.view(self.B, H * hd), m['o_w'][li], m['o_s'][li], D, H * hd, out=self.r,
-                     residual=hin, ss_out=self.ss_post)
-            # router logits from RMSNorm+FWHT of r (rotated router weights)
-            ops.gemv('fp16', self.r, m['router_w'][li], None, c['experts'], D, prologue=L.PRO_RMSNORM_FWHT,
-                     out=self.rlog, norm_w=m['post_norm_w'][li], eps=eps, ss_in=self.ss_post)
+            if big:
+                ops.gemm(self.attn.view(self.B, H * hd), m['o_w'][li], m['o_s'][li], D, out=self.o16)
+                ops.residual_f16(self.o16, hin, self.r, ss_out=self.ss_post)
+                ops.norm_fwht_rows(self.r, m['post_norm_w'][li], eps, ss_in=self.ss_post, out=self.xn)
+                ops.gemm(self.xn, m['router_w'][li], None, c['experts'], out=self.rlog)
+            else:
+                ops.gemv('int4', self.attn.view(self.B, H * hd), m['o_w'][li], m['o_s'][li], D, H * hd,
+                         out=self.r, residual=hin, ss_out=self.ss_post)
+                # router logits from RMSNorm+FWHT of r (rotated router weights)
+                ops.gemv('fp16', self.r, m['router_w'][li], None, c['experts'], D, prologue=L.PRO_RMSNORM_FWHT,
+                         out=self.rlog, norm_w=m['post_norm_w'][li], eps=eps, ss_in=self.ss_post)
+                ops.norm_fwht_rows(self.r, m['post_norm_w'][li], eps, ss_in=self.ss_post, out=self.xn)
             ops.moe_route(self.rlog, c['topk'], self.rb)
-            ops.norm_fwht_rows(self.r, m['post_norm_w'][li], eps, ss_in=self.ss_post, out=self.xn)
             ops.moe_gemv(0, self.egu[li][0], self.egu[li][1], self.xn, self.rb, 2 * Ie, D, out=self.gu)
             ops.moe_gemv(1, self.edown[li][0], self.edown[li][1], self.gu, self.rb, D, Ie, out=self.yk)
             if self.comm is None:
@@ -144,8 +156,12 @@ class MoEDecoder:
                 ops.moe_combine(self.yk, self.rb, None, out32=self.part)
                 self.comm.allreduce_f32(self.part, out=self.psum)
                 ops.residual_f32(self.psum, self.r, self.h, ss_out=self.ss_h)
-        ops.gemv('fp16', self.h, m['lm_w'], None, c['vocab'], D, prologue=L.PRO_RMSNORM_FWHT, out=self.logits,
-                 norm_w=m['final_norm_w'], eps=eps)
+        if big:
+            ops.norm_fwht_rows(self.h, m['final_norm_w'], eps, out=self.xn)
+            ops.gemm(self.xn, m['lm_w'], None, c['vocab'], out=self.logits)
+        else:
+            ops.gemv('fp16', self.h, m['lm_w'], None, c['vocab'], D, prologue=L.PRO_RMSNORM_FWHT,
+                     out=self.logits, norm_w=m['final_norm_w'], eps=eps)
 
     def step(self, hidden: torch.Tensor, pos: int, use_graph: bool = True) -> torch.Tensor:
         """hidden fp16 [B, D] at position pos -> logits [B, vocab] (the step's

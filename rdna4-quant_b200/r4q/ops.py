@@ -325,3 +325,10 @@ def residual_f32(s: torch.Tensor, res: torch.Tensor | None, out: torch.Tensor, s
     B, D = s.shape
     L.call("r4q_residual_f32", s.data_ptr(), _ptr(res), out.data_ptr(), _ptr(ss_out), B, D, stream_handle(dev))
     return out
+
+
+def residual_f16(a: torch.Tensor, res: torch.Tensor | None, out: torch.Tensor, ss_out=None) -> torch.Tensor:
+    dev = _require_cuda(a)
+    B, D = a.shape
+    L.call("r4q_residual_f16", a.data_ptr(), _ptr(res), out.data_ptr(), _ptr(ss_out), B, D, stream_handle(dev))
+    return out

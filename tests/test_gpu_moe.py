@@ -59,7 +59,7 @@ def test_grouped_expert_gemv(B):
     assert sorted(lst.tolist()) == list(range(B * k))
 
 
-@pytest.mark.parametrize("B", [1, 4])
+@pytest.mark.parametrize("B", [1, 4, 20])
 def test_moe_decode_step_vs_oracle(B):
     from r4q import moe
     dev = torch.device('cuda')
