@@ -217,15 +217,27 @@ int r4q_kv_write_rows(const void* k, const void* v, long ld, void* k_cache, void
  * expert parallelism), n_active [1].  E <= 256, topk <= 16. */
 int r4q_moe_route(const void* logits, int B, int E, int topk, int e_lo, int e_hi, int* ids, float* wts,
                   int* counts, int* offsets, int* list, int* active, int* n_active, void* stream);
+/* Router of a decode layer in one launch: xn[b] = fp16(H32(x[b] * rrms *
+ * norm_w)) with rrms from the ss_in partials [ss_parts][B] (norm_w null: xn
+ * is an input, already normalised), logits[b][e] = fp16(router_w[e] · xn[b])
+ * (router_w fp16 [E, D], H32-rotated), then the routing of r4q_moe_route by
+ * the grid's last CTA.  done: one int, zero before the first call (the
+ * kernel leaves it zero).  D % 256 == 0, D <= 2048, E <= 256. */
+int r4q_moe_router(const void* x, const float* ss_in, int ss_parts, const void* norm_w, float eps, void* xn,
+                   const void* router_w, void* logits, int B, int D, int E, int topk, int e_lo, int e_hi, int* ids,
+                   float* wts, int* counts, int* offsets, int* list, int* active, int* n_active, int* done,
+                   void* stream);
 /* y[b] = fp16(H32(x[b] * rrms * w)) per 32-block, rrms from ss_in partials
  * ([ss_parts][rows]) or from x: the RMSNorm+FWHT prologue as its own pass. */
 int r4q_norm_fwht_rows(const void* x, const float* ss_in, int ss_parts, const void* w, float eps, void* y,
                        int rows, int D, void* stream);
 /* Grouped INT4 expert GEMV over the routed entries of experts [e_lo, e_hi)
  * (the active list of r4q_moe_route).  This GPU's experts stacked: w
- * [(e_hi - e_lo) * N, K/2], sz [(e_hi - e_lo) * N, K/16].  mode 0: y[j] = W_e · x[j / topk] (x rows of
- * K); mode 1: y[j] = W_e · fp16(H32(silu(g) u)), g, u = halves of x[j] (rows
- * of 2K).  y rows of N fp16 (ldy), one per entry j. */
+ * [(e_hi - e_lo) * N, K/2], sz [(e_hi - e_lo) * N, K/16]; N % 64 == 0,
+ * K % 128 == 0.  mode 0: y[j] = W_e · x[j / topk]; mode 1: y[j] = W_e · x[j];
+ * mode 2 (gate_up, N = 2 Ie, rows [gate; up]): y[j] = fp16(H32(silu(g) u)),
+ * g, u = fp16(W_e · x[j / topk]) halves — down_proj's input, Ie per row.
+ * y rows fp16 (ldy), one per entry j. */
 int r4q_moe_gemv(int mode, const void* w, const void* sz, const void* x, long ldx, void* y, long ldy, int N,
                  int K, int E, int e_lo, int e_hi, int B, int topk, const int* counts, const int* offsets,
                  const int* list, const int* active, const int* n_active, void* stream);

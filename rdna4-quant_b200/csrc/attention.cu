@@ -466,19 +466,25 @@ static int cache_map(CUtensorMap* m, const void* base, long rows) {
   return R4Q_OK;
 }
 
-// CTAs per cluster: 8 (portable), 4 for short contexts (at most 16 tiles).
-// Measured on B200, B = 1, 8 kv heads, 40 layers in a graph: clusters of 16
-// (non-portable) schedule badly (15 us at ctx 2048 against 6.9 us for 8).
-// R4Q_ATTN_CLUSTER forces 1, 2, 4, 8 or 16 (measurement only).
+// CTAs per cluster: 8 (portable), 4 for short contexts (at most 16 tiles),
+// halved while the grid would exceed one wave (two CTAs per SM): with many
+// (row, kv head) pairs the work already fills the GPU and a wave of
+// clusters costs a whole CTA lifetime.  Measured on B200, B = 1, 8 kv heads,
+// 40 layers in a graph: clusters of 16 (non-portable) schedule badly (15 us
+// at ctx 2048 against 6.9 us for 8).  R4Q_ATTN_CLUSTER forces 1, 2, 4, 8 or
+// 16 (measurement only).
 static int attn_cluster(int B, int Hk, int max_tiles) {
-  (void)B;
-  (void)Hk;
   static const int forced = [] {
     const char* e = getenv("R4Q_ATTN_CLUSTER");
     return e ? atoi(e) : 0;
   }();
   if (forced == 1 || forced == 2 || forced == 4 || forced == 8 || forced == 16) return forced;
-  return max_tiles <= 16 ? 4 : 8;
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  int c = max_tiles <= 16 ? 4 : 8;
+  while (c > 1 && (long)B * Hk * c > 2L * sms) c >>= 1;
+  return c;
 }
 
 static size_t attn_smem() {

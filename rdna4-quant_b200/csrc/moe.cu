@@ -9,26 +9,33 @@
 //  * moe_route_kernel: per token softmax over the router logits (fp32), top-k
 //    (ties to the lower expert), weights renormalised over the k; then the
 //    (token, slot) pairs grouped by expert in token order — a deterministic
-//    counting sort in one CTA — and the ascending list of active experts;
-//  * moe_gemv_kernel: grouped dequant-GEMV.  CTA = (64-row tile, active-expert
-//    slot); a fixed grid (so it can live in a CUDA graph) whose CTAs past the
-//    active count exit.  The CTA stages the activations of its expert's
-//    tokens (16 at a time) in shared memory — for down_proj with the
-//    SiLU(gate)·up + FWHT prologue applied — and 8 warps (4 m-tiles x 2 K
-//    halves) stream the expert's weights with 128-bit loads, dequantise in
-//    registers and accumulate on the tensor cores (m16n8k16, tokens as N);
+//    counting sort in one CTA (warp scan of the counts, match_any ranks) —
+//    and the ascending list of active experts;
+//  * moe_gemv_kernel: grouped dequant-GEMV.  CTAs walk the work items
+//    (active expert, 64-row tile), an expert's tiles adjacent, the item count
+//    read on the device; the grid is fixed (one CTA per possible item), so
+//    the launch can live in a CUDA graph.  8 warps = 4 m-tiles x 2 K halves.  Lane t of a warp
+//    owns whole 32-k blocks (block 4q + t of batch q): one 128-bit load per
+//    row brings its 32 nibbles, so a warp load covers 64 contiguous bytes of
+//    8 rows; the k order inside the m16n8k16 fragments is permuted to match
+//    (the activations are read with the same permutation, so the dot products
+//    are unchanged).  Tokens are the N dimension, 8 per pass.  Mode 2 is
+//    gate_up with the SiLU(gate)·up + H32 FWHT epilogue (the tile holds 32
+//    gate rows and the matching 32 up rows), writing down_proj's input;
 //  * moe_combine_kernel: h = fp16(fp16(Σ_k w_k fp16(y_k)) + residual) in slot
 //    order, with the per-16-row sums of squares the next RMSNorm prologue takes.
+#include <atomic>
+#include <cstdlib>
+
 #include "r4q_common.cuh"
 
 namespace r4q {
 namespace {
 
-constexpr int kMoeTile = 64;
-constexpr int kMoeTokChunk = 16;        // tokens staged per pass (2 n-groups of 8)
-constexpr int kMoeThreads = 512;       // 16 warps: 4 m-tiles x 4 K quarters
-constexpr int kMoeKq = 4;
-constexpr int kMoeBatch = 4;            // 32-k blocks whose loads are in flight together
+constexpr int kMoeTok = 8;              // tokens per pass (one m16n8k16 n-group)
+constexpr int kMoeThreads = 256;        // 8 warps: 4 m-tiles x 2 K halves
+constexpr int kMoeKp = 2;
+constexpr int kMoeUnroll = 4;           // 128-k batches whose weight loads are in flight together
 
 struct MoeRoute {
   const int* counts;      // [E]
@@ -39,39 +46,48 @@ struct MoeRoute {
 };
 
 // ---------------------------------------------------------------- routing
-__global__ void moe_route_kernel(const __half* __restrict__ logits, int B, int E, int topk, int e_lo, int e_hi,
-                                 int* ids, float* wts, int* counts, int* offsets, int* list, int* active,
-                                 int* n_active) {
-  extern __shared__ int sm[];
-  int* s_cnt = sm;                  // [E]
-  int* s_ids = sm + E;              // [B * topk]
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, nw = blockDim.x >> 5;
-  for (int e = tid; e < E; e += blockDim.x) s_cnt[e] = 0;
-  // one warp per token: softmax, then top-k by repeated arg-max
-  for (int b = warp; b < B; b += nw) {
+// Top-k of B tokens, G lanes per token (32 / G tokens per warp at once):
+// logits in registers (expert sub + G i, PL = 256 / G per lane), softmax,
+// top-k by repeated arg-max over the experts not yet taken; reductions stay
+// inside the G-lane group.  Writes ids / wts, s_ids and the counts s_cnt.
+template <int G>
+__device__ __forceinline__ void route_topk(const __half* logits, int B, int E, int topk, int* ids, float* wts,
+                                           int* s_cnt, int* s_ids, int warp, int lane, int nw) {
+  constexpr int PL = 256 / G;
+  const int sub = lane & (G - 1);
+  for (int b0 = warp * (32 / G); b0 < B; b0 += nw * (32 / G)) {
+    const int b = b0 + lane / G;
+    const bool valid = b < B;
     const __half* lr = logits + (long)b * E;
+    float lv[PL];
     float mx = -INFINITY;
-    for (int e = lane; e < E; e += 32) mx = fmaxf(mx, __half2float(lr[e]));
-    for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+#pragma unroll
+    for (int i = 0; i < PL; ++i) {
+      const int e = sub + G * i;
+      lv[i] = (valid && e < E) ? __half2float(__ldcg(lr + e)) : -INFINITY;
+      mx = fmaxf(mx, lv[i]);
+    }
+    for (int o = G / 2; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
     float sum = 0.0f;
-    for (int e = lane; e < E; e += 32) sum += expf(__half2float(lr[e]) - mx);
-    sum = warp_sum(sum);
-    unsigned long long taken[4] = {0, 0, 0, 0};      // E <= 256
-    float psel = 0.0f;
-    float pk[16];
-    int ik[16];
+#pragma unroll
+    for (int i = 0; i < PL; ++i)
+      if (valid && sub + G * i < E) sum += expf(lv[i] - mx);
+    for (int o = G / 2; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    uint32_t taken = 0;
+    float psel = 0.0f, pm[2] = {0.f, 0.f};
+    int im[2] = {0, 0};
     for (int k = 0; k < topk; ++k) {
       float bv = -INFINITY;
       int bi = 0x7fffffff;
-      for (int e = lane; e < E; e += 32) {
-        if ((taken[e >> 6] >> (e & 63)) & 1ull) continue;
-        const float v = __half2float(lr[e]);
-        if (v > bv || (v == bv && e < bi)) {
-          bv = v;
+#pragma unroll
+      for (int i = 0; i < PL; ++i) {
+        const int e = sub + G * i;
+        if (e < E && !((taken >> i) & 1u) && (lv[i] > bv || (lv[i] == bv && e < bi))) {
+          bv = lv[i];
           bi = e;
         }
       }
-      for (int o = 16; o; o >>= 1) {
+      for (int o = G / 2; o; o >>= 1) {
         const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
         const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
         if (ov > bv || (ov == bv && oi < bi)) {
@@ -79,40 +95,234 @@ __global__ void moe_route_kernel(const __half* __restrict__ logits, int B, int E
           bi = oi;
         }
       }
-      taken[bi >> 6] |= 1ull << (bi & 63);
+      if (valid && bi < E && (bi & (G - 1)) == sub) taken |= 1u << (bi / G);
       const float p = expf(bv - mx) / sum;
-      pk[k] = p;
-      ik[k] = bi;
       psel += p;
+      if (k % G == sub) {
+        if (k < G) {
+          pm[0] = p;
+          im[0] = bi;
+        } else {
+          pm[1] = p;
+          im[1] = bi;
+        }
+      }
     }
-    if (lane == 0)
-      for (int k = 0; k < topk; ++k) {
-        ids[b * topk + k] = ik[k];
-        wts[b * topk + k] = pk[k] / psel;
-        s_ids[b * topk + k] = ik[k];
-        atomicAdd(&s_cnt[ik[k]], 1);
+    if (valid)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int kk = sub + G * h;
+        if (kk < topk) {
+          ids[b * topk + kk] = im[h];
+          wts[b * topk + kk] = pm[h] / psel;
+          s_ids[b * topk + kk] = im[h];
+          atomicAdd(&s_cnt[im[h]], 1);
+        }
       }
   }
+}
+
+// The whole routing of B tokens by one CTA (any multiple of 32 threads);
+// sm: (3 E + B * topk) ints.  Logits are read through L2 (.cg): in the fused
+// router they were written by other CTAs of the same grid.
+__device__ void route_tokens(const __half* logits, int B, int E, int topk, int e_lo, int e_hi, int* ids, float* wts,
+                             int* counts, int* offsets, int* list, int* active, int* n_active, int* sm) {
+  int* s_cnt = sm;                  // [E]
+  int* s_off = sm + E;              // [E]
+  int* s_run = sm + 2 * E;          // [E]
+  int* s_ids = sm + 3 * E;          // [B * topk]
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, nw = blockDim.x >> 5;
+  for (int e = tid; e < E; e += blockDim.x) s_cnt[e] = s_run[e] = 0;
   __syncthreads();
-  if (tid == 0) {
-    int off = 0, na = 0;
-    for (int e = 0; e < E; ++e) {
-      offsets[e] = off;
-      counts[e] = s_cnt[e];
-      if (s_cnt[e] && e >= e_lo && e < e_hi) active[na++] = e;
-      off += s_cnt[e];
+  // small batches: a warp per token (short per-lane loops); large: 8 lanes
+  if (B <= nw) route_topk<32>(logits, B, E, topk, ids, wts, s_cnt, s_ids, warp, lane, nw);
+  else route_topk<8>(logits, B, E, topk, ids, wts, s_cnt, s_ids, warp, lane, nw);
+  __syncthreads();
+  const int n = B * topk;
+  if (warp == 0) {
+    // offsets (exclusive scan of the counts) and the active experts in
+    // [e_lo, e_hi), ascending: lane owns experts [lane * per, lane * per + per)
+    const int per = (E + 31) / 32;
+    int c = 0, a = 0;
+    for (int i = 0; i < per; ++i) {
+      const int e = lane * per + i;
+      if (e < E) {
+        c += s_cnt[e];
+        a += (s_cnt[e] > 0 && e >= e_lo && e < e_hi);
+      }
     }
-    offsets[E] = off;
-    *n_active = na;
+    int cs = c, as = a;
+    for (int o = 1; o < 32; o <<= 1) {
+      const int oc = __shfl_up_sync(0xffffffffu, cs, o), oa = __shfl_up_sync(0xffffffffu, as, o);
+      if (lane >= o) {
+        cs += oc;
+        as += oa;
+      }
+    }
+    int off = cs - c, na = as - a;
+    for (int i = 0; i < per; ++i) {
+      const int e = lane * per + i;
+      if (e < E) {
+        s_off[e] = off;
+        offsets[e] = off;
+        counts[e] = s_cnt[e];
+        if (s_cnt[e] > 0 && e >= e_lo && e < e_hi) active[na++] = e;
+        off += s_cnt[e];
+      }
+    }
+    if (lane == 31) {
+      offsets[E] = off;
+      *n_active = na;
+    }
+    __syncwarp();
+    // stable placement, 32 entries at a time: rank among the same expert's
+    // entries of this group, after those of the earlier groups
+    for (int c0 = 0; c0 < n; c0 += 32) {
+      const int j = c0 + lane;
+      const int e = j < n ? s_ids[j] : -1;
+      const unsigned peers = __match_any_sync(0xffffffffu, e);
+      const int r = __popc(peers & ((1u << lane) - 1u));
+      if (j < n) list[s_off[e] + s_run[e] + r] = j;
+      __syncwarp();
+      if (j < n && r == 0) s_run[e] += __popc(peers);
+      __syncwarp();
+    }
   }
+}
+
+__global__ void __launch_bounds__(512) moe_route_kernel(const __half* __restrict__ logits, int B, int E, int topk,
+                                                        int e_lo, int e_hi, int* ids, float* wts, int* counts,
+                                                        int* offsets, int* list, int* active, int* n_active) {
+  pdl_wait_trigger();
+  extern __shared__ int sm_route[];
+  route_tokens(logits, B, E, topk, e_lo, e_hi, ids, wts, counts, offsets, list, active, n_active, sm_route);
+}
+
+// rrms of row b from the per-16-row sums of squares [parts][rows] (fixed
+// order: lane-strided partial sums, then lanes 0..31) — the arithmetic of
+// the GEMV prologue.  Called by warp 0; result in lane 0..31 alike.
+__device__ __forceinline__ float rrms_from_parts(const float* ss_in, int parts, int rows, int b, int D, float eps,
+                                                 int lane) {
+  float ss = 0.0f;
+  for (int i = lane; i < parts; i += 32) ss += ss_in[(long)i * rows + b];
+  float t = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) t += __shfl_sync(0xffffffffu, ss, i);
+  return rsqrtf(t / (float)D + eps);
+}
+
+// ------------------------------------------------------------ fused router
+// One pass for the router of a decode layer: xn = fp16(H32(r * rrms * w))
+// (when w is given; else xn is read as given), logits[b][e] = fp16(W_r[e] ·
+// xn[b]) with W_r fp16 [E, D] (H32-rotated), then the last CTA to finish
+// routes (route_tokens).  CTA (c, t): experts [8c, 8c + 8), one warp each
+// (the router row in registers, D <= 2048), tokens [16t, 16t + 16) staged in
+// shared memory.  `done` [1] int counts finished CTAs
+// and is reset by the last one.
+constexpr int kRouterTok = 16;
+__global__ void __launch_bounds__(256) moe_router_kernel(const __half* __restrict__ x, const float* __restrict__ ss_in,
+                                                         int parts, const __half* __restrict__ nw, float eps,
+                                                         __half* __restrict__ xn, const __half* __restrict__ wr,
+                                                         __half* logits, int B, int D, int E, int topk, int e_lo,
+                                                         int e_hi, int* ids, float* wts, int* counts, int* offsets,
+                                                         int* list, int* active, int* n_active, int* done) {
+  extern __shared__ __align__(16) uint8_t sm_r[];
+  __half* xs = reinterpret_cast<__half*>(sm_r);                  // [16][D]
+  __shared__ float s_rr[kRouterTok];
+  __shared__ int s_last;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int e = blockIdx.x * 8 + warp;
+  const int nv = D / 256;                                         // uint4 per lane
+  uint4 wv[8];
+  if (e < E) {                                                    // weights: no dependence on the previous kernel
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      if (i < nv) wv[i] = __ldg(reinterpret_cast<const uint4*>(wr + (long)e * D) + i * 32 + lane);
+  }
+  pdl_wait_trigger();
+  {
+    const int b0 = blockIdx.y * kRouterTok;          // this CTA's 16 tokens
+    const int nb = min(kRouterTok, B - b0);
+    if (nw) {
+      // one warp per (row, 32-block), 8 blocks per warp per round with their
+      // loads first; the first round's loads go out before the rrms is known.
+      // CTA c also stores the blocks c, c + G, ... of xn.
+      const int items = nb * (D / 32);                 // >= 8: every warp takes part in round 0
+      for (int i0 = warp; i0 < items; i0 += 64) {
+        float xv[8], wv8[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const int i = i0 + 8 * u;
+          if (i < items) {
+            const int r = i / (D / 32), k = (i - r * (D / 32)) * 32 + lane;
+            xv[u] = __half2float(x[(long)(b0 + r) * D + k]);
+            wv8[u] = __half2float(nw[k]);
+          }
+        }
+        if (i0 == warp) {
+          if (warp == 0)
+            for (int r = 0; r < nb; ++r) {
+              const float rr = rrms_from_parts(ss_in, parts, B, b0 + r, D, eps, lane);
+              if (lane == 0) s_rr[r] = rr;
+            }
+          __syncthreads();
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const int i = i0 + 8 * u;
+          if (i < items) {
+            const int r = i / (D / 32), blk = i - r * (D / 32), k = blk * 32 + lane;
+            const __half h = __float2half(fwht32_lane(xv[u] * s_rr[r] * wv8[u], lane));
+            xs[r * D + k] = h;
+            if (blk % gridDim.x == blockIdx.x) xn[(long)(b0 + r) * D + k] = h;
+          }
+        }
+      }
+    } else {
+      for (int i = tid; i < nb * (D / 8); i += 256) {
+        const int r = i / (D / 8), c = i - r * (D / 8);
+        reinterpret_cast<uint4*>(xs + r * D)[c] = reinterpret_cast<const uint4*>(xn + (long)(b0 + r) * D)[c];
+      }
+    }
+    __syncthreads();
+    if (e < E)
+      for (int r0 = 0; r0 < nb; r0 += 4) {             // 4 tokens at once: independent FMA chains
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          if (i < nv) {
+            const uint32_t wq[4] = {wv[i].x, wv[i].y, wv[i].z, wv[i].w};
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              const int r = min(r0 + u, nb - 1);
+              const uint4 xv = reinterpret_cast<const uint4*>(xs + r * D)[i * 32 + lane];
+              const uint32_t xq[4] = {xv.x, xv.y, xv.z, xv.w};
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                const float2 wf = __half22float2(u32_as_h2(wq[j])), xf = __half22float2(u32_as_h2(xq[j]));
+                acc[u] = fmaf(wf.x, xf.x, acc[u]);
+                acc[u] = fmaf(wf.y, xf.y, acc[u]);
+              }
+            }
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const float v = warp_sum(acc[u]);
+          if (lane == 0 && r0 + u < nb) logits[(long)(b0 + r0 + u) * E + e] = __float2half(v);
+        }
+      }
+  }
+  // ---- the last CTA routes
+  __threadfence();
   __syncthreads();
-  // stable placement: entry j goes after the earlier entries of its expert
-  for (int j = tid; j < B * topk; j += blockDim.x) {
-    const int e = s_ids[j];
-    int before = 0;
-    for (int i = 0; i < j; ++i) before += (s_ids[i] == e);
-    list[offsets[e] + before] = j;
-  }
+  if (tid == 0) s_last = (atomicAdd(done, 1) == (int)(gridDim.x * gridDim.y) - 1);
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  route_tokens(logits, B, E, topk, e_lo, e_hi, ids, wts, counts, offsets, list, active, n_active,
+               reinterpret_cast<int*>(sm_r));
+  if (tid == 0) *done = 0;
 }
 
 // ------------------------------------------------- row RMSNorm + H32 FWHT
@@ -120,6 +330,7 @@ __global__ void moe_route_kernel(const __half* __restrict__ logits, int B, int E
 // of the dense GEMVs as a standalone pass (rrms from ss_in partials or x).
 __global__ void norm_fwht_kernel(const __half* __restrict__ x, const float* __restrict__ ss_in, int parts,
                                  const __half* __restrict__ w, float eps, __half* __restrict__ y, int D) {
+  pdl_wait_trigger();
   const int b = blockIdx.x;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
   __shared__ float s_r;
@@ -149,147 +360,152 @@ __global__ void norm_fwht_kernel(const __half* __restrict__ x, const float* __re
   }
   __syncthreads();
   const float rr = s_r;
-  for (int blk = warp; blk < D / 32; blk += nw) {
-    const int i = blk * 32 + lane;
-    const float v = __half2float(xr[i]) * rr * __half2float(w[i]);
-    y[(long)b * D + i] = __float2half(fwht32_lane(v, lane));
+  for (int b0 = warp; b0 < D / 32; b0 += 8 * nw) {     // 8 blocks per warp per round, loads first
+    float xv[8], wv8[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int blk = b0 + u * nw;
+      if (blk < D / 32) {
+        xv[u] = __half2float(xr[blk * 32 + lane]);
+        wv8[u] = __half2float(w[blk * 32 + lane]);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int blk = b0 + u * nw;
+      if (blk < D / 32) y[(long)b * D + blk * 32 + lane] = __float2half(fwht32_lane(xv[u] * rr * wv8[u], lane));
+    }
   }
 }
 
 // ------------------------------------------------------ grouped expert GEMV
-// MODE 0 (gate_up): activation of entry j is xin[j / topk] (rows of K).
-// MODE 1 (down): activation of entry j is fp16(FWHT(silu(g) * u)), g, u =
-// halves of xin[j] (rows of 2K), one rounding (silu_hadamard_ds, :1031-1051).
+// MODE 0: plain, activation of entry j = xin[j / topk] (rows of K), y[j] [N].
+// MODE 1: plain, activation of entry j = xin[j].
+// MODE 2 (gate_up, N = 2 Ie): activation xin[j / topk]; y[j] [Ie] =
+// fp16(H32(silu(g) * u)), g, u = fp16 gate / up outputs, one rounding
+// (silu_hadamard_ds, :1031-1051).  Tile x of mode 2 covers gate rows
+// [32x, 32x + 32) (m-tiles 0, 1) and up rows Ie + [32x, 32x + 32) (2, 3).
 template <int MODE>
-__global__ void __launch_bounds__(kMoeThreads)
+__global__ void __launch_bounds__(kMoeThreads, 2)
     moe_gemv_kernel(const uint8_t* __restrict__ w, const __half* __restrict__ sz, const __half* __restrict__ xin,
                     long ldx, __half* __restrict__ y, long ldy, int N, int K, int topk, int e_lo,
                     const MoeRoute rt) {
-  const int a = blockIdx.y;
-  if (a >= *rt.n_active) return;
-  const int e = rt.active[a];
-  const int cnt = rt.counts[e];
-  const int* ent = rt.list + rt.offsets[e];
-  const int row0 = blockIdx.x * kMoeTile;
-  extern __shared__ __align__(16) uint8_t smem[];
-  __half* xs = reinterpret_cast<__half*>(smem);                           // [16][K + 8]
-  float* red = reinterpret_cast<float*>(xs + kMoeTokChunk * (K + 8));     // [3 quarters][4][2 ng][4][32]
-  const int ldxs = K + 8;
+  pdl_wait_trigger();
+  __shared__ float red[4][4][32];                 // K half 1 -> K half 0
+  __shared__ float cs[kMoeTok][64];               // mode 2: fp16-rounded gate | up per token
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, t = lane & 3;
-  const int mt = warp & 3, kh = warp >> 2;                // m-tile, K quarter
-  const int nblk = K / 32;
-  const int b0 = (nblk * kh) / kMoeKq, b1 = (nblk * (kh + 1)) / kMoeKq;
+  const int mt = warp & 3, kp = warp >> 2;
+  const int nbat = K / 128;                        // 4 blocks of 32 k per batch
+  const int q0 = (nbat * kp) / kMoeKp, q1 = (nbat * (kp + 1)) / kMoeKp;
   const long wrow = (long)K / 2, srow = (long)K / 16;
-  const int ra = row0 + mt * 16 + g, rb = ra + 8;
-  const long el = e - e_lo;                              // this GPU's expert slice starts at e_lo
-  const uint8_t* wa = w + (el * N + ra) * wrow;
-  const uint8_t* wb = w + (el * N + rb) * wrow;
-  const __half* sa = sz + (el * N + ra) * srow;
-  const __half* sb = sz + (el * N + rb) * srow;
+  const int tiles = N / 64;
+  const int items = *rt.n_active * tiles;          // (active expert, 64-row tile), tiles of an expert adjacent
+  for (int it = blockIdx.x; it < items; it += gridDim.x) {
+    const int a = it / tiles, tile = it - a * tiles;
+    const int e = rt.active[a];
+    const int cnt = rt.counts[e];
+    const int* ent = rt.list + rt.offsets[e];
+    int ra;
+    if (MODE == 2) ra = (mt < 2 ? 0 : N / 2) + tile * 32 + (mt & 1) * 16 + g;
+    else ra = tile * 64 + mt * 16 + g;
+    const long el = e - e_lo;                        // this GPU's expert slice starts at e_lo
+    const uint8_t* wa = w + (el * N + ra) * wrow + t * 16;
+    const uint8_t* wb = wa + 8 * wrow;
+    const __half* sa = sz + (el * N + ra) * srow + t * 2;
+    const __half* sb = sa + 8 * srow;
 
-  for (int c0 = 0; c0 < cnt; c0 += kMoeTokChunk) {
-    const int nc = min(kMoeTokChunk, cnt - c0);
-    __syncthreads();
-    // ---- stage the activations of tokens c0 .. c0 + nc (zeros past nc)
-    if (MODE == 0) {
-      for (int i = tid; i < kMoeTokChunk * (K / 8); i += kMoeThreads) {
-        const int r = i / (K / 8), c8 = i - r * (K / 8);
-        uint4 v = make_uint4(0, 0, 0, 0);
-        if (r < nc) v = *reinterpret_cast<const uint4*>(xin + (long)(ent[c0 + r] / topk) * ldx + c8 * 8);
-        *reinterpret_cast<uint4*>(xs + r * ldxs + c8 * 8) = v;
+    for (int c0 = 0; c0 < cnt; c0 += kMoeTok) {
+      const int nc = min(kMoeTok, cnt - c0);
+      const bool tok_ok = g < nc;
+      const __half* xr = xin + t * 32;
+      if (tok_ok) {
+        const int j = ent[c0 + g];
+        xr += (long)(MODE == 1 ? j : j / topk) * ldx;
       }
-    } else {
-      // one warp per (token, 32-block): silu(g) * u -> fp16 -> H32 -> fp16
-      for (int i = warp; i < kMoeTokChunk * nblk; i += kMoeThreads / 32) {
-        const int r = i / nblk, blk = i - r * nblk;
-        float v = 0.0f;
-        if (r < nc) {
-          const __half* xr = xin + (long)ent[c0 + r] * ldx;
-          const float gg = __half2float(xr[blk * 32 + lane]);
-          const float uu = __half2float(xr[K + blk * 32 + lane]);
-          v = fwht32_lane(gg / (1.0f + expf(-gg)) * uu, lane);
-        }
-        xs[r * ldxs + blk * 32 + lane] = __float2half(v);
-      }
-    }
-    __syncthreads();
-    float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-    const bool live = ra < N;
-    if (live) {
-      for (int bb = b0; bb < b1; bb += kMoeBatch) {
-        uint4 qa[kMoeBatch], qb[kMoeBatch];
-        __half2 pa[kMoeBatch], pb[kMoeBatch];
-#pragma unroll
-        for (int u = 0; u < kMoeBatch; ++u) {       // every load of the batch first
-          const int blk = min(bb + u, b1 - 1);
-          qa[u] = __ldg(reinterpret_cast<const uint4*>(wa + blk * 16));
-          qb[u] = __ldg(reinterpret_cast<const uint4*>(wb + blk * 16));
-          pa[u] = __ldg(reinterpret_cast<const __half2*>(sa + blk * 2));
-          pb[u] = __ldg(reinterpret_cast<const __half2*>(sb + blk * 2));
-        }
-#pragma unroll
-        for (int u = 0; u < kMoeBatch; ++u) {
-          const int blk = bb + u;
-          if (blk >= b1) break;
-          const uint32_t wa4[4] = {qa[u].x, qa[u].y, qa[u].z, qa[u].w}, wb4[4] = {qb[u].x, qb[u].y, qb[u].z, qb[u].w};
-          // this lane's bytes t, t + 4, t + 8, t + 12 of each row: k pairs
-          // (2t, 2t+1), (2t+8, 2t+9), (16+2t, ..), (24+2t, ..)
-          uint32_t fa[4], fb[4];
-          const __half2 s2a = __half2half2(__low2half(pa[u])),
-                        z2a = __hadd2(__half2half2(__high2half(pa[u])), __float2half2_rn(1024.0f));
-          const __half2 s2b = __half2half2(__low2half(pb[u])),
-                        z2b = __hadd2(__half2half2(__high2half(pb[u])), __float2half2_rn(1024.0f));
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const uint32_t byte_a = (wa4[q] >> (8 * t)) & 0xFFu;   // byte 4q + t
-            const uint32_t byte_b = (wb4[q] >> (8 * t)) & 0xFFu;
-            const uint32_t ha = (byte_a & 0xFu) | ((byte_a >> 4) << 16);
-            const uint32_t hb = (byte_b & 0xFu) | ((byte_b >> 4) << 16);
-            fa[q] = h2_as_u32(__hmul2(__hsub2(u32_as_h2(ha | 0x64006400u), z2a), s2a));
-            fb[q] = h2_as_u32(__hmul2(__hsub2(u32_as_h2(hb | 0x64006400u), z2b), s2b));
+      float acc[4] = {0.f, 0.f, 0.f, 0.f};
+      for (int q = q0; q < q1; q += kMoeUnroll) {
+        uint4 qa[kMoeUnroll], qb[kMoeUnroll];
+        uint32_t pa[kMoeUnroll], pb[kMoeUnroll];
+  #pragma unroll
+        for (int u = 0; u < kMoeUnroll; ++u) {          // every weight load of the batches first
+          if (q + u < q1) {
+            qa[u] = __ldg(reinterpret_cast<const uint4*>(wa + (long)(q + u) * 64));
+            qb[u] = __ldg(reinterpret_cast<const uint4*>(wb + (long)(q + u) * 64));
+            pa[u] = __ldg(reinterpret_cast<const unsigned*>(sa + (q + u) * 8));
+            pb[u] = __ldg(reinterpret_cast<const unsigned*>(sb + (q + u) * 8));
           }
-          const int kb = blk * 32;
-#pragma unroll
-          for (int ks = 0; ks < 2; ++ks) {
-            const uint32_t a0 = fa[2 * ks], a1 = fb[2 * ks], a2 = fa[2 * ks + 1], a3 = fb[2 * ks + 1];
-#pragma unroll
-            for (int ng = 0; ng < 2; ++ng) {
-              const __half* xr = xs + (ng * 8 + g) * ldxs + kb + ks * 16 + 2 * t;
-              const uint32_t bb0 = *reinterpret_cast<const uint32_t*>(xr);
-              const uint32_t bb1 = *reinterpret_cast<const uint32_t*>(xr + 8);
-              mma16816(acc[ng], a0, a1, a2, a3, bb0, bb1);
+        }
+  #pragma unroll
+        for (int u = 0; u < kMoeUnroll; ++u) {
+          if (q + u >= q1) break;
+          uint4 xv[4];
+  #pragma unroll
+          for (int i = 0; i < 4; ++i)
+            xv[i] = tok_ok ? __ldg(reinterpret_cast<const uint4*>(xr + (long)(q + u) * 128 + 8 * i))
+                           : make_uint4(0, 0, 0, 0);
+          const __half2 pha = u32_as_h2(pa[u]), phb = u32_as_h2(pb[u]);
+          const __half2 s2a = __half2half2(__low2half(pha)),
+                        z2a = __hadd2(__half2half2(__high2half(pha)), __float2half2_rn(1024.0f));
+          const __half2 s2b = __half2half2(__low2half(phb)),
+                        z2b = __hadd2(__half2half2(__high2half(phb)), __float2half2_rn(1024.0f));
+          const uint32_t wa4[4] = {qa[u].x, qa[u].y, qa[u].z, qa[u].w};
+          const uint32_t wb4[4] = {qb[u].x, qb[u].y, qb[u].z, qb[u].w};
+  #pragma unroll
+          for (int jj = 0; jj < 8; ++jj) {
+            // k-step jj: this lane's block bytes 2jj (k 4jj, 4jj+1) and 2jj+1
+            // (k 4jj+2, 4jj+3) stand for fragment k (2t, 2t+1) and (2t+8, 2t+9)
+            const int sh = 16 * (jj & 1);
+            const uint32_t wA = wa4[jj >> 1] >> sh, wB = wb4[jj >> 1] >> sh;
+            const uint32_t lA = (wA & 0xFu) | (((wA >> 4) & 0xFu) << 16);
+            const uint32_t hA = ((wA >> 8) & 0xFu) | (((wA >> 12) & 0xFu) << 16);
+            const uint32_t lB = (wB & 0xFu) | (((wB >> 4) & 0xFu) << 16);
+            const uint32_t hB = ((wB >> 8) & 0xFu) | (((wB >> 12) & 0xFu) << 16);
+            const uint32_t a0 = h2_as_u32(__hmul2(__hsub2(u32_as_h2(lA | 0x64006400u), z2a), s2a));
+            const uint32_t a2 = h2_as_u32(__hmul2(__hsub2(u32_as_h2(hA | 0x64006400u), z2a), s2a));
+            const uint32_t a1 = h2_as_u32(__hmul2(__hsub2(u32_as_h2(lB | 0x64006400u), z2b), s2b));
+            const uint32_t a3 = h2_as_u32(__hmul2(__hsub2(u32_as_h2(hB | 0x64006400u), z2b), s2b));
+            const uint4 xq = xv[jj >> 1];
+            const uint32_t b0 = (jj & 1) ? xq.z : xq.x, b1 = (jj & 1) ? xq.w : xq.y;
+            mma16816(acc, a0, a1, a2, a3, b0, b1);
+          }
+        }
+      }
+      // ---- K half 1 hands its partial to K half 0 (fixed order)
+      if (kp == 1) {
+  #pragma unroll
+        for (int i = 0; i < 4; ++i) red[mt][i][lane] = acc[i];
+      }
+      __syncthreads();
+      if (kp == 0) {
+  #pragma unroll
+        for (int i = 0; i < 4; ++i) acc[i] += red[mt][i][lane];
+        // C: (row g, tokens 2t, 2t+1), (row g + 8, tokens 2t, 2t+1)
+        if (MODE == 2) {
+  #pragma unroll
+          for (int i = 0; i < 4; ++i)
+            cs[2 * t + (i & 1)][mt * 16 + g + 8 * (i >> 1)] = __half2float(__float2half(acc[i]));
+        } else {
+  #pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const int tok = 2 * t + h;
+            if (tok < nc) {
+              __half* yr = y + (long)ent[c0 + tok] * ldy;
+              yr[ra] = __float2half(acc[h]);
+              yr[ra + 8] = __float2half(acc[2 + h]);
             }
           }
         }
       }
-    }
-    // ---- the K quarters meet in shared memory (fixed order); quarter 0 writes
-    if (kh != 0) {
-#pragma unroll
-      for (int ng = 0; ng < 2; ++ng)
-#pragma unroll
-        for (int i = 0; i < 4; ++i) red[((((kh - 1) * 4 + mt) * 2 + ng) * 4 + i) * 32 + lane] = acc[ng][i];
-    }
-    __syncthreads();
-    if (kh == 0 && live) {
-#pragma unroll
-      for (int ng = 0; ng < 2; ++ng) {
-#pragma unroll
-        for (int i = 0; i < 4; ++i)
-#pragma unroll
-          for (int q = 0; q < kMoeKq - 1; ++q) acc[ng][i] += red[(((q * 4 + mt) * 2 + ng) * 4 + i) * 32 + lane];
-        // C: (row g, tokens 2t, 2t+1), (row g + 8, tokens 2t, 2t+1)
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const int tok = ng * 8 + 2 * t + h;
-          if (tok < nc) {
-            __half* yr = y + (long)ent[c0 + tok] * ldy;
-            yr[ra] = __float2half(acc[ng][h]);
-            if (rb < N) yr[rb] = __float2half(acc[ng][2 + h]);
-          }
+      if (MODE == 2) {
+        __syncthreads();
+        if (warp < nc) {      // warp = token of the pass
+          const float gg = cs[warp][lane], uu = cs[warp][32 + lane];
+          const float v = fwht32_lane(gg / (1.0f + expf(-gg)) * uu, lane);
+          y[(long)ent[c0 + warp] * ldy + tile * 32 + lane] = __float2half(v);
         }
       }
+      __syncthreads();        // red / cs are rewritten by the next pass
     }
   }
 }
@@ -302,6 +518,7 @@ __global__ void __launch_bounds__(kMoeThreads)
 __global__ void moe_combine_kernel(const __half* __restrict__ yk, const float* __restrict__ wts,
                                    const int* __restrict__ ids, int e_lo, int e_hi, const __half* res, __half* out,
                                    float* __restrict__ out32, float* __restrict__ ss_out, int B, int D, int topk) {
+  pdl_wait_trigger();
   const long i = ((long)blockIdx.x * blockDim.x + threadIdx.x) * 4;
   const bool ok = i < (long)B * D;
   float sq = 0.0f;
@@ -342,6 +559,7 @@ __global__ void moe_combine_kernel(const __half* __restrict__ yk, const float* _
 template <bool F16>
 __global__ void residual_f32_kernel(const void* __restrict__ sumv, const __half* res, __half* out,
                                     float* __restrict__ ss_out, int B, int D) {
+  pdl_wait_trigger();
   const long i = ((long)blockIdx.x * blockDim.x + threadIdx.x) * 4;
   const bool ok = i < (long)B * D;
   float sq = 0.0f;
@@ -368,52 +586,90 @@ __global__ void residual_f32_kernel(const void* __restrict__ sumv, const __half*
 
 using namespace r4q;
 
+static int pdl_status(cudaError_t e, const char* what) {
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return set_error(R4Q_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+  }
+  return R4Q_OK;
+}
+
 extern "C" int r4q_moe_route(const void* logits, int B, int E, int topk, int e_lo, int e_hi, int* ids, float* wts,
                              int* counts, int* offsets, int* list, int* active, int* n_active, void* stream) {
   if (!logits || !ids || !wts || !counts || !offsets || !list || !active || !n_active || B < 1 || E < 1 ||
       E > 256 || topk < 1 || topk > 16 || topk > E || B * topk > 4096 || e_lo < 0 || e_hi > E || e_lo >= e_hi)
     return set_error(R4Q_ERR_ARG, "moe_route: bad arguments (B %d E %d topk %d)", B, E, topk);
-  const size_t smem = (size_t)(E + B * topk) * sizeof(int);
-  moe_route_kernel<<<1, 512, smem, (cudaStream_t)stream>>>((const __half*)logits, B, E, topk, e_lo, e_hi, ids, wts,
-                                                          counts, offsets, list, active, n_active);
-  return check_launch("moe_route_kernel");
+  const size_t smem = (size_t)(3 * E + B * topk) * sizeof(int);
+  return pdl_status(launch_pdl(moe_route_kernel, dim3(1), dim3(512), smem, (cudaStream_t)stream,
+                               (const __half*)logits, B, E, topk, e_lo, e_hi, ids, wts, counts, offsets, list, active,
+                               n_active), "moe_route_kernel");
+}
+
+extern "C" int r4q_moe_router(const void* x, const float* ss_in, int ss_parts, const void* norm_w, float eps,
+                              void* xn, const void* router_w, void* logits, int B, int D, int E, int topk, int e_lo,
+                              int e_hi, int* ids, float* wts, int* counts, int* offsets, int* list, int* active,
+                              int* n_active, int* done, void* stream) {
+  if (!xn || !router_w || !logits || !ids || !wts || !counts || !offsets || !list || !active || !n_active || !done ||
+      B < 1 || D < 256 || D % 256 || D > 2048 || E < 1 || E > 256 || topk < 1 || topk > 16 || topk > E ||
+      B * topk > 4096 || e_lo < 0 || e_hi > E || e_lo >= e_hi || (norm_w && (!x || !ss_in || ss_parts < 1)))
+    return set_error(R4Q_ERR_ARG, "moe_router: bad arguments (B %d D %d E %d topk %d)", B, D, E, topk);
+  if (!aligned(router_w, 16) || !aligned(xn, 16))
+    return set_error(R4Q_ERR_ALIGN, "moe_router: router weights / xn not 16-byte aligned");
+  const size_t smem_x = (size_t)kRouterTok * D * 2, smem_r = (size_t)(3 * E + B * topk) * sizeof(int);
+  const size_t smem = smem_x > smem_r ? smem_x : smem_r;
+  if (smem > 48 * 1024) {
+    static std::atomic<size_t> set_to{0};
+    if (set_to.load() < smem) {
+      cudaFuncSetAttribute(moe_router_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      set_to.store(smem);
+    }
+  }
+  return pdl_status(launch_pdl(moe_router_kernel, dim3((E + 7) / 8, (B + kRouterTok - 1) / kRouterTok), dim3(256), smem, (cudaStream_t)stream,
+                               (const __half*)x, ss_in, ss_parts, (const __half*)norm_w, eps, (__half*)xn,
+                               (const __half*)router_w, (__half*)logits, B, D, E, topk, e_lo, e_hi, ids, wts, counts,
+                               offsets, list, active, n_active, done),
+                    "moe_router_kernel");
 }
 
 extern "C" int r4q_norm_fwht_rows(const void* x, const float* ss_in, int ss_parts, const void* w, float eps, void* y,
                                   int rows, int D, void* stream) {
   if (!x || !w || !y || rows < 1 || D < 32 || D % 32 || (ss_in && ss_parts < 1))
     return set_error(R4Q_ERR_ARG, "norm_fwht_rows: bad arguments");
-  norm_fwht_kernel<<<rows, 256, 0, (cudaStream_t)stream>>>((const __half*)x, ss_in, ss_parts, (const __half*)w, eps,
-                                                           (__half*)y, D);
-  return check_launch("norm_fwht_kernel");
+  return pdl_status(launch_pdl(norm_fwht_kernel, dim3(rows), dim3(256), 0, (cudaStream_t)stream, (const __half*)x,
+                               ss_in, ss_parts, (const __half*)w, eps, (__half*)y, D), "norm_fwht_kernel");
 }
 
 extern "C" int r4q_moe_gemv(int mode, const void* w, const void* sz, const void* x, long ldx, void* y, long ldy,
                             int N, int K, int E, int e_lo, int e_hi, int B, int topk, const int* counts,
                             const int* offsets, const int* list, const int* active, const int* n_active,
                             void* stream) {
-  if (!w || !sz || !x || !y || !counts || !offsets || !list || !active || !n_active || N < 16 || N % 16 ||
-      K < 32 || K % 32 || E < 1 || B < 1 || topk < 1 || (mode != 0 && mode != 1) || e_lo < 0 || e_hi > E ||
+  if (!w || !sz || !x || !y || !counts || !offsets || !list || !active || !n_active || N < 64 || N % 64 ||
+      K < 128 || K % 128 || E < 1 || B < 1 || topk < 1 || mode < 0 || mode > 2 || e_lo < 0 || e_hi > E ||
       e_lo >= e_hi)
-    return set_error(R4Q_ERR_ARG, "moe_gemv: bad arguments (N %d K %d)", N, K);
+    return set_error(R4Q_ERR_ARG, "moe_gemv: bad arguments (mode %d N %d K %d; N %% 64, K %% 128)", mode, N, K);
   if (!aligned(w, 16) || !aligned(sz, 4) || !aligned(x, 16) || ldx % 8)
     return set_error(R4Q_ERR_ALIGN, "moe_gemv: weights / activations misaligned");
   MoeRoute rt{counts, offsets, list, active, n_active};
-  const size_t smem = (size_t)kMoeTokChunk * (K + 8) * 2 + (kMoeKq - 1) * 4 * 2 * 4 * 32 * 4;
   const int el = e_hi - e_lo;
   const int slots = (el < B * topk) ? el : B * topk;
-  dim3 grid((N + kMoeTile - 1) / kMoeTile, slots);
+  // one CTA per (active-expert slot, tile); the kernel also runs as a
+  // persistent grid (R4Q_MOE_GRID = CTA count, measurement only) — measured
+  // on B200 the full grid is faster (B = 64: 101 us against 115 us for 296
+  // persistent CTAs, gate_up of 127 experts)
+  static const int forced = [] {
+    const char* v = getenv("R4Q_MOE_GRID");
+    return v ? atoi(v) : -1;
+  }();
+  const long items_max = (long)slots * (N / 64);
+  long ctas = forced > 0 ? forced : items_max;
+  if (ctas > items_max) ctas = items_max;
+  dim3 grid((unsigned)ctas);
   cudaStream_t st = (cudaStream_t)stream;
-  if (mode == 0) {
-    if (smem > 48 * 1024) cudaFuncSetAttribute(moe_gemv_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    moe_gemv_kernel<0><<<grid, kMoeThreads, smem, st>>>((const uint8_t*)w, (const __half*)sz, (const __half*)x, ldx,
-                                                        (__half*)y, ldy, N, K, topk, e_lo, rt);
-  } else {
-    if (smem > 48 * 1024) cudaFuncSetAttribute(moe_gemv_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    moe_gemv_kernel<1><<<grid, kMoeThreads, smem, st>>>((const uint8_t*)w, (const __half*)sz, (const __half*)x, ldx,
-                                                        (__half*)y, ldy, N, K, topk, e_lo, rt);
-  }
-  return check_launch("moe_gemv_kernel");
+  const uint8_t* wp = (const uint8_t*)w;
+  const __half *sp = (const __half*)sz, *xp = (const __half*)x;
+  auto k = mode == 0 ? moe_gemv_kernel<0> : mode == 1 ? moe_gemv_kernel<1> : moe_gemv_kernel<2>;
+  return pdl_status(launch_pdl(k, grid, dim3(kMoeThreads), 0, st, wp, sp, xp, ldx, (__half*)y, ldy, N, K, topk, e_lo,
+                               rt), "moe_gemv_kernel");
 }
 
 extern "C" int r4q_moe_combine(const void* yk, const float* wts, const int* ids, int e_lo, int e_hi, const void* res,
@@ -421,25 +677,25 @@ extern "C" int r4q_moe_combine(const void* yk, const float* wts, const int* ids,
   if (!yk || !wts || !ids || (!out && !out32) || B < 1 || D < 16 || D % 16 || topk < 1 || e_lo >= e_hi)
     return set_error(R4Q_ERR_ARG, "moe_combine: bad arguments");
   const long n4 = (long)B * D / 4;
-  moe_combine_kernel<<<(unsigned)((n4 + 255) / 256), 256, 0, (cudaStream_t)stream>>>(
-      (const __half*)yk, wts, ids, e_lo, e_hi, (const __half*)res, (__half*)out, out32, ss_out, B, D, topk);
-  return check_launch("moe_combine_kernel");
+  return pdl_status(launch_pdl(moe_combine_kernel, dim3((unsigned)((n4 + 255) / 256)), dim3(256), 0,
+                               (cudaStream_t)stream, (const __half*)yk, wts, ids, e_lo, e_hi, (const __half*)res,
+                               (__half*)out, out32, ss_out, B, D, topk), "moe_combine_kernel");
 }
 
 extern "C" int r4q_residual_f32(const float* sum, const void* res, void* out, float* ss_out, int B, int D,
                                 void* stream) {
   if (!sum || !out || B < 1 || D < 16 || D % 16) return set_error(R4Q_ERR_ARG, "residual_f32: bad arguments");
   const long n4 = (long)B * D / 4;
-  residual_f32_kernel<false><<<(unsigned)((n4 + 255) / 256), 256, 0, (cudaStream_t)stream>>>(
-      sum, (const __half*)res, (__half*)out, ss_out, B, D);
-  return check_launch("residual_f32_kernel");
+  return pdl_status(launch_pdl(residual_f32_kernel<false>, dim3((unsigned)((n4 + 255) / 256)), dim3(256), 0,
+                               (cudaStream_t)stream, (const void*)sum, (const __half*)res, (__half*)out, ss_out, B, D),
+                    "residual_f32_kernel");
 }
 
 extern "C" int r4q_residual_f16(const void* a, const void* res, void* out, float* ss_out, int B, int D,
                                 void* stream) {
   if (!a || !out || B < 1 || D < 16 || D % 16) return set_error(R4Q_ERR_ARG, "residual_f16: bad arguments");
   const long n4 = (long)B * D / 4;
-  residual_f32_kernel<true><<<(unsigned)((n4 + 255) / 256), 256, 0, (cudaStream_t)stream>>>(
-      a, (const __half*)res, (__half*)out, ss_out, B, D);
-  return check_launch("residual_f16_kernel");
+  return pdl_status(launch_pdl(residual_f32_kernel<true>, dim3((unsigned)((n4 + 255) / 256)), dim3(256), 0,
+                               (cudaStream_t)stream, a, (const __half*)res, (__half*)out, ss_out, B, D),
+                    "residual_f16_kernel");
 }

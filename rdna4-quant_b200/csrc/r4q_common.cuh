@@ -19,7 +19,33 @@ int check_launch(const char* what);
 int num_sms();
 inline bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
+// Launch with programmatic dependent launch allowed: the kernel's CTAs may
+// be scheduled while the previous kernel of the stream finishes, so the
+// kernel must call pdl_wait() before touching anything that kernel writes.
+// Hides the launch gap between the short kernels of a decode step.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                              Args... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
 // ------------------------------------------------------------- device side
+// wait for the previous kernel of the stream (complete, writes visible), then
+// let the next one be scheduled
+__device__ __forceinline__ void pdl_wait_trigger() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
 __device__ __forceinline__ uint32_t lop3_and_or(uint32_t a, uint32_t mask, uint32_t orv) {
   uint32_t d;
   // (a & mask) | orv  -> immediate LUT 0xEA

@@ -88,6 +88,8 @@ _SIGS = {
     "r4q_kv_write_rows": (i32, [vp, vp, i64, vp, vp, i32, i32, i32, i32, i32, i32, vp, vp, vp]),
     "r4q_moe_route": (i32, [vp, i32, i32, i32, i32, i32, vp, vp, vp, vp, vp, vp, vp, vp]),
     "r4q_norm_fwht_rows": (i32, [vp, vp, i32, vp, f32, vp, i32, i32, vp]),
+    "r4q_moe_router": (i32, [vp, vp, i32, vp, f32, vp, vp, vp, i32, i32, i32, i32, i32, i32, vp, vp, vp, vp, vp, vp,
+                             vp, vp, vp]),
     "r4q_moe_gemv": (i32, [i32, vp, vp, vp, i64, vp, i64, i32, i32, i32, i32, i32, i32, i32, vp, vp, vp, vp, vp,
                            vp]),
     "r4q_moe_combine": (i32, [vp, vp, vp, i32, i32, vp, vp, vp, vp, i32, i32, i32, vp]),

@@ -274,6 +274,7 @@ class MoeRouteBuffers:
         self.list = torch.empty(B * topk, **i32)
         self.active = torch.empty(E, **i32)
         self.n_active = torch.empty(1, **i32)
+        self.done = torch.zeros(1, **i32)          # CTA counter of the fused router (kept zero between calls)
 
 
 def moe_route(logits: torch.Tensor, topk: int, rb: MoeRouteBuffers | None = None) -> MoeRouteBuffers:
@@ -284,6 +285,25 @@ def moe_route(logits: torch.Tensor, topk: int, rb: MoeRouteBuffers | None = None
            rb.counts.data_ptr(), rb.offsets.data_ptr(), rb.list.data_ptr(), rb.active.data_ptr(),
            rb.n_active.data_ptr(), stream_handle(dev))
     return rb
+
+
+def moe_router(xn: torch.Tensor, router_w: torch.Tensor, topk: int, rb: MoeRouteBuffers,
+               logits: torch.Tensor | None = None, x: torch.Tensor | None = None, ss_in: torch.Tensor | None = None,
+               norm_w: torch.Tensor | None = None, eps: float = 1e-6) -> torch.Tensor:
+    """Fused router (r4q_moe_router): with x / ss_in / norm_w, xn is written
+    as fp16(H32(RMSNorm(x))); otherwise xn is the given normalised input.
+    Router logits fp16 [B, E] go to ``logits`` (returned) and the routing to rb."""
+    dev = _require_cuda(xn, router_w)
+    B, D = xn.shape
+    E = router_w.shape[0]
+    lg = logits if logits is not None else torch.empty(B, E, dtype=torch.float16, device=dev)
+    if norm_w is not None and (x is None or ss_in is None):
+        raise ValueError("moe_router: the fused norm needs x and ss_in")
+    L.call("r4q_moe_router", _ptr(x), _ptr(ss_in), 0 if ss_in is None else int(ss_in.shape[0]), _ptr(norm_w),
+           float(eps), xn.data_ptr(), router_w.data_ptr(), lg.data_ptr(), B, D, E, topk, rb.e_lo, rb.e_hi,
+           rb.ids.data_ptr(), rb.wts.data_ptr(), rb.counts.data_ptr(), rb.offsets.data_ptr(), rb.list.data_ptr(),
+           rb.active.data_ptr(), rb.n_active.data_ptr(), rb.done.data_ptr(), stream_handle(dev))
+    return lg
 
 
 def norm_fwht_rows(x: torch.Tensor, w: torch.Tensor, eps: float = 1e-6, ss_in: torch.Tensor | None = None,
@@ -299,10 +319,14 @@ def norm_fwht_rows(x: torch.Tensor, w: torch.Tensor, eps: float = 1e-6, ss_in: t
 def moe_gemv(mode: int, w: torch.Tensor, sz: torch.Tensor, x: torch.Tensor, rb: MoeRouteBuffers, N: int, K: int,
              out: torch.Tensor | None = None) -> torch.Tensor:
     """Grouped INT4 expert GEMV (r4q_moe_gemv) over experts [rb.e_lo, rb.e_hi);
-    w [(e_hi-e_lo)*N, K/2], sz [(e_hi-e_lo)*N, K/16]; returns y [B*topk, N]
-    (one row per routed entry; rows of other GPUs' experts untouched)."""
+    w [(e_hi-e_lo)*N, K/2], sz [(e_hi-e_lo)*N, K/16].  mode 0: x rows are
+    tokens (entry j reads x[j // topk]); mode 1: x rows are entries; mode 2:
+    gate_up (N = 2 Ie) with the SiLU(gate)*up + H32 FWHT epilogue, x rows
+    tokens.  Returns y [B*topk, N] (mode 2: [B*topk, N/2]), one row per routed
+    entry; rows of other GPUs' experts untouched."""
     dev = _require_cuda(w, sz, x)
-    y = out if out is not None else torch.empty(rb.B * rb.topk, N, dtype=torch.float16, device=dev)
+    y = out if out is not None else torch.empty(rb.B * rb.topk, N // 2 if mode == 2 else N, dtype=torch.float16,
+                                                device=dev)
     L.call("r4q_moe_gemv", mode, w.data_ptr(), sz.data_ptr(), x.data_ptr(), x.stride(0), y.data_ptr(), y.stride(0),
            N, K, rb.E, rb.e_lo, rb.e_hi, rb.B, rb.topk, rb.counts.data_ptr(), rb.offsets.data_ptr(), rb.list.data_ptr(),
            rb.active.data_ptr(), rb.n_active.data_ptr(), stream_handle(dev))

@@ -6,7 +6,8 @@ the oracle top-k of the logits the device computed (bit-exact selection and
 1e-6 weights), and the rest of the step is compared given that routing —
 decode-step tolerance 2e-3 (see test_gpu_decode).  Plus the grouped expert
 GEMV on its own at 1e-3 for batches 1, 5 and 40 (tokens per expert above one
-16-token chunk), and graph == eager."""
+8-token pass) in its three modes (plain rows of tokens, plain rows of
+entries, gate_up with the SiLU*up + FWHT epilogue), and graph == eager."""
 import numpy as np
 import pytest
 import torch
@@ -39,7 +40,8 @@ def test_grouped_expert_gemv(B):
     x = torch.randn(B, D, generator=g, device=dev).half()
     rb = ops.moe_route(logits, k)
     gu = ops.moe_gemv(0, wgu, sgu, x, rb, 2 * Ie, D)
-    yk = ops.moe_gemv(1, wd, sd, gu, rb, D, Ie)
+    act = ops.moe_gemv(2, wgu, sgu, x, rb, 2 * Ie, D)
+    yk = ops.moe_gemv(1, wd, sd, act, rb, D, Ie)
     ids, w = O.moe_route(_np(logits), k)
     assert np.array_equal(_np(rb.ids), ids)
     assert np.allclose(_np(rb.wts), w, rtol=1e-5, atol=1e-6)
@@ -49,8 +51,9 @@ def test_grouped_expert_gemv(B):
             e = int(ids[b, j])
             ref_gu = O.linear(_np(x)[b:b + 1], _lin4(wgu, sgu, e, 2 * Ie))
             close(_np(gu)[b * k + j:b * k + j + 1], ref_gu)
-            act = O.silu_fwht(_np(gu)[b * k + j:b * k + j + 1, :Ie], _np(gu)[b * k + j:b * k + j + 1, Ie:])
-            close(_np(yk)[b * k + j:b * k + j + 1], O.linear(act, _lin4(wd, sd, e, D)))
+            ref_act = O.silu_fwht(_np(gu)[b * k + j:b * k + j + 1, :Ie], _np(gu)[b * k + j:b * k + j + 1, Ie:])
+            close(_np(act)[b * k + j:b * k + j + 1], ref_act)
+            close(_np(yk)[b * k + j:b * k + j + 1], O.linear(_np(act)[b * k + j:b * k + j + 1], _lin4(wd, sd, e, D)))
     # grouping: every entry once, experts ascending, token order inside
     cnt, off, lst = _np(rb.counts), _np(rb.offsets), _np(rb.list)
     for e in range(E):
@@ -59,7 +62,41 @@ def test_grouped_expert_gemv(B):
     assert sorted(lst.tolist()) == list(range(B * k))
 
 
-@pytest.mark.parametrize("B", [1, 4, 20])
+@pytest.mark.parametrize("B", [1, 3, 40])
+def test_fused_router(B):
+    """r4q_moe_router: xn bit-identical to the row RMSNorm+FWHT pass, logits
+    within fp16 rounding of xn · W_r, routing identical to r4q_moe_route on
+    those logits; the precomputed-xn form gives the same logits; a second
+    call (CTA counter reset by the kernel) repeats the first."""
+    from r4q import ops
+    dev = torch.device('cuda')
+    g = torch.Generator(device=dev).manual_seed(40 + B)
+    E, k, D = 16, 4, 256
+    r = torch.randn(B, D, generator=g, device=dev).half()
+    nw = (1 + 0.1 * torch.randn(D, generator=g, device=dev)).half()
+    wr = (torch.randn(E, D, generator=g, device=dev) * 0.05).half()
+    ss = (r.float() ** 2).view(B, D // 16, 16).sum(-1).t().contiguous()       # [D/16, B]
+    ref_xn = ops.norm_fwht_rows(r, nw, 1e-6, ss_in=ss)
+    rb = ops.MoeRouteBuffers(B, E, k, dev)
+    xn = torch.empty(B, D, dtype=torch.float16, device=dev)
+    lg = ops.moe_router(xn, wr, k, rb, x=r, ss_in=ss, norm_w=nw, eps=1e-6)
+    torch.cuda.synchronize()
+    assert torch.equal(xn, ref_xn)
+    close(_np(lg), (ref_xn.float() @ wr.float().t()).cpu().numpy(), 1e-3)
+    rb2 = ops.moe_route(lg, k, ops.MoeRouteBuffers(B, E, k, dev))
+    for name in ('ids', 'wts', 'counts', 'offsets', 'list', 'n_active'):
+        assert torch.equal(getattr(rb, name), getattr(rb2, name)), name
+    na = int(rb.n_active.item())
+    assert torch.equal(rb.active[:na], rb2.active[:na])
+    rb3 = ops.MoeRouteBuffers(B, E, k, dev)
+    lg3 = ops.moe_router(ref_xn.clone(), wr, k, rb3)
+    lg4 = ops.moe_router(ref_xn.clone(), wr, k, rb3)
+    torch.cuda.synchronize()
+    assert torch.equal(lg3, lg) and torch.equal(lg4, lg) and torch.equal(rb3.ids, rb.ids)
+    assert int(rb.done.item()) == 0 and int(rb3.done.item()) == 0
+
+
+@pytest.mark.parametrize("B", [1, 4, 7, 20])
 def test_moe_decode_step_vs_oracle(B):
     from r4q import moe
     dev = torch.device('cuda')
