@@ -192,6 +192,11 @@ int r4q_gemm_fp16(const void* x, long ldx, const void* w, void* y, long ldy, int
  * reference prefill (:1973-1988) in one pass over the weights.  K % 64 == 0. */
 int r4q_gemm_int4(const void* x, long ldx, const void* w, const void* sz, void* y, long ldy, int M, int N,
                   int K, void* workspace, size_t ws_bytes, void* stream);
+/* Workspace bytes for r4q_gemm_fp16 / r4q_gemm_int4 at this shape (16-byte
+ * aligned, zeroed once; the kernels leave it zero).  Decode-sized M splits K
+ * over the SMs and needs fp32 partials; with a smaller workspace the split
+ * count drops (256 bytes: no split). */
+size_t r4q_gemm_workspace_bytes(int M, int N, int K);
 
 /* Row kernels of the batched prefill (int4_decode_step.hip:766-792, 2112-2124):
  * y = fp16(H32 x) on every 32-block of rows x K; y = fp16(silu(g) * u) with

@@ -7,11 +7,12 @@
 //
 // B200 design (one 128 x 256 output tile per CTA, 8 warps):
 //  * warp 0, one lane: TMA producer.  X tiles [128 x 64] and W tiles
-//    [256 x 64] (fp16, K-major, 128-byte swizzle) into a 4-stage ring with
+//    [256 x 64] (fp16, K-major, 128-byte swizzle) into a 3-stage ring with
 //    mbarrier transaction counts;
 //  * INT4 weights (`w4` set): warps 2-7 dequantise instead of TMA-loading W:
-//    the nibbles come in by TMA, the (scale, zero) pairs by plain loads (8 bytes
-//    per row and stage, below TMA's 16-byte box minimum), the exact reference value
+//    the nibbles come in by TMA, the (scale, zero) pairs by the producer warp's
+//    cp.async (8 bytes per row and stage, below TMA's 16-byte box minimum) into
+//    the same stage, completing on the same mbarrier; the exact reference value
 //    fp16((q - z) · s) is written into the same swizzled fp16 layout, then
 //    fence.proxy.async makes it visible to the tensor cores;
 //  * warp 1, one lane: issues tcgen05.mma.cta_group::1.kind::f16 (M = 128,
@@ -20,10 +21,14 @@
 //    tcgen05.commit releases each stage back to the producer;
 //  * all 8 warps: epilogue, tcgen05.ld of their 32 accumulator lanes (= rows)
 //    and half of the columns, fp16 conversion, stores.
+// Decode-sized M (few output tiles): the K range is split over gridDim.z so
+// the grid covers the SMs; each split writes an fp32 partial and the tile's
+// last CTA to arrive sums them in split order (deterministic).
 // Every mbarrier wait is bounded; a timeout sets the status word and the
 // kernel drains.  No multicast anywhere.
 #include <cuda.h>
 
+#include <cstdlib>
 #include <mutex>
 
 #include "r4q_common.cuh"
@@ -32,10 +37,11 @@ namespace r4q {
 namespace {
 
 constexpr int kBM = 128, kBN = 256, kBK = 64;
-constexpr int kStages = 4;
+constexpr int kStages = 3;
 constexpr int kABytes = kBM * kBK * 2;             // 16 KB
 constexpr int kBBytes = kBN * kBK * 2;             // 32 KB
 constexpr int kW4Bytes = kBN * kBK / 2;            // 8 KB of nibbles per stage
+constexpr int kPairBytes = kBN * 8;                // (scale, zero) of 2 blocks per row per stage
 constexpr int kGemmThreads = 256;   // 8 warps
 constexpr int kDequantThreads = kGemmThreads - 64;
 constexpr long kGemmSpin = 1L << 26;
@@ -47,6 +53,9 @@ struct GemmParams {
   int M, N, K;
   int w4;          // 1: W is INT4 (nibbles + pairs), dequantised in the kernel
   int* status;
+  int splits;      // K splits (gridDim.z); > 1: fp32 partials merged by the tile's last CTA
+  unsigned* cnt;   // [tiles] arrival counters (left zero)
+  float* part;     // [splits][M][N] fp32 partials
 };
 
 __device__ __forceinline__ uint32_t sm_u32(const void* p) {
@@ -108,18 +117,16 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
 }
 
 // One INT4 stage: 256 rows x 64 k.  Nibbles [256][32 B] (plain TMA box) and
-// the rows' (scale, zero) pairs of blocks 2 kt, 2 kt + 1 (8 bytes in global
-// memory) -> fp16 in the 128-byte swizzled K-major layout TMA would have
+// the rows' (scale, zero) pairs of blocks 2 kt, 2 kt + 1 ([256][8 B], brought
+// in by the producer warp's cp.async; zero past N) -> fp16 in the 128-byte swizzled K-major layout TMA would have
 // produced: element (r, k) at r * 128 + (((k >> 3) ^ (r & 7)) << 4) + (k & 7) * 2.
 // The dequant threads take (row, 8-k chunk) items.  Exact reference value:
 // OR-ing a nibble into 0x6400 gives the fp16 1024 + q; subtracting the fp16
 // 1024 + z is exact (both integers below 2048), and the one fp16 multiply by s
 // rounds (q - z) · s once, as dequantize_int4_asym does.  Rows past N get
 // zero pairs.
-__device__ __forceinline__ void dequant_stage(const uint8_t* w4, const uint8_t* sz, long ld_sz, int n0, int N,
-                                              int kt, uint8_t* bdst, int t, int nthr) {
-  // all loads of this thread's items first (the pair loads go to L2: issuing
-  // them together keeps one round trip per stage instead of one per item)
+__device__ __forceinline__ void dequant_stage(const uint8_t* w4, const uint8_t* pairs, uint8_t* bdst, int t,
+                                              int nthr) {
   constexpr int kItems = (kBN * 8 + kDequantThreads - 1) / kDequantThreads;
   uint32_t wqs[kItems], prs[kItems];
 #pragma unroll
@@ -130,8 +137,7 @@ __device__ __forceinline__ void dequant_stage(const uint8_t* w4, const uint8_t* 
     prs[i] = 0u;
     if (item < kBN * 8) {
       wqs[i] = *reinterpret_cast<const uint32_t*>(w4 + r * 32 + c * 4);
-      if (n0 + r < N)
-        prs[i] = __ldg(reinterpret_cast<const uint32_t*>(sz + (long)(n0 + r) * ld_sz + kt * 8 + (c >> 2) * 4));
+      prs[i] = *reinterpret_cast<const uint32_t*>(pairs + r * 8 + (c >> 2) * 4);
     }
   }
 #pragma unroll
@@ -163,22 +169,26 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint8_t* sa = smem;                                        // [stage][16 KB]
   uint8_t* sb = sa + kStages * kABytes;                      // [stage][32 KB] fp16 W
   uint8_t* sw4 = sb + kStages * kBBytes;                     // [stage][8 KB]  INT4 nibbles
-  uint64_t* full = reinterpret_cast<uint64_t*>(sw4 + kStages * kW4Bytes);
+  uint8_t* spr = sw4 + kStages * kW4Bytes;                   // [stage][2 KB]  INT4 (scale, zero) pairs
+  uint64_t* full = reinterpret_cast<uint64_t*>(spr + kStages * kPairBytes);
   uint64_t* empty = full + kStages;
   uint64_t* w4full = empty + kStages;                        // INT4 bytes landed
   uint64_t* bready = w4full + kStages;                       // dequantised W ready
   uint64_t* accum = bready + kStages;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
+  int& s_last = *reinterpret_cast<int*>(tmem_slot + 1);      // split-K: this CTA merges
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int n0 = blockIdx.x * kBN, m0 = blockIdx.y * kBM;
-  const int KT = (p.K + kBK - 1) / kBK;
+  const int KTT = (p.K + kBK - 1) / kBK;
+  const int kz = blockIdx.z;
+  const int kt0 = (int)((long)kz * KTT / p.splits), KT = (int)((long)(kz + 1) * KTT / p.splits) - kt0;
 
   if (tid == 0) {
     for (int s = 0; s < kStages; ++s) {
       g_mbar_init(&full[s], 1);
       g_mbar_init(&empty[s], 1);
-      g_mbar_init(&w4full[s], 1);
+      g_mbar_init(&w4full[s], p.w4 ? 33 : 1);    // INT4: TMA arrival + 32 lanes' cp.async
       g_mbar_init(&bready[s], kDequantThreads);
     }
     g_mbar_init(accum, 1);
@@ -194,19 +204,31 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   asm volatile("tcgen05.fence::after_thread_sync;");
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 0 && lane == 0) {
-    // ---- producer
+  if (warp == 0) {
+    // ---- producer: lane 0 issues the TMA loads; for INT4 all 32 lanes copy
+    //      the stage's (scale, zero) pairs (8 bytes per row, below TMA's
+    //      16-byte box minimum) with cp.async, whose completion arrives on
+    //      the same mbarrier as the nibbles
     bool ok = true;
-    for (int kt = 0; kt < KT && ok; ++kt) {
-      const int s = kt % kStages;
-      if (kt >= kStages) ok = g_wait(&empty[s], ((kt / kStages) - 1) & 1, p.status);
+    for (int i = 0; i < KT && ok; ++i) {                // i: stage of this CTA's K range
+      const int s = i % kStages, kt = kt0 + i;
+      if (i >= kStages) ok = g_wait(&empty[s], ((i / kStages) - 1) & 1, p.status);
       if (!ok) break;
       if (p.w4) {
-        g_expect_tx(&full[s], kABytes);
-        g_tma2d(sa + s * kABytes, &tma, kt * kBK, m0, &full[s]);
-        g_expect_tx(&w4full[s], kW4Bytes);
-        g_tma2d(sw4 + s * kW4Bytes, &tmb, kt * (kBK / 2), n0, &w4full[s]);
-      } else {
+        if (lane == 0) {
+          g_expect_tx(&full[s], kABytes);
+          g_tma2d(sa + s * kABytes, &tma, kt * kBK, m0, &full[s]);
+          g_expect_tx(&w4full[s], kW4Bytes);
+          g_tma2d(sw4 + s * kW4Bytes, &tmb, kt * (kBK / 2), n0, &w4full[s]);
+        }
+        for (int r = lane; r < kBN; r += 32) {
+          const bool in = n0 + r < p.N;
+          const uint8_t* src = p.sz + (in ? (long)(n0 + r) * (p.K / 8) + kt * 8 : 0);
+          asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;" ::"r"(sm_u32(spr + s * kPairBytes + r * 8)),
+                       "l"(src), "r"(in ? 8 : 0) : "memory");
+        }
+        asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(sm_u32(&w4full[s])) : "memory");
+      } else if (lane == 0) {
         g_expect_tx(&full[s], kABytes + kBBytes);
         g_tma2d(sa + s * kABytes, &tma, kt * kBK, m0, &full[s]);
         g_tma2d(sb + s * kBBytes, &tmb, kt * kBK, n0, &full[s]);
@@ -215,9 +237,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   } else if (warp == 1 && lane == 0) {
     // ---- MMA issuer
     bool ok = true;
-    for (int kt = 0; kt < KT; ++kt) {
-      const int s = kt % kStages;
-      const unsigned ph = (kt / kStages) & 1;
+    for (int i = 0; i < KT; ++i) {
+      const int s = i % kStages;
+      const unsigned ph = (i / kStages) & 1;
       if (ok) ok = g_wait(&full[s], ph, p.status);
       if (ok && p.w4) ok = g_wait(&bready[s], ph, p.status);
       asm volatile("tcgen05.fence::after_thread_sync;");
@@ -225,7 +247,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const uint32_t a0 = sm_u32(sa + s * kABytes), b0 = sm_u32(sb + s * kBBytes);
 #pragma unroll
         for (int kk = 0; kk < kBK / 16; ++kk)
-          umma_f16(tmem, sw128_desc(a0 + kk * 32), sw128_desc(b0 + kk * 32), (kt | kk) ? 1u : 0u);
+          umma_f16(tmem, sw128_desc(a0 + kk * 32), sw128_desc(b0 + kk * 32), (i | kk) ? 1u : 0u);
       }
       umma_commit(&empty[s]);               // the stage is free once these MMAs have read it
     }
@@ -234,13 +256,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     // ---- INT4 dequantisers (warps 2-7)
     const int t = tid - 64;
     bool ok = true;
-    for (int kt = 0; kt < KT; ++kt) {
-      const int s = kt % kStages;
-      const unsigned ph = (kt / kStages) & 1;
+    for (int i = 0; i < KT; ++i) {
+      const int s = i % kStages;
+      const unsigned ph = (i / kStages) & 1;
       if (ok) ok = g_wait(&w4full[s], ph, p.status);
-      // the fp16 slot was last read by the MMAs of stage kt - kStages
-      if (ok && kt >= kStages) ok = g_wait(&empty[s], ((kt / kStages) - 1) & 1, p.status);
-      if (ok) dequant_stage(sw4 + s * kW4Bytes, p.sz, p.K / 8, n0, p.N, kt, sb + s * kBBytes, t, kDequantThreads);
+      // the fp16 slot was last read by the MMAs of stage i - kStages
+      if (ok && i >= kStages) ok = g_wait(&empty[s], ((i / kStages) - 1) & 1, p.status);
+      if (ok) dequant_stage(sw4 + s * kW4Bytes, spr + s * kPairBytes, sb + s * kBBytes, t, kDequantThreads);
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       g_arrive(&bready[s]);
     }
@@ -267,8 +289,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         : "r"(taddr));
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
     if (!ok || row >= p.M) continue;
-    __half* yr = p.y + (long)row * p.ldy + n0 + c0;
     const int nvalid = min(32, p.N - (n0 + c0));
+    if (p.splits > 1) {                                 // this K split's fp32 partial
+      float* pr = p.part + ((long)kz * p.M + row) * p.N + n0 + c0;
+      if (nvalid == 32 && (p.N % 4) == 0) {
+#pragma unroll
+        for (int q = 0; q < 8; ++q)
+          reinterpret_cast<float4*>(pr)[q] = make_float4(__uint_as_float(v[4 * q]), __uint_as_float(v[4 * q + 1]),
+                                                         __uint_as_float(v[4 * q + 2]), __uint_as_float(v[4 * q + 3]));
+      } else {
+        for (int j = 0; j < nvalid; ++j) pr[j] = __uint_as_float(v[j]);
+      }
+      continue;
+    }
+    __half* yr = p.y + (long)row * p.ldy + n0 + c0;
     if (nvalid == 32 && (p.ldy % 8) == 0 && (reinterpret_cast<uintptr_t>(p.y) & 15) == 0) {
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
@@ -281,6 +315,46 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
     } else {
       for (int j = 0; j < nvalid; ++j) yr[j] = __float2half(__uint_as_float(v[j]));
+    }
+  }
+  if (p.splits > 1) {
+    // the last CTA of the tile to arrive sums the partials in split order
+    // (deterministic) and writes fp16; it leaves the counter zero
+    const int tile = blockIdx.y * gridDim.x + blockIdx.x;
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) s_last = (atomicAdd(&p.cnt[tile], 1u) == (unsigned)p.splits - 1u);
+    __syncthreads();
+    if (s_last) {
+      __threadfence();
+      // coalesced: 256 threads = 4 rows x 64 float4 columns per pass
+      const int rows = min(kBM, p.M - m0), cols = min(kBN, p.N - n0);
+      const bool vec = (p.N % 4) == 0 && (p.ldy % 4) == 0 && (reinterpret_cast<uintptr_t>(p.y) & 7) == 0;
+      if (ok)
+        for (int r = tid >> 6; r < rows; r += kGemmThreads / 64) {
+          const int c = (tid & 63) * 4;
+          if (c >= cols) continue;
+          const long prow = (long)(m0 + r) * p.N + n0 + c;
+          __half* yr = p.y + (long)(m0 + r) * p.ldy + n0 + c;
+          if (vec && c + 4 <= cols) {
+            float4 a4 = __ldcg(reinterpret_cast<const float4*>(p.part + prow));
+            for (int q = 1; q < p.splits; ++q) {
+              const float4 b4 = __ldcg(reinterpret_cast<const float4*>(p.part + (long)q * p.M * p.N + prow));
+              a4.x += b4.x; a4.y += b4.y; a4.z += b4.z; a4.w += b4.w;
+            }
+            uint2 o;
+            o.x = h2_as_u32(__floats2half2_rn(a4.x, a4.y));
+            o.y = h2_as_u32(__floats2half2_rn(a4.z, a4.w));
+            *reinterpret_cast<uint2*>(yr) = o;
+          } else {
+            for (int j = 0; j < 4 && c + j < cols; ++j) {
+              float v = 0.0f;
+              for (int q = 0; q < p.splits; ++q) v += __ldcg(p.part + (long)q * p.M * p.N + prow + j);
+              yr[j] = __float2half(v);
+            }
+          }
+        }
+      if (tid == 0) p.cnt[tile] = 0u;
     }
   }
   asm volatile("tcgen05.fence::before_thread_sync;");
@@ -321,11 +395,39 @@ int map2d(CUtensorMap* m, const void* base, CUtensorMapDataType dt, int esize, l
 }
 
 size_t gemm_smem() {
-  return 1024 + (size_t)kStages * (kABytes + kBBytes + kW4Bytes) + (4 * kStages + 1) * 8 + 16;
+  return 1024 + (size_t)kStages * (kABytes + kBBytes + kW4Bytes + kPairBytes) + (4 * kStages + 1) * 8 + 16;
+}
+
+// Workspace: status word at 0, tile counters from byte 256 (split grids have
+// at most kMaxSplitTiles tiles), fp32 partials from byte kPartOffset.
+constexpr int kMaxSplitTiles = 1024;
+constexpr size_t kPartOffset = 256 + kMaxSplitTiles * 4;
+
+// K splits: enough CTAs to cover the SMs once when the output has few tiles
+// (decode-sized M), at least 4 k-tiles per split, within the workspace.
+// R4Q_GEMM_SPLIT forces the split count (measurement only).
+int gemm_splits(int M, int N, int K, size_t ws_bytes) {
+  const int tiles = ((N + kBN - 1) / kBN) * ((M + kBM - 1) / kBM);
+  const int KT = (K + kBK - 1) / kBK;
+  static const int forced = [] {
+    const char* e = getenv("R4Q_GEMM_SPLIT");
+    return e ? atoi(e) : 0;
+  }();
+  int S = forced > 0 ? (forced < KT ? forced : KT) : num_sms() / tiles;
+  if (forced > 0) {
+    if (tiles > kMaxSplitTiles) S = 1;
+    while (S > 1 && kPartOffset + (size_t)S * M * N * 4 > ws_bytes) --S;
+    return S;
+  }
+  if (S > KT / 4) S = KT / 4;
+  if (S > 16) S = 16;
+  if (tiles > kMaxSplitTiles) S = 1;
+  while (S > 1 && kPartOffset + (size_t)S * M * N * 4 > ws_bytes) --S;
+  return S < 1 ? 1 : S;
 }
 
 int launch_gemm(const void* x, long ldx, const void* w, const void* s, void* y, long ldy, int M, int N, int K,
-                int w4, int* status, cudaStream_t st) {
+                int w4, void* ws, size_t ws_bytes, cudaStream_t st) {
   CUtensorMap ta, tb;
   int rc = map2d(&ta, x, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, M, K, ldx, kBK, kBM, CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
@@ -344,7 +446,10 @@ int launch_gemm(const void* x, long ldx, const void* w, const void* s, void* y, 
   p.N = N;
   p.K = K;
   p.w4 = w4;
-  p.status = status;
+  p.status = (int*)ws;
+  p.splits = gemm_splits(M, N, K, ws_bytes);
+  p.cnt = reinterpret_cast<unsigned*>(reinterpret_cast<uint8_t*>(ws) + 256);
+  p.part = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(ws) + kPartOffset);
   const size_t smem = gemm_smem();
   static std::mutex mu;
   static bool done[64] = {};
@@ -358,7 +463,7 @@ int launch_gemm(const void* x, long ldx, const void* w, const void* s, void* y, 
       done[dev] = true;
     }
   }
-  dim3 grid((N + kBN - 1) / kBN, (M + kBM - 1) / kBM);
+  dim3 grid((N + kBN - 1) / kBN, (M + kBM - 1) / kBM, p.splits);
   gemm_tc_kernel<<<grid, kGemmThreads, smem, st>>>(ta, tb, p);
   return check_launch("gemm_tc_kernel");
 }
@@ -373,8 +478,9 @@ extern "C" int r4q_gemm_fp16(const void* x, long ldx, const void* w, void* y, lo
   if (!x || !w || !y || M < 1 || N < 1 || K < 1) return set_error(R4Q_ERR_ARG, "gemm_fp16: bad arguments");
   if (K % 8 || ldx % 8 || ldx < K || ldy < N || !aligned(x, 16) || !aligned(w, 16) || !aligned(y, 2))
     return set_error(R4Q_ERR_ALIGN, "gemm_fp16: K, ldx multiples of 8 and 16-byte aligned x, w required");
-  if (!ws || ws_bytes < 4) return set_error(R4Q_ERR_CAPACITY, "gemm_fp16: workspace (status word) required");
-  return launch_gemm(x, ldx, w, nullptr, y, ldy, M, N, K, 0, (int*)ws, (cudaStream_t)stream);
+  if (!ws || ws_bytes < 4 || !aligned(ws, 16))
+    return set_error(R4Q_ERR_CAPACITY, "gemm_fp16: 16-byte aligned workspace (status word) required");
+  return launch_gemm(x, ldx, w, nullptr, y, ldy, M, N, K, 0, ws, ws_bytes, (cudaStream_t)stream);
 }
 
 extern "C" int r4q_gemm_int4(const void* x, long ldx, const void* w, const void* sz, void* y, long ldy, int M,
@@ -383,6 +489,13 @@ extern "C" int r4q_gemm_int4(const void* x, long ldx, const void* w, const void*
   if (K % 64 || ldx % 8 || ldx < K || ldy < N || !aligned(x, 16) || !aligned(w, 16) || !aligned(sz, 16) ||
       !aligned(y, 2))
     return set_error(R4Q_ERR_ALIGN, "gemm_int4: K % 64 == 0, ldx % 8 == 0 and 16-byte aligned x, w, sz required");
-  if (!ws || ws_bytes < 4) return set_error(R4Q_ERR_CAPACITY, "gemm_int4: workspace (status word) required");
-  return launch_gemm(x, ldx, w, sz, y, ldy, M, N, K, 1, (int*)ws, (cudaStream_t)stream);
+  if (!ws || ws_bytes < 4 || !aligned(ws, 16))
+    return set_error(R4Q_ERR_CAPACITY, "gemm_int4: 16-byte aligned workspace (status word) required");
+  return launch_gemm(x, ldx, w, sz, y, ldy, M, N, K, 1, ws, ws_bytes, (cudaStream_t)stream);
+}
+
+extern "C" size_t r4q_gemm_workspace_bytes(int M, int N, int K) {
+  if (M < 1 || N < 1 || K < 1) return 256;
+  const int S = gemm_splits(M, N, K, (size_t)-1);
+  return S > 1 ? kPartOffset + (size_t)S * M * N * 4 : 256;
 }

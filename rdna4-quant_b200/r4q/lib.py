@@ -82,6 +82,7 @@ _SIGS = {
                                     i32, i32, i32, i32, vp, i32, vp, sz_t, vp]),
     "r4q_gemm_fp16": (i32, [vp, i64, vp, vp, i64, i32, i32, i32, vp, sz_t, vp]),
     "r4q_gemm_int4": (i32, [vp, i64, vp, vp, vp, i64, i32, i32, i32, vp, sz_t, vp]),
+    "r4q_gemm_workspace_bytes": (sz_t, [i32, i32, i32]),
     "r4q_fwht_rows": (i32, [vp, i64, vp, i64, i32, i32, vp]),
     "r4q_silu_mul": (i32, [vp, i64, vp, i64, i32, i32, vp]),
     "r4q_dequant_int8": (i32, [vp, vp, vp, i32, i32, vp]),

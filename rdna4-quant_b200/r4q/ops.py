@@ -93,9 +93,10 @@ def gemv(fmt: str, x: torch.Tensor, w: torch.Tensor, s: torch.Tensor | None, N: 
     return out if out32 is None else out32
 
 
-def dequant_int4(packed: torch.Tensor, sz: torch.Tensor, N: int, K: int) -> torch.Tensor:
+def dequant_int4(packed: torch.Tensor, sz: torch.Tensor, N: int, K: int,
+                 out: torch.Tensor | None = None) -> torch.Tensor:
     dev = _require_cuda(packed, sz)
-    out = torch.empty(N, K, dtype=torch.float16, device=dev)
+    out = out if out is not None else torch.empty(N, K, dtype=torch.float16, device=dev)
     L.call("r4q_dequant_int4", packed.data_ptr(), sz.data_ptr(), out.data_ptr(), N, K,
            stream_handle(dev))
     return out
@@ -199,12 +200,15 @@ def attn_decode_fused(qkv, k_cache, v_cache, q_w, k_w, cos, sin, H, Hk, seq_len,
 _gws: dict = {}
 
 
-def _status_ws(dev):
+def _status_ws(dev, nbytes: int = 256):
+    """Per (device, stream) GEMM workspace (status word, split counters, fp32
+    partials), zeroed once and grown on demand; the kernels leave it zero.
+    Grow it outside graph capture (a warm-up call at the same shape)."""
     key = (dev.index, stream_handle(dev))
     with _ws_lock:
         cur = _gws.get(key)
-        if cur is None:
-            cur = torch.zeros(256, dtype=torch.uint8, device=dev)
+        if cur is None or cur.numel() < nbytes:
+            cur = torch.zeros(max(256, nbytes), dtype=torch.uint8, device=dev)
             _gws[key] = cur
     return cur
 
@@ -221,7 +225,7 @@ def gemm(x: torch.Tensor, w: torch.Tensor, s: torch.Tensor | None = None, N: int
     M, K = x2.shape
     N = int(w.shape[0]) if N is None else N
     y = out if out is not None else torch.empty(M, N, dtype=torch.float16, device=dev)
-    ws = _status_ws(dev)
+    ws = _status_ws(dev, int(L.LIB.r4q_gemm_workspace_bytes(M, N, K)))
     st = stream_handle(dev)
     if s is None:
         L.call("r4q_gemm_fp16", x2.data_ptr(), x2.stride(0), w.data_ptr(), y.data_ptr(), y.stride(0), M, N, K,

@@ -50,3 +50,31 @@ def test_gemm_repeat_and_status_clean():
     torch.cuda.synchronize()
     assert torch.equal(a, b)
     assert int(ops._status_ws(x.device)[:4].view(torch.int32)[0]) == 0
+
+
+@pytest.mark.parametrize("M,N,K,int4", [(64, 5120, 2048, True), (16, 2048, 4096, True), (1, 2048, 4096, False)])
+def test_gemm_split_k_decode_sizes(M, N, K, int4):
+    """Decode-sized M: K split over gridDim.z, fp32 partials merged by the
+    tile's last CTA in split order — within tolerance of the reference,
+    identical on repeat, counters left zero."""
+    from r4q import ops
+    from r4q import lib as Lb
+    assert Lb.LIB.r4q_gemm_workspace_bytes(M, N, K) > 256          # the split path is taken
+    rng = np.random.default_rng(M + K)
+    x = rng.standard_normal((M, K)).astype(np.float16)
+    if int4:
+        packed, sz = make_int4(rng, N, K)
+        W = O.dequant_int4_runtime(packed, sz).astype(np.float64)
+        args = (cuda(packed), cuda(sz), N)
+    else:
+        w = (rng.standard_normal((N, K)) * 0.05).astype(np.float16)
+        W = w.astype(np.float64)
+        args = (cuda(w),)
+    a = ops.gemm(cuda(x), *args)
+    b = ops.gemm(cuda(x), *args)
+    torch.cuda.synchronize()
+    close(a.cpu().numpy(), x.astype(np.float64) @ W.T)
+    assert torch.equal(a, b)
+    ws = ops._status_ws(a.device)
+    assert int(ws[:4].view(torch.int32)[0]) == 0
+    assert int(ws[256:256 + 4096].count_nonzero()) == 0
