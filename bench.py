@@ -61,6 +61,8 @@ def parse():
     ap.add_argument("--moe-batches", default="1,16,64",
                     help="batches of the config-4 MoE decode measurement ('' skips it)")
     ap.add_argument("--moe-tokens", type=int, default=32)
+    ap.add_argument("--moe-probe", type=int, default=0,
+                    help="ncu target: 3 eager MoE decode steps of a 2-layer config-4 model at this batch")
     ap.add_argument("--gemm-probe", action="store_true",
                     help="run the INT4 tcgen05 prefill GEMM (M=512, qkv shape) 4 times and exit (for ncu)")
     ap.add_argument("--kernel-probe", default=None, choices=[n for n, *_ in LAYER_SHAPES],
@@ -336,9 +338,9 @@ def main_ours(a):
         del layers
         torch.cuda.empty_cache()
         line["decode"] = decode_tok_s(a, dev, peak, ws, rank)
-    if a.moe_batches and ws == 1:
+    if a.moe_batches:
         torch.cuda.empty_cache()
-        line["moe"] = moe_tok_s(a, dev, peak)
+        line["moe"] = moe_tok_s(a, dev, peak, ws, rank)
     if rank == 0 and ws == 1 and not a.no_cpu_baseline:
         threads = os.cpu_count() or 1
         setup = cpu_port_setup(B)
@@ -518,29 +520,35 @@ def prefill_tok_s(a, dev, m, cfg):
             "api": "int4_hip.prefill_logits (r4q.prefill): tcgen05 GEMM per projection, torch SDPA attention"}
 
 
-def moe_tok_s(a, dev, peak):
-    """BASELINE config 4 on one GPU: 48-layer Qwen3-30B-A3B-shaped MoE decode
-    (random init, INT4 experts, top-8 of 128), KV cache of ctx 2048 filled
-    with seeded FP8 values, batches from --moe-batches; each token one
-    CUDA-graph replay of the whole step (routing on the device).  Bytes per
-    step count the dense weights, the router, the lm_head, the KV read and
-    the distinct experts the step's routing selects (expected count for
-    uniform routing: E (1 - (1 - k/E)^B) per layer)."""
+def moe_tok_s(a, dev, peak, ws=1, rank=0):
+    """48-layer Qwen3-30B-A3B-shaped MoE decode (random
+    init, INT4 experts, top-8 of 128), KV cache of ctx 2048 filled with seeded
+    FP8 values, batches from --moe-batches; each token one CUDA-graph replay
+    of the whole step (routing on the device).  ws > 1: expert parallelism,
+    E / ws experts per rank, attention and router replicated, fp32 expert
+    partials all-reduced over NVLink; time = max over ranks.  Bytes per step
+    and GPU count the dense weights, the router, the lm_head, the KV read and
+    this GPU's share of the distinct experts the step's routing selects
+    (expected count for uniform routing: E (1 - (1 - k/E)^B) per layer)."""
     import torch
-    from r4q import moe, synth
+    import torch.distributed as dist
+    from r4q import moe, synth, tp
     cfg = moe.qwen3_30b_a3b_config()
     bs = [int(b) for b in a.moe_batches.split(",") if b]
     ctx, steps = 2048, a.moe_tokens
     m = moe.build_moe_model(cfg, dev, seed=11, max_seq=ctx + steps + 16, batch=max(bs))
     synth.fill_kv_synthetic(m, ctx, seed=5)
     E, k, D = cfg['experts'], cfg['topk'], cfg['hidden']
+    comm = tp.Comm(rank, ws, max_batch=max(bs), hidden=D, sa_cap=max(bs) * D) if ws > 1 else None
     res = []
     for B in bs:
-        dec = moe.MoEDecoder(m, cfg, batch=B)
+        dec = moe.MoEDecoder(m, cfg, batch=B, comm=comm)
         h = m['embed'][torch.arange(B, device=dev) * 31 + 1]
         for w in range(3):
             dec.step(h, ctx + w)
         torch.cuda.synchronize()
+        if ws > 1:
+            dist.barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
         for t in range(steps):
@@ -548,15 +556,44 @@ def moe_tok_s(a, dev, peak):
         e1.record()
         torch.cuda.synchronize()
         ms = e0.elapsed_time(e1) / steps
+        if ws > 1:
+            comm.status()
+            tm = torch.tensor([ms], device=dev)
+            dist.all_reduce(tm, op=dist.ReduceOp.MAX)
+            ms = float(tm.item())
         distinct = E * (1 - (1 - k / E) ** B)
-        byt = int(m['dense_weight_bytes'] + cfg['num_layers'] * (E * D * 2 + moe.expert_bytes(cfg, 1) * distinct)
+        byt = int(m['dense_weight_bytes'] + cfg['num_layers'] * (E * D * 2 + moe.expert_bytes(cfg, 1) * distinct / ws)
                   + 2 * cfg['vocab'] * D + cfg['num_layers'] * 2 * B * cfg['num_kv_heads'] * 128 * (ctx + steps // 2))
         res.append({"batch": B, "tok_s": round(B * 1e3 / ms, 1), "ms_per_step": round(ms, 4),
-                    "bytes_per_step": byt, "GBps": round(byt / ms / 1e6, 1), "frac": round(byt / ms / 1e6 / peak, 4)})
+                    "bytes_per_step_per_gpu": byt, "GBps_per_gpu": round(byt / ms / 1e6, 1),
+                    "frac": round(byt / ms / 1e6 / peak, 4)})
         del dec
+    if comm is not None:
+        comm.close()
     return {"model": "Qwen3-30B-A3B shape (48 layers, 128 experts, top-8), random init, INT4 experts",
-            "ctx": ctx, "tokens": steps, "gpus": 1, "results": res,
+            "ctx": ctx, "tokens": steps, "gpus": ws,
+            "parallelism": f"expert parallel x{ws} (all-reduce of fp32 expert partials)" if ws > 1 else "1 GPU",
+            "results": res,
             "api": "r4q.moe.MoEDecoder.step (one CUDA graph per step: router, top-k, grouped expert GEMVs)"}
+
+
+def moe_probe(a):
+    """Config-4 layer shapes (hidden 2048, 128 experts, top-8) with 2 layers,
+    KV at ctx 2048, batch --moe-probe: 3 eager steps (each layer's kernels
+    launch separately), for an ncu launch list / capture on a small case."""
+    import torch
+    from r4q import moe, synth
+    dev = torch.device("cuda", 0)
+    cfg = moe.qwen3_30b_a3b_config(layers=2)
+    B = a.moe_probe
+    m = moe.build_moe_model(cfg, dev, seed=11, max_seq=2048 + 16, batch=B)
+    synth.fill_kv_synthetic(m, 2048, seed=5)
+    dec = moe.MoEDecoder(m, cfg, batch=B)
+    h = m['embed'][torch.arange(B, device=dev) * 31 + 1]
+    for t in range(3):
+        dec.step(h, 2048 + t, use_graph=False)
+    torch.cuda.synchronize()
+    print(f"moe probe B={B} ok")
 
 
 def kernel_probe(a):
@@ -621,6 +658,8 @@ if __name__ == "__main__":
         decode_probe(args)
     elif args.kernel_probe:
         kernel_probe(args)
+    elif args.moe_probe:
+        moe_probe(args)
     elif args.impl == "reference":
         main_reference(args)
     else:

@@ -242,10 +242,11 @@ int r4q_norm_fwht_rows(const void* x, const float* ss_in, int ss_parts, const vo
  * K % 128 == 0.  mode 0: y[j] = W_e · x[j / topk]; mode 1: y[j] = W_e · x[j];
  * mode 2 (gate_up, N = 2 Ie, rows [gate; up]): y[j] = fp16(H32(silu(g) u)),
  * g, u = fp16(W_e · x[j / topk]) halves — down_proj's input, Ie per row.
- * y rows fp16 (ldy), one per entry j. */
+ * y rows fp16 (ldy), one per entry j.  status (nullable): set to 1 when a
+ * bounded wait for the weight tile gives up. */
 int r4q_moe_gemv(int mode, const void* w, const void* sz, const void* x, long ldx, void* y, long ldy, int N,
                  int K, int E, int e_lo, int e_hi, int B, int topk, const int* counts, const int* offsets,
-                 const int* list, const int* active, const int* n_active, void* stream);
+                 const int* list, const int* active, const int* n_active, int* status, void* stream);
 /* Over the entries of experts [e_lo, e_hi): h[b] = fp16(fp16(sum_k wts[b,k]
  * y[b*topk+k]) + res[b]) in slot order with ss_out [D/16][B] the sums of
  * squares of the unrounded h (res may alias h); or, with out32, the fp32

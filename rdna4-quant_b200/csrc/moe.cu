@@ -24,8 +24,11 @@
 //    gate rows and the matching 32 up rows), writing down_proj's input;
 //  * moe_combine_kernel: h = fp16(fp16(Σ_k w_k fp16(y_k)) + residual) in slot
 //    order, with the per-16-row sums of squares the next RMSNorm prologue takes.
+#include <cuda.h>
+
 #include <atomic>
 #include <cstdlib>
+#include <mutex>
 
 #include "r4q_common.cuh"
 
@@ -427,7 +430,7 @@ __global__ void __launch_bounds__(kMoeThreads, 2)
       for (int q = q0; q < q1; q += kMoeUnroll) {
         uint4 qa[kMoeUnroll], qb[kMoeUnroll];
         uint32_t pa[kMoeUnroll], pb[kMoeUnroll];
-  #pragma unroll
+#pragma unroll
         for (int u = 0; u < kMoeUnroll; ++u) {          // every weight load of the batches first
           if (q + u < q1) {
             qa[u] = __ldg(reinterpret_cast<const uint4*>(wa + (long)(q + u) * 64));
@@ -436,35 +439,39 @@ __global__ void __launch_bounds__(kMoeThreads, 2)
             pb[u] = __ldg(reinterpret_cast<const unsigned*>(sb + (q + u) * 8));
           }
         }
-  #pragma unroll
+#pragma unroll
         for (int u = 0; u < kMoeUnroll; ++u) {
           if (q + u >= q1) break;
           uint4 xv[4];
-  #pragma unroll
+#pragma unroll
           for (int i = 0; i < 4; ++i)
             xv[i] = tok_ok ? __ldg(reinterpret_cast<const uint4*>(xr + (long)(q + u) * 128 + 8 * i))
                            : make_uint4(0, 0, 0, 0);
           const __half2 pha = u32_as_h2(pa[u]), phb = u32_as_h2(pb[u]);
-          const __half2 s2a = __half2half2(__low2half(pha)),
-                        z2a = __hadd2(__half2half2(__high2half(pha)), __float2half2_rn(1024.0f));
-          const __half2 s2b = __half2half2(__low2half(phb)),
-                        z2b = __hadd2(__half2half2(__high2half(phb)), __float2half2_rn(1024.0f));
+          // biased nibbles: low half 1024 + q (nibble in mantissa bits 0-3),
+          // high half 64 + q (bits 4-7 of a 64-based fp16), both exact, so
+          // subtracting (1024 + z, 64 + z) and one multiply by s give the
+          // reference's fp16((q - z) s)
+          const __half2 bias = __halves2half2(__float2half(1024.0f), __float2half(64.0f));
+          const __half2 s2a = __half2half2(__low2half(pha)), z2a = __hadd2(__half2half2(__high2half(pha)), bias);
+          const __half2 s2b = __half2half2(__low2half(phb)), z2b = __hadd2(__half2half2(__high2half(phb)), bias);
           const uint32_t wa4[4] = {qa[u].x, qa[u].y, qa[u].z, qa[u].w};
           const uint32_t wb4[4] = {qb[u].x, qb[u].y, qb[u].z, qb[u].w};
-  #pragma unroll
+#pragma unroll
           for (int jj = 0; jj < 8; ++jj) {
             // k-step jj: this lane's block bytes 2jj (k 4jj, 4jj+1) and 2jj+1
-            // (k 4jj+2, 4jj+3) stand for fragment k (2t, 2t+1) and (2t+8, 2t+9)
-            const int sh = 16 * (jj & 1);
-            const uint32_t wA = wa4[jj >> 1] >> sh, wB = wb4[jj >> 1] >> sh;
-            const uint32_t lA = (wA & 0xFu) | (((wA >> 4) & 0xFu) << 16);
-            const uint32_t hA = ((wA >> 8) & 0xFu) | (((wA >> 12) & 0xFu) << 16);
-            const uint32_t lB = (wB & 0xFu) | (((wB >> 4) & 0xFu) << 16);
-            const uint32_t hB = ((wB >> 8) & 0xFu) | (((wB >> 12) & 0xFu) << 16);
-            const uint32_t a0 = h2_as_u32(__hmul2(__hsub2(u32_as_h2(lA | 0x64006400u), z2a), s2a));
-            const uint32_t a2 = h2_as_u32(__hmul2(__hsub2(u32_as_h2(hA | 0x64006400u), z2a), s2a));
-            const uint32_t a1 = h2_as_u32(__hmul2(__hsub2(u32_as_h2(lB | 0x64006400u), z2b), s2b));
-            const uint32_t a3 = h2_as_u32(__hmul2(__hsub2(u32_as_h2(hB | 0x64006400u), z2b), s2b));
+            // (k 4jj+2, 4jj+3) stand for fragment k (2t, 2t+1) and (2t+8, 2t+9);
+            // the byte is copied to both halves and one LOP3 keeps lo / hi nibble
+            const uint32_t sl = (uint32_t)(2 * (jj & 1)) * 0x1111u, sh = sl + 0x1111u;
+            const uint32_t wA = wa4[jj >> 1], wB = wb4[jj >> 1];
+            const uint32_t lA = lop3_and_or(__byte_perm(wA, 0, sl), 0x00F0000Fu, 0x54006400u);
+            const uint32_t hA = lop3_and_or(__byte_perm(wA, 0, sh), 0x00F0000Fu, 0x54006400u);
+            const uint32_t lB = lop3_and_or(__byte_perm(wB, 0, sl), 0x00F0000Fu, 0x54006400u);
+            const uint32_t hB = lop3_and_or(__byte_perm(wB, 0, sh), 0x00F0000Fu, 0x54006400u);
+            const uint32_t a0 = h2_as_u32(__hmul2(__hsub2(u32_as_h2(lA), z2a), s2a));
+            const uint32_t a2 = h2_as_u32(__hmul2(__hsub2(u32_as_h2(hA), z2a), s2a));
+            const uint32_t a1 = h2_as_u32(__hmul2(__hsub2(u32_as_h2(lB), z2b), s2b));
+            const uint32_t a3 = h2_as_u32(__hmul2(__hsub2(u32_as_h2(hB), z2b), s2b));
             const uint4 xq = xv[jj >> 1];
             const uint32_t b0 = (jj & 1) ? xq.z : xq.x, b1 = (jj & 1) ? xq.w : xq.y;
             mma16816(acc, a0, a1, a2, a3, b0, b1);
@@ -473,20 +480,20 @@ __global__ void __launch_bounds__(kMoeThreads, 2)
       }
       // ---- K half 1 hands its partial to K half 0 (fixed order)
       if (kp == 1) {
-  #pragma unroll
+#pragma unroll
         for (int i = 0; i < 4; ++i) red[mt][i][lane] = acc[i];
       }
       __syncthreads();
       if (kp == 0) {
-  #pragma unroll
+#pragma unroll
         for (int i = 0; i < 4; ++i) acc[i] += red[mt][i][lane];
         // C: (row g, tokens 2t, 2t+1), (row g + 8, tokens 2t, 2t+1)
         if (MODE == 2) {
-  #pragma unroll
+#pragma unroll
           for (int i = 0; i < 4; ++i)
             cs[2 * t + (i & 1)][mt * 16 + g + 8 * (i >> 1)] = __half2float(__float2half(acc[i]));
         } else {
-  #pragma unroll
+#pragma unroll
           for (int h = 0; h < 2; ++h) {
             const int tok = 2 * t + h;
             if (tok < nc) {
@@ -507,6 +514,197 @@ __global__ void __launch_bounds__(kMoeThreads, 2)
       }
       __syncthreads();        // red / cs are rewritten by the next pass
     }
+  }
+}
+
+// ------------------------------------------- grouped expert GEMV, TMA tiles
+// Same work and modes as moe_gemv_kernel, for K % 256 == 0 and a 64-row tile
+// that fits shared memory (64 x K/2 bytes): one TMA burst brings the tile's
+// nibbles (128-byte columns x 32-row boxes, 128-byte swizzle) while the
+// (scale, zero) pairs and the routing metadata load; up to three CTAs per SM
+// keep ~200 KB per SM in flight, where the register-staged kernel holds
+// 64 KB.  Lane (g, t) then reads its 16-byte block chunks from shared memory
+// (conflict-free under the swizzle) and computes exactly as the LDG kernel.
+__device__ __forceinline__ uint32_t moe_su32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ bool moe_mbar_wait(uint64_t* b, unsigned parity) {
+  const uint32_t a = moe_su32(b);
+  for (long i = 0; i < (1L << 26); ++i) {
+    uint32_t ok;
+    asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+                 " selp.u32 %0, 1, 0, p;\n}\n" : "=r"(ok) : "r"(a), "r"(parity) : "memory");
+    if (ok) return true;
+  }
+  return false;
+}
+
+constexpr int kMoeTmaMaxPairs = 8;      // 128-k batches per K half held in registers (K <= 8192)
+
+template <int MODE>
+__global__ void __launch_bounds__(kMoeThreads, 3)
+    moe_gemv_tma_kernel(const __grid_constant__ CUtensorMap tmw, const __half* __restrict__ sz,
+                        const __half* __restrict__ xin, long ldx, __half* __restrict__ y, long ldy, int N, int K,
+                        int topk, int e_lo, const MoeRoute rt, int* status) {
+  extern __shared__ __align__(1024) uint8_t moe_smem[];
+  uint8_t* wsm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(moe_smem) + 1023) & ~uintptr_t(1023));
+  __shared__ __align__(8) uint64_t bars[kMoeKp];             // one per K half: its warps start when it lands
+  __shared__ float red[4][4][32];
+  __shared__ float cs[kMoeTok][64];
+  pdl_wait_trigger();
+  const int a = blockIdx.y;
+  if (a >= *rt.n_active) return;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int mt = warp & 3, kp = warp >> 2;
+  const int e = rt.active[a];
+  const int tile = blockIdx.x;
+  const long el = e - e_lo;
+  // tile rows: smem rows 0-31 from global row r0, 32-63 from r1
+  const int r0 = MODE == 2 ? tile * 32 : tile * 64;
+  const int r1 = MODE == 2 ? N / 2 + tile * 32 : tile * 64 + 32;
+  const int ncol = K / 256;                                   // 128-byte columns of nibbles
+  // K half p covers 128-k batches [nbat p / 2, nbat (p + 1) / 2); its 128-byte
+  // columns (two batches each, a batch is 64 bytes of a row) load on bars[p]
+  const int nbat = K / 128;
+  const int q0 = (nbat * kp) / kMoeKp, q1 = (nbat * (kp + 1)) / kMoeKp;
+  if (tid == 0) {
+#pragma unroll
+    for (int p = 0; p < kMoeKp; ++p) asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(moe_su32(&bars[p])));
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  if (tid == 0) {
+    // column b (batches 2b, 2b + 1) belongs to the half of batch 2b; a
+    // column split between halves (odd batch count per half) goes to the
+    // first half, whose warps then also hold the second half's first batch
+    int cb[kMoeKp + 1];
+    cb[0] = 0;
+    for (int p = 1; p <= kMoeKp; ++p) cb[p] = ((nbat * p) / kMoeKp + 1) / 2;
+    for (int p = 0; p < kMoeKp; ++p) {
+      asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(moe_su32(&bars[p])),
+                   "r"((cb[p + 1] - cb[p]) * 8192) : "memory");
+      for (int b = cb[p]; b < cb[p + 1]; ++b)
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+          asm volatile(
+              "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+              " [%0], [%1, {%2, %3}], [%4];" ::"r"(moe_su32(wsm + (2 * b + h) * 4096)),
+              "l"(reinterpret_cast<uint64_t>(&tmw)), "r"(b * 128), "r"((int)(el * N) + (h ? r1 : r0)),
+              "r"(moe_su32(&bars[p]))
+              : "memory");
+    }
+  }
+  // while the tile lands: this lane's (scale, zero) pairs and the routing
+  const int lr = mt * 16 + g;                                  // tile row of fragment rows g (and g + 8)
+  const int gra = (lr < 32 ? r0 + lr : r1 + lr - 32), grb = gra + 8;
+  const long srow = (long)K / 16;
+  const __half* sa = sz + (el * N + gra) * srow + t * 2;
+  const __half* sb = sz + (el * N + grb) * srow + t * 2;
+  uint32_t pa[kMoeTmaMaxPairs], pb[kMoeTmaMaxPairs];
+#pragma unroll
+  for (int i = 0; i < kMoeTmaMaxPairs; ++i) {
+    if (q0 + i < q1) {
+      pa[i] = __ldg(reinterpret_cast<const unsigned*>(sa + (q0 + i) * 8));
+      pb[i] = __ldg(reinterpret_cast<const unsigned*>(sb + (q0 + i) * 8));
+    }
+  }
+  const int cnt = rt.counts[e];
+  const int* ent = rt.list + rt.offsets[e];
+  // the columns this warp reads: batches [q0, q1) lie in columns
+  // [q0 / 2, (q1 + 1) / 2), which bars[kp] covers — and, when q0 is odd,
+  // column q0 / 2 sits with the previous half
+  bool landed = moe_mbar_wait(&bars[kp], 0);
+  if (landed && kp > 0 && (q0 & 1)) landed = moe_mbar_wait(&bars[kp - 1], 0);
+  if (__syncthreads_or(!landed)) {                            // a wait gave up: the whole CTA leaves
+    if (tid == 0 && status) atomicExch(status, 1);
+    return;
+  }
+  const int ra_out = MODE == 2 ? 0 : tile * 64 + lr;           // plain modes: output rows ra_out, ra_out + 8
+  const uint32_t rowa = moe_su32(wsm) + (lr >> 5) * 4096 + (lr & 31) * 128;
+  const uint32_t rowb = moe_su32(wsm) + ((lr + 8) >> 5) * 4096 + ((lr + 8) & 31) * 128;
+  const int swa = (lr & 31) & 7, swb = ((lr + 8) & 31) & 7;
+  const __half2 bias = __halves2half2(__float2half(1024.0f), __float2half(64.0f));
+
+  for (int c0 = 0; c0 < cnt; c0 += kMoeTok) {
+    const int nc = min(kMoeTok, cnt - c0);
+    const bool tok_ok = g < nc;
+    const __half* xr = xin + t * 32;
+    if (tok_ok) {
+      const int j = ent[c0 + g];
+      xr += (long)(MODE == 1 ? j : j / topk) * ldx;
+    }
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int i = 0; i < kMoeTmaMaxPairs; ++i) {
+      const int q = q0 + i;
+      if (q >= q1) break;
+      const int blk = 4 * q + t, col = blk >> 3, cc = blk & 7;
+      uint4 qa, qb;
+      asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+                   : "=r"(qa.x), "=r"(qa.y), "=r"(qa.z), "=r"(qa.w)
+                   : "r"(rowa + col * 8192 + ((cc ^ swa) << 4)));
+      asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+                   : "=r"(qb.x), "=r"(qb.y), "=r"(qb.z), "=r"(qb.w)
+                   : "r"(rowb + col * 8192 + ((cc ^ swb) << 4)));
+      uint4 xv[4];
+#pragma unroll
+      for (int k4 = 0; k4 < 4; ++k4)
+        xv[k4] = tok_ok ? __ldg(reinterpret_cast<const uint4*>(xr + (long)q * 128 + 8 * k4)) : make_uint4(0, 0, 0, 0);
+      const __half2 pha = u32_as_h2(pa[i]), phb = u32_as_h2(pb[i]);
+      const __half2 s2a = __half2half2(__low2half(pha)), z2a = __hadd2(__half2half2(__high2half(pha)), bias);
+      const __half2 s2b = __half2half2(__low2half(phb)), z2b = __hadd2(__half2half2(__high2half(phb)), bias);
+      const uint32_t wa4[4] = {qa.x, qa.y, qa.z, qa.w}, wb4[4] = {qb.x, qb.y, qb.z, qb.w};
+#pragma unroll
+      for (int jj = 0; jj < 8; ++jj) {
+        const uint32_t sl = (uint32_t)(2 * (jj & 1)) * 0x1111u, sh = sl + 0x1111u;
+        const uint32_t wA = wa4[jj >> 1], wB = wb4[jj >> 1];
+        const uint32_t lA = lop3_and_or(__byte_perm(wA, 0, sl), 0x00F0000Fu, 0x54006400u);
+        const uint32_t hA = lop3_and_or(__byte_perm(wA, 0, sh), 0x00F0000Fu, 0x54006400u);
+        const uint32_t lB = lop3_and_or(__byte_perm(wB, 0, sl), 0x00F0000Fu, 0x54006400u);
+        const uint32_t hB = lop3_and_or(__byte_perm(wB, 0, sh), 0x00F0000Fu, 0x54006400u);
+        const uint32_t a0 = h2_as_u32(__hmul2(__hsub2(u32_as_h2(lA), z2a), s2a));
+        const uint32_t a2 = h2_as_u32(__hmul2(__hsub2(u32_as_h2(hA), z2a), s2a));
+        const uint32_t a1 = h2_as_u32(__hmul2(__hsub2(u32_as_h2(lB), z2b), s2b));
+        const uint32_t a3 = h2_as_u32(__hmul2(__hsub2(u32_as_h2(hB), z2b), s2b));
+        const uint4 xq = xv[jj >> 1];
+        const uint32_t b0 = (jj & 1) ? xq.z : xq.x, b1 = (jj & 1) ? xq.w : xq.y;
+        mma16816(acc, a0, a1, a2, a3, b0, b1);
+      }
+    }
+    if (kp == 1) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) red[mt][i][lane] = acc[i];
+    }
+    __syncthreads();
+    if (kp == 0) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) acc[i] += red[mt][i][lane];
+      if (MODE == 2) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          cs[2 * t + (i & 1)][mt * 16 + g + 8 * (i >> 1)] = __half2float(__float2half(acc[i]));
+      } else {
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int tok = 2 * t + h;
+          if (tok < nc) {
+            __half* yr = y + (long)ent[c0 + tok] * ldy;
+            yr[ra_out] = __float2half(acc[h]);
+            yr[ra_out + 8] = __float2half(acc[2 + h]);
+          }
+        }
+      }
+    }
+    if (MODE == 2) {
+      __syncthreads();
+      if (warp < nc) {
+        const float gg = cs[warp][lane], uu = cs[warp][32 + lane];
+        const float v = fwht32_lane(gg / (1.0f + expf(-gg)) * uu, lane);
+        y[(long)ent[c0 + warp] * ldy + tile * 32 + lane] = __float2half(v);
+      }
+    }
+    __syncthreads();
   }
 }
 
@@ -586,6 +784,34 @@ __global__ void residual_f32_kernel(const void* __restrict__ sumv, const __half*
 
 using namespace r4q;
 
+typedef CUresult (*MoeEncodeFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+// Stacked expert nibbles [rows, row_bytes] as a 2-D byte tensor, box 128 bytes
+// x 32 rows, 128-byte swizzle.
+static int moe_weight_map(CUtensorMap* m, const void* base, long rows, long row_bytes) {
+  static MoeEncodeFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<MoeEncodeFn>(f);
+  });
+  if (!fn) return set_error(R4Q_ERR_CUDA, "moe_gemv: cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[2] = {(cuuint64_t)row_bytes, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)row_bytes};
+  cuuint32_t box[2] = {128, 32};
+  cuuint32_t es[2] = {1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, es,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(R4Q_ERR_CUDA, "moe_gemv: tensor map encode failed (%d)", (int)r);
+  return R4Q_OK;
+}
+
 static int pdl_status(cudaError_t e, const char* what) {
   if (e != cudaSuccess) {
     cudaGetLastError();
@@ -642,7 +868,7 @@ extern "C" int r4q_norm_fwht_rows(const void* x, const float* ss_in, int ss_part
 extern "C" int r4q_moe_gemv(int mode, const void* w, const void* sz, const void* x, long ldx, void* y, long ldy,
                             int N, int K, int E, int e_lo, int e_hi, int B, int topk, const int* counts,
                             const int* offsets, const int* list, const int* active, const int* n_active,
-                            void* stream) {
+                            int* status, void* stream) {
   if (!w || !sz || !x || !y || !counts || !offsets || !list || !active || !n_active || N < 64 || N % 64 ||
       K < 128 || K % 128 || E < 1 || B < 1 || topk < 1 || mode < 0 || mode > 2 || e_lo < 0 || e_hi > E ||
       e_lo >= e_hi)
@@ -652,6 +878,30 @@ extern "C" int r4q_moe_gemv(int mode, const void* w, const void* sz, const void*
   MoeRoute rt{counts, offsets, list, active, n_active};
   const int el = e_hi - e_lo;
   const int slots = (el < B * topk) ? el : B * topk;
+  cudaStream_t st = (cudaStream_t)stream;
+  const uint8_t* wp = (const uint8_t*)w;
+  const __half *sp = (const __half*)sz, *xp = (const __half*)x;
+  // TMA tiles when the 64-row tile fits two or more CTAs per SM
+  // (R4Q_MOE_LDG = 1 forces the register-staged kernel, measurement only)
+  static const int force_ldg = [] {
+    const char* v = getenv("R4Q_MOE_LDG");
+    return v ? atoi(v) : 0;
+  }();
+  const size_t tma_smem = (size_t)32 * K + 1024;
+  if (!force_ldg && K % 256 == 0 && tma_smem <= 100 * 1024) {
+    CUtensorMap tm;
+    int rc = moe_weight_map(&tm, w, (long)el * N, K / 2);
+    if (rc) return rc;
+    auto k = mode == 0 ? moe_gemv_tma_kernel<0> : mode == 1 ? moe_gemv_tma_kernel<1> : moe_gemv_tma_kernel<2>;
+    static std::atomic<size_t> set_to[3];
+    if (set_to[mode].load() < tma_smem) {
+      cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tma_smem);
+      set_to[mode].store(tma_smem);
+    }
+    return pdl_status(launch_pdl(k, dim3(N / 64, slots), dim3(kMoeThreads), tma_smem, st, tm, sp, xp, ldx, (__half*)y,
+                                 ldy, N, K, topk, e_lo, rt, status),
+                      "moe_gemv_tma_kernel");
+  }
   // one CTA per (active-expert slot, tile); the kernel also runs as a
   // persistent grid (R4Q_MOE_GRID = CTA count, measurement only) — measured
   // on B200 the full grid is faster (B = 64: 101 us against 115 us for 296
@@ -664,9 +914,6 @@ extern "C" int r4q_moe_gemv(int mode, const void* w, const void* sz, const void*
   long ctas = forced > 0 ? forced : items_max;
   if (ctas > items_max) ctas = items_max;
   dim3 grid((unsigned)ctas);
-  cudaStream_t st = (cudaStream_t)stream;
-  const uint8_t* wp = (const uint8_t*)w;
-  const __half *sp = (const __half*)sz, *xp = (const __half*)x;
   auto k = mode == 0 ? moe_gemv_kernel<0> : mode == 1 ? moe_gemv_kernel<1> : moe_gemv_kernel<2>;
   return pdl_status(launch_pdl(k, grid, dim3(kMoeThreads), 0, st, wp, sp, xp, ldx, (__half*)y, ldy, N, K, topk, e_lo,
                                rt), "moe_gemv_kernel");

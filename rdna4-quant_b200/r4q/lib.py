@@ -92,7 +92,7 @@ _SIGS = {
     "r4q_moe_router": (i32, [vp, vp, i32, vp, f32, vp, vp, vp, i32, i32, i32, i32, i32, i32, vp, vp, vp, vp, vp, vp,
                              vp, vp, vp]),
     "r4q_moe_gemv": (i32, [i32, vp, vp, vp, i64, vp, i64, i32, i32, i32, i32, i32, i32, i32, vp, vp, vp, vp, vp,
-                           vp]),
+                           vp, vp]),
     "r4q_moe_combine": (i32, [vp, vp, vp, i32, i32, vp, vp, vp, vp, i32, i32, i32, vp]),
     "r4q_residual_f32": (i32, [vp, vp, vp, vp, i32, i32, vp]),
     "r4q_residual_f16": (i32, [vp, vp, vp, vp, i32, i32, vp]),

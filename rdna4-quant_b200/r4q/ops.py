@@ -279,6 +279,7 @@ class MoeRouteBuffers:
         self.active = torch.empty(E, **i32)
         self.n_active = torch.empty(1, **i32)
         self.done = torch.zeros(1, **i32)          # CTA counter of the fused router (kept zero between calls)
+        self.status = torch.zeros(1, **i32)        # set by a kernel whose bounded wait gave up
 
 
 def moe_route(logits: torch.Tensor, topk: int, rb: MoeRouteBuffers | None = None) -> MoeRouteBuffers:
@@ -333,7 +334,7 @@ def moe_gemv(mode: int, w: torch.Tensor, sz: torch.Tensor, x: torch.Tensor, rb: 
                                                 device=dev)
     L.call("r4q_moe_gemv", mode, w.data_ptr(), sz.data_ptr(), x.data_ptr(), x.stride(0), y.data_ptr(), y.stride(0),
            N, K, rb.E, rb.e_lo, rb.e_hi, rb.B, rb.topk, rb.counts.data_ptr(), rb.offsets.data_ptr(), rb.list.data_ptr(),
-           rb.active.data_ptr(), rb.n_active.data_ptr(), stream_handle(dev))
+           rb.active.data_ptr(), rb.n_active.data_ptr(), rb.status.data_ptr(), stream_handle(dev))
     return y
 
 

@@ -28,12 +28,15 @@ def _lin4(w, s, e, N):
     return ('int4', _np(w[e * N:(e + 1) * N]), _np(s[e * N:(e + 1) * N]))
 
 
-@pytest.mark.parametrize("B", [1, 5, 40])
-def test_grouped_expert_gemv(B):
+@pytest.mark.parametrize("B,D", [(1, 256), (5, 256), (40, 256), (5, 4096)])
+def test_grouped_expert_gemv(B, D):
+    """D = 256: gate_up on the TMA-tile kernel, down (K = 128) on the
+    register-staged one; D = 4096: gate_up (K = 4096, tile above 100 KB) on
+    the register-staged kernel too."""
     from r4q import ops, synth
     dev = torch.device('cuda')
     g = torch.Generator(device=dev).manual_seed(B)
-    E, k, D, Ie = 16, 4, 256, 128
+    E, k, Ie = 16, 4, 128
     wgu, sgu = synth.quantize_int4_asym(synth.weight_fp32(E * 2 * Ie, D, g, dev))
     wd, sd = synth.quantize_int4_asym(synth.weight_fp32(E * D, Ie, g, dev))
     logits = (torch.randn(B, E, generator=g, device=dev) * 2).half()
@@ -54,6 +57,7 @@ def test_grouped_expert_gemv(B):
             ref_act = O.silu_fwht(_np(gu)[b * k + j:b * k + j + 1, :Ie], _np(gu)[b * k + j:b * k + j + 1, Ie:])
             close(_np(act)[b * k + j:b * k + j + 1], ref_act)
             close(_np(yk)[b * k + j:b * k + j + 1], O.linear(_np(act)[b * k + j:b * k + j + 1], _lin4(wd, sd, e, D)))
+    assert int(rb.status.item()) == 0
     # grouping: every entry once, experts ascending, token order inside
     cnt, off, lst = _np(rb.counts), _np(rb.offsets), _np(rb.list)
     for e in range(E):
