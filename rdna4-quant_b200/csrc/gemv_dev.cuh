@@ -65,6 +65,32 @@ __device__ __forceinline__ uint4 tp_row8(const GemvParams& p, int col, int k) {
   return out;
 }
 
+// tp_row8 plus the sum of squares of the unrounded fp16(sum) + residual
+// values (what the residual epilogue of the 1-GPU path accumulates).
+__device__ __forceinline__ uint4 tp_row8_ss(const GemvParams& p, int col, int k, float& ss) {
+  const float* rb = p.tpx.red + (long)col * p.K + k;
+  float4 a0 = __ldcg(reinterpret_cast<const float4*>(rb));
+  float4 a1 = __ldcg(reinterpret_cast<const float4*>(rb + 4));
+  for (int s = 1; s < p.tpx.nwait; ++s) {
+    const float4 b0 = __ldcg(reinterpret_cast<const float4*>(rb + s * p.tpx.red_slot));
+    const float4 b1 = __ldcg(reinterpret_cast<const float4*>(rb + s * p.tpx.red_slot + 4));
+    a0.x += b0.x; a0.y += b0.y; a0.z += b0.z; a0.w += b0.w;
+    a1.x += b1.x; a1.y += b1.y; a1.z += b1.z; a1.w += b1.w;
+  }
+  const uint4 rr = *reinterpret_cast<const uint4*>(p.tpx.red_res + (long)col * p.K + k);
+  const __half* hr = reinterpret_cast<const __half*>(&rr);
+  const float a[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+  uint4 out;
+  __half* ho = reinterpret_cast<__half*>(&out);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const float v = __half2float(__float2half(a[j])) + __half2float(hr[j]);
+    ss += v * v;
+    ho[j] = __float2half(v);
+  }
+  return out;
+}
+
 __host__ __device__ inline int steps_total(int K, int ck, int u) {
   const int nch = K / ck;
   return (nch + 4 * u - 1) / (4 * u);
@@ -276,10 +302,12 @@ __device__ __forceinline__ void chunk_mma(const RowChunk& ra, const RowChunk& rb
 // 8 and 16 across the quad, same stage order as the 32-register form) and
 // stores its 8 values as one 16-byte sub-row of the permuted layout.  All 32
 // lanes of the warp must call it (shuffles); `valid` masks the stores.
+// have_raw: the 8 input values are given (a TP consumer read them already).
 template <int FMT, bool DIAG>
 __device__ __forceinline__ void stage_quad(const GemvParams& p, int col, int k0, int q, float rrms,
                                            uint8_t* xs_col, int nch_pad, int blk, bool valid,
-                                           float2* xsum_slot) {
+                                           float2* xsum_slot, bool have_raw = false,
+                                           uint4 raw_in = uint4{0, 0, 0, 0}) {
   __half v[8];
   const bool in = valid && k0 < p.K;
   const __half* xr = p.x + (long)col * p.ldx + k0 + 8 * q;
@@ -289,7 +317,8 @@ __device__ __forceinline__ void stage_quad(const GemvParams& p, int col, int k0,
   } else {
     float f[8];
     if (in) {
-      const uint4 raw = p.tpx.nwait ? tp_row8(p, col, k0 + 8 * q) : *reinterpret_cast<const uint4*>(xr);
+      const uint4 raw = have_raw ? raw_in
+                        : p.tpx.nwait ? tp_row8(p, col, k0 + 8 * q) : *reinterpret_cast<const uint4*>(xr);
       const __half* h = reinterpret_cast<const __half*>(&raw);
       if (p.prologue == R4Q_PRO_SILU_FWHT) {
         const uint4 ru = *reinterpret_cast<const uint4*>(xr + p.K);

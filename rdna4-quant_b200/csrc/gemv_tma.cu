@@ -36,6 +36,7 @@ constexpr int kTmaThreads = (kTmaConsumers + 1) * 32;
 constexpr int kTileRows = 64;
 constexpr int kTmaMaxSplit = 32;
 constexpr long kSpinLimit = 1L << 26;
+constexpr int kTpPre = 3;      // staging items per thread held in registers by a TP consumer
 
 #ifdef R4Q_TRACE
 // Development-only event trace (compiled only with -DR4Q_TRACE).
@@ -277,6 +278,13 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
 
   const bool stamp = blockIdx.x == 0 && ctid == 0;
   if (stamp && p.tpx.nsig) tp_stamp(p.tpx, 0, p.tpx.sig_idx);
+  // TP consumer with the whole K staged here and at most kTpPre staging items
+  // per thread: read the exchange buffer once (see below)
+  const int tp_nblk = nch_pad * F::CK / 32;
+  const int tp_items = ncolx * tp_nblk * 4;
+  const bool tp_one = p.tpx.nwait && DIAG && st0 == 0 && nst == tp.nstages &&
+                      tp_items <= kTmaConsumers * 32 * kTpPre;
+  uint4 tp_raw[kTpPre];
   if (p.tpx.nwait) {
     // tensor-parallel consumer: wait for every rank's partials, then r and
     // its sum of squares straight from the exchange buffer (CTA 0 stores r)
@@ -284,9 +292,38 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
     if (warp == 0) tp_wait_lane(p.tpx, lane);
     consumer_sync();
     if (stamp) tp_stamp(p.tpx, 3, p.tpx.wait_idx);
+    __shared__ float s_ssp[kTmaConsumers][16];
+    if (tp_one) {
+      // one pass (whole K staged, B <= 2): every thread reads its staging
+      // items' r values once, keeps them in registers for the staging below
+      // and accumulates the sums of squares
+      float ssc[2] = {0.0f, 0.0f};
+#pragma unroll
+      for (int r = 0; r < kTpPre; ++r) {
+        const int item = warp * 32 + lane + r * (kTmaConsumers * 32);
+        tp_raw[r] = make_uint4(0, 0, 0, 0);
+        if (item < tp_items) {
+          const int qq = item & 3, cb = item >> 2;
+          const int col = cb / tp_nblk, blk = cb - col * tp_nblk;
+          const int k = blk * 32 + qq * 8;
+          if (k < p.K) {
+            float ss = 0.0f;
+            tp_raw[r] = tp_row8_ss(p, col, k, ss);
+            if (col) ssc[1] += ss;
+            else ssc[0] += ss;
+            if (blockIdx.x == 0 && p.tpx.red_out)
+              *reinterpret_cast<uint4*>(p.tpx.red_out + (long)col * p.K + k) = tp_raw[r];
+          }
+        }
+      }
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        const float ss = warp_sum(ssc[c]);
+        if (lane == 0 && c < ncolx) s_ssp[warp][c] = ss;
+      }
+    } else
     // every consumer thread takes 4 consecutive k of every column; partial
     // sums of squares per (warp, column) meet in shared memory
-    __shared__ float s_ssp[kTmaConsumers][16];
     for (int c = 0; c < ncolx; ++c) {
       const float* rb = p.tpx.red + (long)c * p.K;
       const __half* hr = p.tpx.red_res + (long)c * p.K;
@@ -347,10 +384,17 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
       const int it2 = valid ? item : 0;
       const int q = it2 & 3, cb = it2 >> 2;
       const int col = cb / nblk, blk = cb - col * nblk;
+      const int rnd = (base - warp * 32) / (kTmaConsumers * 32);         // round of this item
+      uint4 raw_in = make_uint4(0, 0, 0, 0);
+      if (tp_one) {
+#pragma unroll
+        for (int r = 0; r < kTpPre; ++r)
+          if (r == rnd) raw_in = tp_raw[r];
+      }
       stage_quad<FMT, DIAG>(p, col, k_base + blk * 32, q,
                             p.prologue == R4Q_PRO_RMSNORM_FWHT ? s_rrms[col] : 1.0f,
                             xs + (long)col * colstride, nch_pad, blk, valid,
-                            xsum + col * nch_pad + blk);
+                            xsum + col * nch_pad + blk, tp_one, raw_in);
     }
     if (ctid < 4) reinterpret_cast<uint32_t*>(zero16)[ctid] = 0u;
   }
