@@ -336,10 +336,10 @@ int r4q_decode_loop(r4q_decode_ctx* ctx, const void* embed, const void* hidden_f
 int r4q_decode_profile(r4q_decode_ctx* ctx, const void* hidden_in, int pos, float* out5, void* stream);
 
 /* Exchange timeline of a tensor-parallel context created with the environment
- * variable R4Q_TP_TRACE set (synchronous; host array of 6 x 256 u64 global-timer
+ * variable R4Q_TP_TRACE set (synchronous; host array of 8 x 256 u64 global-timer
  * stamps in ns, per exchange index: producer compute start, producer signal,
  * consumer wait start, consumer wait end, consumer input staged, producer
- * entry).  A profiling aid; R4Q_ERR_ARG when the context has no trace. */
+ * entry, producer CTA 0 done, producer's last CTA arrived).  A profiling aid; R4Q_ERR_ARG when the context has no trace. */
 int r4q_decode_tp_trace(r4q_decode_ctx* ctx, unsigned long long* host);
 
 /* ------------------------------------------- tensor-parallel exchange --- */

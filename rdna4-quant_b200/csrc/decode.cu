@@ -53,7 +53,7 @@ struct r4q_decode_ctx {
   };
   bool prof;
   std::vector<ProfEv> prof_ev;
-  unsigned long long* tp_trace;  // R4Q_TP_TRACE: exchange timeline u64 [6][256]
+  unsigned long long* tp_trace;  // R4Q_TP_TRACE: exchange timeline u64 [8][256]
 };
 
 namespace r4q {
@@ -444,8 +444,8 @@ extern "C" int r4q_decode_ctx_create(const r4q_model_desc* md, const r4q_layer_d
     }
   }
   if (tps > 1 && getenv("R4Q_TP_TRACE")) {
-    if (cudaMalloc(&c->tp_trace, 6 * kTpExchangesPerStep * 8) != cudaSuccess ||
-        cudaMemset(c->tp_trace, 0, 6 * kTpExchangesPerStep * 8) != cudaSuccess) {
+    if (cudaMalloc(&c->tp_trace, 8 * kTpExchangesPerStep * 8) != cudaSuccess ||
+        cudaMemset(c->tp_trace, 0, 8 * kTpExchangesPerStep * 8) != cudaSuccess) {
       free_ctx(c);
       return set_error(R4Q_ERR_CUDA, "decode_ctx_create: trace buffer");
     }
@@ -643,6 +643,6 @@ extern "C" int r4q_decode_profile(r4q_decode_ctx* c, const void* hidden_in, int 
 extern "C" int r4q_decode_tp_trace(r4q_decode_ctx* c, unsigned long long* host) {
   if (!c || !host) return set_error(R4Q_ERR_ARG, "decode_tp_trace: null argument");
   if (!c->tp_trace) return set_error(R4Q_ERR_ARG, "decode_tp_trace: context built without R4Q_TP_TRACE");
-  cudaError_t e = cudaMemcpy(host, c->tp_trace, 6 * kTpExchangesPerStep * 8, cudaMemcpyDeviceToHost);
+  cudaError_t e = cudaMemcpy(host, c->tp_trace, 8 * kTpExchangesPerStep * 8, cudaMemcpyDeviceToHost);
   return e == cudaSuccess ? R4Q_OK : set_error(R4Q_ERR_CUDA, "decode_tp_trace: %s", cudaGetErrorString(e));
 }

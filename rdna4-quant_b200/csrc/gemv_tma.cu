@@ -693,6 +693,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
   // outputs pushed into peer memory: the last CTA signals the exchange to
   // every rank once all CTAs' pushes are fenced at system scope
   if (p.tpx.nsig) {
+    if (stamp) tp_stamp(p.tpx, 6, p.tpx.sig_idx);
     consumer_sync();
     if (ctid == 0) tp_signal_cta(p.tpx);
   } else if (p.npush > 1) {

@@ -43,9 +43,10 @@ struct TpExchange {
   // both
   const unsigned long long* ep_ctr;      // step counter
   unsigned long long* status;            // timeout bits (one per rank waited for)
-  // optional timeline (R4Q_TP_TRACE): u64 [6][256] global-timer stamps per
+  // optional timeline (R4Q_TP_TRACE): u64 [8][256] global-timer stamps per
   // exchange index: 0 producer compute start, 1 producer signal, 2 consumer
-  // wait start, 3 consumer wait end, 4 consumer input staged, 5 producer entry
+  // wait start, 3 consumer wait end, 4 consumer input staged, 5 producer
+  // entry, 6 producer CTA 0 done, 7 producer's last CTA arrived
   unsigned long long* trace;
 };
 
@@ -89,19 +90,23 @@ __device__ __forceinline__ void tp_wait_lane(const TpExchange& x, int lane) {
 }
 
 // One thread per CTA, after a CTA-wide barrier that follows every thread's
-// pushes: a system-scope fence (cumulative over the writes the barrier made
-// visible to this thread — the grid-barrier pattern at system scope), then
-// the last CTA to arrive publishes the epoch to all ranks.
+// pushes: a system-scope acq_rel fence (cumulative over the writes the
+// barrier made visible to this thread; it completes once those pushes are
+// performed at system scope), then the gpu-scope counter.  The last CTA to
+// arrive therefore finds every CTA's pushes already performed system-wide and
+// publishes the epoch to all ranks with plain system-scope stores.  Measured
+// on B200 (2 GPUs): each fence.sc.sys, and each st.release.sys, cost ~5 us
+// here — against an exchange whose data moves in ~1 us.
 __device__ __forceinline__ void tp_signal_cta(const TpExchange& x) {
-  __threadfence_system();
+  asm volatile("fence.acq_rel.sys;" ::: "memory");
   unsigned old;
   asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(old) : "l"(x.sig_done) : "memory");
   if (old != gridDim.x * gridDim.y * gridDim.z - 1) return;
+  tp_stamp(x, 7, x.sig_idx);
   *x.sig_done = 0u;
   const unsigned long long e = tp_epoch(x, x.sig_idx);
-  __threadfence_system();
   for (int q = 0; q < x.nsig; ++q)
-    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(x.sig[q]), "l"(e) : "memory");
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(x.sig[q]), "l"(e) : "memory");
   tp_stamp(x, 1, x.sig_idx);
 }
 #endif
