@@ -173,27 +173,60 @@ __global__ void gather_kernel(const SyncArgs s, const float* __restrict__ gat, _
   comm_done(s, e);
 }
 
-// Standalone all-reduce, step 1: push x into slot [rank] of every rank.
+// Standalone all-reduce (the expert-parallel MoE sum), flag-free: every
+// element travels as one 64-bit word (epoch << 32 | fp32 bits), so a reader
+// knows an element has arrived from the element itself — no fence, no flag
+// (each system-scope fence or release store cost ~5 us on B200).  The epoch
+// is this rank's count of completed all-reduces + 1, the same on every rank.
+// Step 1: push x into slot [rank] of every rank.
 struct PushTable {
-  float* p[kMaxWorld];
+  unsigned long long* p[kMaxWorld];
 };
 
-__global__ void push_kernel_t(const float* __restrict__ x, const PushTable t, int world, long n) {
+__global__ void push_kernel_t(const float* __restrict__ x, const PushTable t, int world, long n,
+                              const unsigned long long* ctl) {
+  const unsigned long long e = (*(volatile const unsigned long long*)&ctl[0] + 1ull) & 0xffffffffull;
   for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
-    const float v = x[i];
-    for (int r = 0; r < world; ++r) t.p[r][i] = v;
+    const unsigned long long w = (e << 32) | (unsigned long long)__float_as_uint(x[i]);
+    for (int r = 0; r < world; ++r)
+      asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(t.p[r] + i), "l"(w) : "memory");
   }
-  __threadfence_system();
 }
 
-// Standalone all-reduce, step 2: sync, y = sum over src in rank order.
-__global__ void sum_kernel(const SyncArgs s, const float* __restrict__ sa, long slot, float* __restrict__ y,
+// Step 2: y = sum over src in rank order, each element waited for (bounded
+// by ~2 s of wall time, then the missing rank is recorded and 0 used).
+__global__ void sum_kernel(const SyncArgs s, const unsigned long long* sa, long slot, float* __restrict__ y,
                            long n) {
-  unsigned long long e;
-  comm_sync(s, e);
+  __shared__ unsigned long long s_ep;
+  if (threadIdx.x == 0) s_ep = *(volatile unsigned long long*)&s.ctl[0] + 1ull;
+  __syncthreads();
+  const unsigned long long e = s_ep;
+  const unsigned long long tag = e & 0xffffffffull;
   for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
-    float v = __ldcg(sa + i);
-    for (int r = 1; r < s.world; ++r) v += __ldcg(sa + r * slot + i);
+    float v = 0.0f;
+    for (int r = 0; r < s.world; ++r) {
+      unsigned long long w;
+      const unsigned long long* a = sa + r * slot + i;
+      asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w) : "l"(a) : "memory");
+      if ((w >> 32) != tag && !((*(volatile unsigned long long*)&s.ctl[2] >> r) & 1ull)) {
+        // (a rank that already timed out in this call is not waited for again)
+        const unsigned long long t0 = globaltimer();
+        unsigned it = 0;
+        for (;;) {
+          __nanosleep(32);
+          asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w) : "l"(a) : "memory");
+          if ((w >> 32) == tag) break;
+          if ((++it & 63) == 0 && globaltimer() - t0 > 2000000000ull) {
+            atomicOr(&s.ctl[2], 1ull << r);
+            w = 0;
+            break;
+          }
+        }
+      }
+      if ((w >> 32) != tag) w = 0;
+      const float f = __uint_as_float((unsigned)(w & 0xffffffffull));
+      v = r == 0 ? f : v + f;
+    }
     y[i] = v;
   }
   comm_done(s, e);
@@ -307,7 +340,7 @@ extern "C" int r4q_comm_create(int rank, int world, int max_batch, int hidden, i
   c->off_red = 256;
   c->off_gat = c->off_red + 2 * world * c->red_slot * 4;
   c->off_sa = c->off_gat + align256((size_t)max_batch * vocab * 4);
-  c->bytes = c->off_sa + 2 * world * c->sa_slot * 4 + 256;
+  c->bytes = c->off_sa + 2 * world * c->sa_slot * 8 + 256;     // all-reduce words: epoch | fp32
   cudaError_t e = cudaMalloc(&c->base, c->bytes);
   if (e == cudaSuccess) e = cudaMemset(c->base, 0, c->bytes);
   if (e == cudaSuccess) e = cudaMalloc(&c->ctl, 64 + 4 * kTpExchangesPerStep);
@@ -384,14 +417,16 @@ extern "C" int r4q_comm_allreduce_f32(r4q_comm* c, const float* x, float* y, lon
   c->sa_calls++;
   PushTable t{};
   for (int r = 0; r < c->world; ++r)
-    t.p[r] = reinterpret_cast<float*>(c->peer[r] + c->off_sa) + ((size_t)par * c->world + c->rank) * c->sa_slot;
+    t.p[r] = reinterpret_cast<unsigned long long*>(c->peer[r] + c->off_sa) +
+             ((size_t)par * c->world + c->rank) * c->sa_slot;
   int grid = (int)((n + 255) / 256);
   if (grid > 2 * num_sms()) grid = 2 * num_sms();
   if (grid < 1) grid = 1;
-  push_kernel_t<<<grid, 256, 0, st>>>(x, t, c->world, n);
+  push_kernel_t<<<grid, 256, 0, st>>>(x, t, c->world, n, c->ctl);
   int rc = check_launch("push_kernel");
   if (rc) return rc;
-  const float* sa = reinterpret_cast<const float*>(c->base + c->off_sa) + (size_t)par * c->world * c->sa_slot;
+  const unsigned long long* sa =
+      reinterpret_cast<const unsigned long long*>(c->base + c->off_sa) + (size_t)par * c->world * c->sa_slot;
   sum_kernel<<<grid, 256, 0, st>>>(sync_args(c, kFlagsSA, 0, false), sa, (long)c->sa_slot, y, n);
   return check_launch("sum_kernel");
 }
