@@ -250,9 +250,10 @@ __global__ void tick_kernel(unsigned long long* ctr) { *ctr += 1ull; }
 
 }  // namespace
 
-float* comm_reduce_slot(r4q_comm* c, int peer, int parity) {
-  return reinterpret_cast<float*>(c->peer[peer] + c->off_red) +
-         ((size_t)(parity & 1) * c->world + c->rank) * c->red_slot;
+float* comm_reduce_slot(r4q_comm* c, int peer, int parity, bool ll) {
+  const size_t i = ((size_t)(parity & 1) * c->world + c->rank) * c->red_slot;
+  if (ll) return reinterpret_cast<float*>(reinterpret_cast<unsigned long long*>(c->peer[peer] + c->off_red) + i);
+  return reinterpret_cast<float*>(c->peer[peer] + c->off_red) + i;
 }
 float* comm_gather_base(r4q_comm* c, int peer) {
   return reinterpret_cast<float*>(c->peer[peer] + c->off_gat);
@@ -273,11 +274,14 @@ void comm_fill_signal(r4q_comm* c, TpExchange& x, int idx) {
   x.status = c->ctl + 2;
 }
 
-void comm_fill_wait(r4q_comm* c, TpExchange& x, int idx, int parity, const __half* res, __half* out) {
+void comm_fill_wait(r4q_comm* c, TpExchange& x, int idx, int parity, const __half* res, __half* out, bool ll) {
   x.wait_flags = reinterpret_cast<const unsigned long long*>(c->base + kFlagsX);
   x.nwait = c->world;
   x.wait_idx = idx;
-  x.red = reinterpret_cast<const float*>(c->base + c->off_red) + (size_t)(parity & 1) * c->world * c->red_slot;
+  x.ll_wait = ll ? 1 : 0;
+  const size_t i = (size_t)(parity & 1) * c->world * c->red_slot;
+  x.red = ll ? reinterpret_cast<const float*>(reinterpret_cast<const unsigned long long*>(c->base + c->off_red) + i)
+             : reinterpret_cast<const float*>(c->base + c->off_red) + i;
   x.red_slot = (long)c->red_slot;
   x.red_res = res;
   x.red_out = out;
@@ -338,7 +342,7 @@ extern "C" int r4q_comm_create(int rank, int world, int max_batch, int hidden, i
   c->red_slot = align256((size_t)max_batch * hidden * 4) / 4;
   c->sa_slot = (size_t)c->sa_cap;
   c->off_red = 256;
-  c->off_gat = c->off_red + 2 * world * c->red_slot * 4;
+  c->off_gat = c->off_red + 2 * world * c->red_slot * 8;   // room for tagged 64-bit words
   c->off_sa = c->off_gat + align256((size_t)max_batch * vocab * 4);
   c->bytes = c->off_sa + 2 * world * c->sa_slot * 8 + 256;     // all-reduce words: epoch | fp32
   cudaError_t e = cudaMalloc(&c->base, c->bytes);

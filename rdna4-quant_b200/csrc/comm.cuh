@@ -21,8 +21,9 @@
 namespace r4q {
 
 // Base of rank `rank`'s all-reduce slot inside peer `peer`'s buffer (parity 0/1):
-// [max_batch * hidden] floats, row stride `hidden`.
-float* comm_reduce_slot(r4q_comm* c, int peer, int parity);
+// [max_batch * hidden] elements, row stride `hidden` — floats, or with `ll`
+// 64-bit tagged words (the pointer is then indexed as unsigned long long).
+float* comm_reduce_slot(r4q_comm* c, int peer, int parity, bool ll = false);
 // Base of peer `peer`'s gather buffer [max_batch][vocab].
 float* comm_gather_base(r4q_comm* c, int peer);
 int comm_rank(const r4q_comm* c);
@@ -36,7 +37,9 @@ int comm_hidden(const r4q_comm* c);
 void comm_fill_signal(r4q_comm* c, TpExchange& x, int idx);
 // Consumer GEMV prologue: wait for exchange idx, read reduce slots of `parity`,
 // r = fp16(fp16(sum) + res) (res [B][hidden]); CTA 0 stores r to out.
-void comm_fill_wait(r4q_comm* c, TpExchange& x, int idx, int parity, const __half* res, __half* out);
+// ll: the producer pushed tagged words (no flag to wait for).
+void comm_fill_wait(r4q_comm* c, TpExchange& x, int idx, int parity, const __half* res, __half* out,
+                    bool ll = false);
 // Advance the step counter (once at the start of every decode step).
 int comm_tick(r4q_comm* c, cudaStream_t st);
 // Stand-alone consumer of exchange idx: out[b, d] = fp16(fp16(sum_src

@@ -216,10 +216,37 @@ struct PushSet {
   float* p[8];
   operator float* const*() const { return p; }
 };
-static PushSet push_slots(r4q_decode_ctx* c, int parity) {
+static PushSet push_slots(r4q_decode_ctx* c, int parity, bool ll) {
   PushSet s{};
-  for (int q = 0; q < c->m.tp_size; ++q) s.p[q] = comm_reduce_slot(c->m.comm, q, parity);
+  for (int q = 0; q < c->m.tp_size; ++q) s.p[q] = comm_reduce_slot(c->m.comm, q, parity, ll);
   return s;
+}
+
+// The consumer GEMV of an exchange reads the slots in its prologue (TMA path);
+// otherwise a reduce kernel materialises r first.
+static bool consumer_fused(r4q_decode_ctx* c, int fmt, const void* w, const void* s, int N) {
+  GemvArgs probe{};
+  probe.K = c->m.hidden; probe.N = N; probe.B = c->m.batch; probe.w = w; probe.s = s;
+  return gemv_tma_supported(probe, fmt) && !getenv_ldg();
+}
+
+// A producer whose consumer is fused pushes tagged words (no fence, no flag,
+// the consumer polls the words); R4Q_TP_FLAGS=1 keeps the flag protocol
+// (measurement only).
+static bool exchange_ll(bool consumer_is_fused) {
+  static const bool flags = [] {
+    const char* e = getenv("R4Q_TP_FLAGS");
+    return e && e[0] == '1';
+  }();
+  return consumer_is_fused && !flags;
+}
+
+static void producer_exchange(r4q_decode_ctx* c, TpExchange& x, int idx, bool ll) {
+  comm_fill_signal(c->m.comm, x, idx);
+  if (ll) {
+    x.ll_sig = 1;
+    x.nsig = 0;      // no flag: the words carry the epoch
+  }
 }
 
 // Head norm + RoPE + KV write of the new token and attention over [0, pos]
@@ -258,13 +285,11 @@ static int consume(r4q_decode_ctx* c, int idx, const __half* res, __half* out, f
                    float* const* push = nullptr, int npush = 0, long ld_push = 0, int sig_idx = -1) {
   const r4q_model_desc& m = c->m;
   const int D = m.hidden;
-  GemvArgs probe{};
-  probe.K = D; probe.N = N; probe.B = m.batch; probe.w = w; probe.s = s;
-  const bool fused = gemv_tma_supported(probe, fmt) && !getenv_ldg();
+  const bool fused = consumer_fused(c, fmt, w, s, N);
   TpExchange x{};
   int rc = 0;
   if (fused) {
-    comm_fill_wait(m.comm, x, idx, idx & 1, res, out);
+    comm_fill_wait(m.comm, x, idx, idx & 1, res, out, exchange_ll(true));
   } else {
     rc = comm_reduce_residual(m.comm, idx, idx & 1, res, out, ss, m.batch, D, st);
     if (rc) return rc;
@@ -299,22 +324,32 @@ static int enqueue_step_tp(r4q_decode_ctx* c, bool with_logits, cudaStream_t st)
     if (rc) break;
     // 4. o_proj over this rank's heads -> pushed + signalled (exchange xo)
     {
+      const bool ll = exchange_ll(consumer_fused(c, ly.gate_up_fmt, ly.gate_up_w, ly.gate_up_s, 2 * I));
       TpExchange x{};
-      comm_fill_signal(m.comm, x, xo);
+      producer_exchange(c, x, xo, ll);
       rc = gemv_call(c, ly.o_fmt, ly.o_w, ly.o_s, c->attn, nullptr, D, qd, R4Q_PRO_NONE, nullptr, nullptr,
-                     0, nullptr, nullptr, st, push_slots(c, xo & 1), m.tp_size, D, &x);
+                     0, nullptr, nullptr, st, push_slots(c, xo & 1, ll), m.tp_size, D, &x);
     }
     if (rc) break;
     // 5. gate_up consumes exchange xo: r = o + h
     rc = consume(c, xo, hin, c->r, c->ss_post, ly.gate_up_fmt, ly.gate_up_w, ly.gate_up_s, c->gu, 2 * I,
                  ly.post_norm, st);
     if (rc) break;
-    // 6. down over this rank's intermediate slice -> pushed + signalled (xd)
+    // 6. down over this rank's intermediate slice -> pushed + signalled (xd);
+    //    its consumer: the next layer's qkv, or the lm_head (or the final
+    //    reduce kernel without logits)
     {
+      bool ll;
+      if (li + 1 < L) {
+        const r4q_layer_desc& nx = c->layers[li + 1];
+        ll = exchange_ll(consumer_fused(c, nx.qkv_fmt, nx.qkv_w, nx.qkv_s, qkv_n));
+      } else {
+        ll = with_logits && exchange_ll(consumer_fused(c, m.lm_fmt, m.lm_w, m.lm_s, m.lm_n));
+      }
       TpExchange x{};
-      comm_fill_signal(m.comm, x, xd);
+      producer_exchange(c, x, xd, ll);
       rc = gemv_call(c, ly.down_fmt, ly.down_w, ly.down_s, c->gu, nullptr, D, I, R4Q_PRO_SILU_FWHT,
-                     nullptr, nullptr, 0, nullptr, nullptr, st, push_slots(c, xd & 1), m.tp_size, D, &x);
+                     nullptr, nullptr, 0, nullptr, nullptr, st, push_slots(c, xd & 1, ll), m.tp_size, D, &x);
     }
   }
   if (rc) return rc;

@@ -216,9 +216,15 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const GemvParams p) {
         for (int h = 0; h < 2; ++h) {
           const int c = cg * 8 + 2 * t + h;
           if (c < p.B && p.npush) {
+            const unsigned ll_tag = p.tpx.ll_sig ? (unsigned)tp_epoch(p.tpx, p.tpx.sig_idx) : 0u;
             for (int q = 0; q < p.npush; ++q) {
-              p.y32p[q][(long)c * p.ldy + row_a] = acc[cg][h];
-              p.y32p[q][(long)c * p.ldy + row_b] = acc[cg][2 + h];
+              if (p.tpx.ll_sig) {
+                tp_push_word(p.y32p[q], (long)c * p.ldy + row_a, ll_tag, acc[cg][h]);
+                tp_push_word(p.y32p[q], (long)c * p.ldy + row_b, ll_tag, acc[cg][2 + h]);
+              } else {
+                p.y32p[q][(long)c * p.ldy + row_a] = acc[cg][h];
+                p.y32p[q][(long)c * p.ldy + row_b] = acc[cg][2 + h];
+              }
             }
           } else if (c < p.B) {
             float va = __half2float(__float2half(acc[cg][h]));
@@ -260,7 +266,7 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const GemvParams p) {
       }
     }
   }
-  if (p.npush > 1 && !p.tpx.nsig) __threadfence_system();  // peer outputs complete before exit
+  if (p.npush > 1 && !p.tpx.nsig && !p.tpx.ll_sig) __threadfence_system();  // peer outputs complete before exit
   if (p.ksplit == 1) {
     tp_exit(p);
     return;
@@ -289,7 +295,10 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const GemvParams p) {
     for (int k2 = 0; k2 < p.ksplit; ++k2) v += __ldcg(p.part + ((long)k2 * p.B + col) * p.N + r);
     if (p.npush) {
       if (lane < 16)
-        for (int q = 0; q < p.npush; ++q) p.y32p[q][(long)col * p.ldy + r] = v;
+        for (int q = 0; q < p.npush; ++q) {
+          if (p.tpx.ll_sig) tp_push_word(p.y32p[q], (long)col * p.ldy + r, (unsigned)tp_epoch(p.tpx, p.tpx.sig_idx), v);
+          else p.y32p[q][(long)col * p.ldy + r] = v;
+        }
       continue;
     }
     v = __half2float(__float2half(v));
@@ -300,7 +309,7 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const GemvParams p) {
     if (p.ss_out && lane == 0) p.ss_out[(long)((trow0 >> 4) + ti) * p.B + col] = sq;
   }
   if (tid == 0) p.cnt[blockIdx.x] = 0u;  // leave the workspace zeroed for the next launch
-  if (p.npush > 1 && !p.tpx.nsig) __threadfence_system();
+  if (p.npush > 1 && !p.tpx.nsig && !p.tpx.ll_sig) __threadfence_system();
   tp_exit(p);
 }
 

@@ -45,8 +45,31 @@ struct GemvParams {
 
 // Tensor-parallel consumer input: 8 fp16 values r = fp16(fp16(sum over src of
 // the fp32 partials) + residual) of row `col`, elements k..k+7 (K = hidden).
-__device__ __forceinline__ uint4 tp_row8(const GemvParams& p, int col, int k) {
-  const float* rb = p.tpx.red + (long)col * p.K + k;
+__device__ __forceinline__ void tp_sum8(const GemvParams& p, int col, int k, float (&a)[8]) {
+  const float* rb = p.tpx.red + (long)col * p.K + k;      // element index (float or word)
+  if (p.tpx.ll_wait) {
+    // 16-byte L2 loads of the tagged words (a stale word just fails its tag
+    // check); any word not yet arrived is then polled on its own
+    const unsigned tag = (unsigned)tp_epoch(p.tpx, p.tpx.wait_idx);
+    for (int s = 0; s < p.tpx.nwait; ++s) {
+      const long i0 = (long)s * p.tpx.red_slot + (long)col * p.K + k;
+      const ulonglong2* w2 = reinterpret_cast<const ulonglong2*>(reinterpret_cast<const unsigned long long*>(p.tpx.red) + i0);
+      unsigned long long w[8];
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        const ulonglong2 v = __ldcg(w2 + h);
+        w[2 * h] = v.x;
+        w[2 * h + 1] = v.y;
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float f = (unsigned)(w[j] >> 32) == tag ? __uint_as_float((unsigned)w[j])
+                                                       : tp_read_word(p.tpx, p.tpx.red, i0 + j, tag, s);
+        a[j] = s == 0 ? f : a[j] + f;
+      }
+    }
+    return;
+  }
   float4 a0 = __ldcg(reinterpret_cast<const float4*>(rb));
   float4 a1 = __ldcg(reinterpret_cast<const float4*>(rb + 4));
   for (int s = 1; s < p.tpx.nwait; ++s) {
@@ -55,9 +78,15 @@ __device__ __forceinline__ uint4 tp_row8(const GemvParams& p, int col, int k) {
     a0.x += b0.x; a0.y += b0.y; a0.z += b0.z; a0.w += b0.w;
     a1.x += b1.x; a1.y += b1.y; a1.z += b1.z; a1.w += b1.w;
   }
+  a[0] = a0.x; a[1] = a0.y; a[2] = a0.z; a[3] = a0.w;
+  a[4] = a1.x; a[5] = a1.y; a[6] = a1.z; a[7] = a1.w;
+}
+
+__device__ __forceinline__ uint4 tp_row8(const GemvParams& p, int col, int k) {
+  float a[8];
+  tp_sum8(p, col, k, a);
   const uint4 rr = *reinterpret_cast<const uint4*>(p.tpx.red_res + (long)col * p.K + k);
   const __half* hr = reinterpret_cast<const __half*>(&rr);
-  const float a[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
   uint4 out;
   __half* ho = reinterpret_cast<__half*>(&out);
 #pragma unroll
@@ -68,18 +97,10 @@ __device__ __forceinline__ uint4 tp_row8(const GemvParams& p, int col, int k) {
 // tp_row8 plus the sum of squares of the unrounded fp16(sum) + residual
 // values (what the residual epilogue of the 1-GPU path accumulates).
 __device__ __forceinline__ uint4 tp_row8_ss(const GemvParams& p, int col, int k, float& ss) {
-  const float* rb = p.tpx.red + (long)col * p.K + k;
-  float4 a0 = __ldcg(reinterpret_cast<const float4*>(rb));
-  float4 a1 = __ldcg(reinterpret_cast<const float4*>(rb + 4));
-  for (int s = 1; s < p.tpx.nwait; ++s) {
-    const float4 b0 = __ldcg(reinterpret_cast<const float4*>(rb + s * p.tpx.red_slot));
-    const float4 b1 = __ldcg(reinterpret_cast<const float4*>(rb + s * p.tpx.red_slot + 4));
-    a0.x += b0.x; a0.y += b0.y; a0.z += b0.z; a0.w += b0.w;
-    a1.x += b1.x; a1.y += b1.y; a1.z += b1.z; a1.w += b1.w;
-  }
+  float a[8];
+  tp_sum8(p, col, k, a);
   const uint4 rr = *reinterpret_cast<const uint4*>(p.tpx.red_res + (long)col * p.K + k);
   const __half* hr = reinterpret_cast<const __half*>(&rr);
-  const float a[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
   uint4 out;
   __half* ho = reinterpret_cast<__half*>(&out);
 #pragma unroll

@@ -278,6 +278,8 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
 
   const bool stamp = blockIdx.x == 0 && ctid == 0;
   if (stamp && p.tpx.nsig) tp_stamp(p.tpx, 0, p.tpx.sig_idx);
+  // tag of this GEMV's pushed words (the step counter is read after the wait)
+  const unsigned ll_tag = p.tpx.ll_sig ? (unsigned)tp_epoch(p.tpx, p.tpx.sig_idx) : 0u;
   // TP consumer with the whole K staged here and at most kTpPre staging items
   // per thread: read the exchange buffer once (see below)
   const int tp_nblk = nch_pad * F::CK / 32;
@@ -289,7 +291,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
     // tensor-parallel consumer: wait for every rank's partials, then r and
     // its sum of squares straight from the exchange buffer (CTA 0 stores r)
     if (stamp) tp_stamp(p.tpx, 2, p.tpx.wait_idx);
-    if (warp == 0) tp_wait_lane(p.tpx, lane);
+    if (warp == 0 && !p.tpx.ll_wait) tp_wait_lane(p.tpx, lane);   // tagged words: the reads wait
     consumer_sync();
     if (stamp) tp_stamp(p.tpx, 3, p.tpx.wait_idx);
     __shared__ float s_ssp[kTmaConsumers][16];
@@ -330,10 +332,30 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
       __half* ro = (blockIdx.x == 0 && p.tpx.red_out) ? p.tpx.red_out + (long)c * p.K : nullptr;
       float ss = 0.0f;
       for (int k = ctid * 4; k < p.K; k += kTmaConsumers * 128) {
-        float4 a = __ldcg(reinterpret_cast<const float4*>(rb + k));
-        for (int s2 = 1; s2 < p.tpx.nwait; ++s2) {
-          const float4 b = __ldcg(reinterpret_cast<const float4*>(rb + s2 * p.tpx.red_slot + k));
-          a.x += b.x; a.y += b.y; a.z += b.z; a.w += b.w;
+        float4 a;
+        if (p.tpx.ll_wait) {
+          const unsigned tag = (unsigned)tp_epoch(p.tpx, p.tpx.wait_idx);
+          float t4[4];
+          for (int s2 = 0; s2 < p.tpx.nwait; ++s2) {
+            const long i0 = (long)s2 * p.tpx.red_slot + (long)c * p.K + k;
+            const ulonglong2* w2 =
+                reinterpret_cast<const ulonglong2*>(reinterpret_cast<const unsigned long long*>(p.tpx.red) + i0);
+            const ulonglong2 v0 = __ldcg(w2), v1 = __ldcg(w2 + 1);
+            const unsigned long long w[4] = {v0.x, v0.y, v1.x, v1.y};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const float f = (unsigned)(w[j] >> 32) == tag ? __uint_as_float((unsigned)w[j])
+                                                             : tp_read_word(p.tpx, p.tpx.red, i0 + j, tag, s2);
+              t4[j] = s2 == 0 ? f : t4[j] + f;
+            }
+          }
+          a = make_float4(t4[0], t4[1], t4[2], t4[3]);
+        } else {
+          a = __ldcg(reinterpret_cast<const float4*>(rb + k));
+          for (int s2 = 1; s2 < p.tpx.nwait; ++s2) {
+            const float4 b = __ldcg(reinterpret_cast<const float4*>(rb + s2 * p.tpx.red_slot + k));
+            a.x += b.x; a.y += b.y; a.z += b.z; a.w += b.w;
+          }
         }
         const uint2 rr = *reinterpret_cast<const uint2*>(hr + k);
         const __half* h4 = reinterpret_cast<const __half*>(&rr);
@@ -619,8 +641,13 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
           const int c = cg * 8 + 2 * t + h;
           if (c < p.B && p.npush) {
             for (int q = 0; q < p.npush; ++q) {
-              p.y32p[q][(long)c * p.ldy + row_a] = r[cg][h];
-              p.y32p[q][(long)c * p.ldy + row_b] = r[cg][2 + h];
+              if (p.tpx.ll_sig) {
+                tp_push_word(p.y32p[q], (long)c * p.ldy + row_a, ll_tag, r[cg][h]);
+                tp_push_word(p.y32p[q], (long)c * p.ldy + row_b, ll_tag, r[cg][2 + h]);
+              } else {
+                p.y32p[q][(long)c * p.ldy + row_a] = r[cg][h];
+                p.y32p[q][(long)c * p.ldy + row_b] = r[cg][2 + h];
+              }
             }
           } else if (c < p.B) {
             float va = __half2float(__float2half(r[cg][h]));
@@ -675,7 +702,10 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
           for (int k2 = 0; k2 < cur.n; ++k2) v += __ldcg(p.part + ((long)k2 * p.B + col) * p.N + rr);
           if (p.npush) {
             if (lane < 16)
-              for (int q = 0; q < p.npush; ++q) p.y32p[q][(long)col * p.ldy + rr] = v;
+              for (int q = 0; q < p.npush; ++q) {
+                if (p.tpx.ll_sig) tp_push_word(p.y32p[q], (long)col * p.ldy + rr, ll_tag, v);
+                else p.y32p[q][(long)col * p.ldy + rr] = v;
+              }
             continue;
           }
           v = __half2float(__float2half(v));
@@ -696,7 +726,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
     if (stamp) tp_stamp(p.tpx, 6, p.tpx.sig_idx);
     consumer_sync();
     if (ctid == 0) tp_signal_cta(p.tpx);
-  } else if (p.npush > 1) {
+  } else if (p.npush > 1 && !p.tpx.ll_sig) {
     __threadfence_system();
   }
   if (ctid == 0) TRACE(0, 2);

@@ -32,10 +32,12 @@ struct TpExchange {
   unsigned* sig_done;                    // CTA-completion counter of this exchange (left zero)
   int nsig;                              // ranks to signal (0: no signal)
   int sig_idx;
+  int ll_sig;                            // pushes are tagged words (epoch << 32 | fp32): no fence, no flag
   // consumer side
   const unsigned long long* wait_flags;  // this rank's flags[world]
   int nwait;                             // ranks to wait for (0: not a TP consumer)
   int wait_idx;
+  int ll_wait;                           // the slots hold tagged words: poll them instead of the flags
   const float* red;                      // reduce slots of this parity: [world][red_slot]
   long red_slot;                         // floats per slot; row b of a slot at b * K
   const __half* red_res;                 // residual added to the reduced sum ([B][K])
@@ -63,6 +65,50 @@ __device__ __forceinline__ void tp_stamp(const TpExchange& x, int ev, int idx) {
 __device__ __forceinline__ unsigned long long tp_epoch(const TpExchange& x, int idx) {
   const unsigned long long c = *reinterpret_cast<const volatile unsigned long long*>(x.ep_ctr);
   return c * (unsigned long long)kTpExchangesPerStep + (unsigned long long)idx + 1ull;
+}
+
+// Tagged exchange words (ll_sig / ll_wait): each pushed element is one 64-bit
+// word, epoch << 32 | fp32 bits, stored with a single-copy-atomic 64-bit
+// store; the reader knows an element has arrived from its own tag, so the
+// producer needs neither a fence nor a flag (each system-scope fence or
+// release store cost ~5 us on B200).
+__device__ __forceinline__ unsigned long long tp_word(unsigned tag, float v) {
+  return ((unsigned long long)tag << 32) | (unsigned long long)__float_as_uint(v);
+}
+// element i of a tagged slot whose base is given as float* (the push table's type)
+__device__ __forceinline__ void tp_push_word(float* base, long i, unsigned tag, float v) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(reinterpret_cast<unsigned long long*>(base) + i),
+               "l"(tp_word(tag, v))
+               : "memory");
+}
+// Element i of a tagged slot (unsigned long long words), waited for until its
+// tag matches (bounded by ~2 s, then the rank's status bit and 0).
+__device__ __forceinline__ float tp_read_word(const TpExchange& x, const float* slot_base, long i, unsigned tag,
+                                              int src) {
+  const unsigned long long* a = reinterpret_cast<const unsigned long long*>(slot_base) + i;
+  unsigned long long w;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w) : "l"(a) : "memory");
+  if ((unsigned)(w >> 32) != tag) {
+    unsigned long long t0;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+    unsigned it = 0;
+    for (;;) {
+      if ((*reinterpret_cast<volatile const unsigned long long*>(x.status) >> src) & 1ull) break;
+      __nanosleep(32);
+      asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w) : "l"(a) : "memory");
+      if ((unsigned)(w >> 32) == tag) break;
+      if ((++it & 63) == 0) {
+        unsigned long long t;
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+        if (t - t0 > 2000000000ull) {
+          atomicOr(x.status, 1ull << src);
+          break;
+        }
+      }
+    }
+    if ((unsigned)(w >> 32) != tag) w = 0;
+  }
+  return __uint_as_float((unsigned)w);
 }
 
 // Lanes 0..nwait-1 of one warp each wait for one rank; bounded by ~2 s of
