@@ -339,7 +339,8 @@ int r4q_decode_profile(r4q_decode_ctx* ctx, const void* hidden_in, int pos, floa
  * variable R4Q_TP_TRACE set (synchronous; host array of 8 x 256 u64 global-timer
  * stamps in ns, per exchange index: producer compute start, producer signal,
  * consumer wait start, consumer wait end, consumer input staged, producer
- * entry, producer CTA 0 done, producer's last CTA arrived).  A profiling aid; R4Q_ERR_ARG when the context has no trace. */
+ * entry, producer CTA 0 done, producer's last CTA arrived; an exchange of
+ * tagged words has no signal, so its events 1, 6 and 7 stay 0).  A profiling aid; R4Q_ERR_ARG when the context has no trace. */
 int r4q_decode_tp_trace(r4q_decode_ctx* ctx, unsigned long long* host);
 
 /* ------------------------------------------- tensor-parallel exchange --- */

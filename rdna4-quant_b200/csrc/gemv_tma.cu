@@ -226,7 +226,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
   SegIter iter0{tp.tiles, tp.gt, cta_in_split, st0, st1, ks, S};
 
   if (tid == 0) TRACE(0, 0);
-  if (tid == 0 && blockIdx.x == 0 && p.tpx.nsig) tp_stamp(p.tpx, 5, p.tpx.sig_idx);
+  if (tid == 0 && blockIdx.x == 0 && (p.tpx.nsig || p.tpx.ll_sig)) tp_stamp(p.tpx, 5, p.tpx.sig_idx);
   if (tid == 0) {
     for (int i = 0; i < NS; ++i) {
       mbar_init(&full[i], 1);
@@ -277,7 +277,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
   const int colstride = tp.x_bytes / (ncolx > 0 ? ncolx : 1);
 
   const bool stamp = blockIdx.x == 0 && ctid == 0;
-  if (stamp && p.tpx.nsig) tp_stamp(p.tpx, 0, p.tpx.sig_idx);
+  if (stamp && (p.tpx.nsig || p.tpx.ll_sig)) tp_stamp(p.tpx, 0, p.tpx.sig_idx);
   // tag of this GEMV's pushed words (the step counter is read after the wait)
   const unsigned ll_tag = p.tpx.ll_sig ? (unsigned)tp_epoch(p.tpx, p.tpx.sig_idx) : 0u;
   // TP consumer with the whole K staged here and at most kTpPre staging items
