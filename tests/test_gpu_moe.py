@@ -28,15 +28,17 @@ def _lin4(w, s, e, N):
     return ('int4', _np(w[e * N:(e + 1) * N]), _np(s[e * N:(e + 1) * N]))
 
 
-@pytest.mark.parametrize("B,D", [(1, 256), (5, 256), (40, 256), (5, 4096)])
-def test_grouped_expert_gemv(B, D):
-    """D = 256: gate_up on the TMA-tile kernel, down (K = 128) on the
+@pytest.mark.parametrize("B,D,Ie", [(1, 256, 128), (5, 256, 128), (40, 256, 128), (5, 4096, 128),
+                                    (5, 256, 768), (6, 2048, 768)])
+def test_grouped_expert_gemv(B, D, Ie):
+    """D = 256: gate_up on the TMA-tile kernel, down (K = Ie = 128) on the
     register-staged one; D = 4096: gate_up (K = 4096, tile above 100 KB) on
-    the register-staged kernel too."""
+    the register-staged kernel too; Ie = 768 (config 4): down on the TMA-tile
+    kernel."""
     from r4q import ops, synth
     dev = torch.device('cuda')
-    g = torch.Generator(device=dev).manual_seed(B)
-    E, k, Ie = 16, 4, 128
+    g = torch.Generator(device=dev).manual_seed(B + Ie)
+    E, k = 16, 4
     wgu, sgu = synth.quantize_int4_asym(synth.weight_fp32(E * 2 * Ie, D, g, dev))
     wd, sd = synth.quantize_int4_asym(synth.weight_fp32(E * D, Ie, g, dev))
     logits = (torch.randn(B, E, generator=g, device=dev) * 2).half()
