@@ -28,17 +28,30 @@ def _require_cuda(*ts: torch.Tensor) -> torch.device:
     return dev
 
 
+# Workspaces replaced by larger ones stay referenced: a CUDA graph captured
+# earlier may still use them.
+_retired: list = []
+
+
+def _grown(cache: dict, key, need: int, minimum: int, dev) -> torch.Tensor:
+    """The cached zero-filled uint8 workspace for key, replaced by a larger one
+    when it holds fewer than `need` bytes (call with _ws_lock held)."""
+    cur = cache.get(key)
+    if cur is None or cur.numel() < need:
+        if cur is not None:
+            _retired.append(cur)
+        cur = torch.zeros(max(need, minimum), dtype=torch.uint8, device=dev)
+        cache[key] = cur
+    return cur
+
+
 def gemv_workspace(dev: torch.device, B: int, N: int, K: int) -> torch.Tensor:
     """Zero-filled workspace for GEMV split-K partials, cached per
     (device, stream).  The kernels leave it zeroed after every call."""
     need = int(L.LIB.r4q_gemv_workspace_bytes(B, N, K))
     key = (dev.index, stream_handle(dev))
     with _ws_lock:
-        cur = _ws.get(key)
-        if cur is None or cur.numel() < need:
-            cur = torch.zeros(max(need, 1 << 20), dtype=torch.uint8, device=dev)
-            _ws[key] = cur
-    return cur
+        return _grown(_ws, key, need, 1 << 20, dev)
 
 
 def _ptr(t: torch.Tensor | None) -> int | None:
@@ -156,11 +169,7 @@ def attn_workspace(dev: torch.device, B: int, H: int, Hk: int, max_seq: int) -> 
     need = int(L.LIB.r4q_flash_decode_workspace_bytes(B, H, Hk, max_seq))
     key = (dev.index, stream_handle(dev))
     with _ws_lock:
-        cur = _aws.get(key)
-        if cur is None or cur.numel() < need:
-            cur = torch.zeros(max(need, 1 << 16), dtype=torch.uint8, device=dev)
-            _aws[key] = cur
-    return cur
+        return _grown(_aws, key, need, 1 << 16, dev)
 
 
 def flash_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, seq_len: int,
@@ -206,11 +215,7 @@ def _status_ws(dev, nbytes: int = 256):
     Grow it outside graph capture (a warm-up call at the same shape)."""
     key = (dev.index, stream_handle(dev))
     with _ws_lock:
-        cur = _gws.get(key)
-        if cur is None or cur.numel() < nbytes:
-            cur = torch.zeros(max(256, nbytes), dtype=torch.uint8, device=dev)
-            _gws[key] = cur
-    return cur
+        return _grown(_gws, key, nbytes, 256, dev)
 
 
 def gemm(x: torch.Tensor, w: torch.Tensor, s: torch.Tensor | None = None, N: int | None = None,
