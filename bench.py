@@ -1,7 +1,7 @@
 #!/usr/bin/env python
 """Benchmark of the B200 decode hot path (rdna4-quant INT4/INT8 dequant-GEMV).
 
-Headline workload: the Qwen3-14B decode-layer INT4 GEMV
+Headline workload (benchmark config 1): the Qwen3-14B decode-layer INT4 GEMV
 set — qkv 5120->7168, o 5120->5120, gate_up 5120->34816, down 17408->5120 (the
 reference's fused runtime shapes, int4_engine_v5.py:136-162) — at batch 1, with
 the H32 FWHT (qkv/o/gate_up inputs) and SiLU*up+FWHT (down input) fused into
@@ -389,7 +389,7 @@ def main_reference(a):
 
 
 def decode_tok_s(a, dev, peak, ws=1, rank=0):
-    """40-layer Qwen3-14B-shaped decode (random-init,
+    """benchmark config 3: 40-layer Qwen3-14B-shaped decode (random-init,
     80 % INT4 / 20 % INT8 groups by seed, fp16 embedding + lm_head), KV cache
     pre-filled for `ctx` prompt positions, greedy decode of `tokens` tokens,
     each one CUDA-graph launch of step + device argmax + embedding lookup
@@ -521,7 +521,7 @@ def prefill_tok_s(a, dev, m, cfg):
 
 
 def moe_tok_s(a, dev, peak, ws=1, rank=0):
-    """48-layer Qwen3-30B-A3B-shaped MoE decode (random
+    """benchmark config 4: 48-layer Qwen3-30B-A3B-shaped MoE decode (random
     init, INT4 experts, top-8 of 128), KV cache of ctx 2048 filled with seeded
     FP8 values, batches from --moe-batches; each token one CUDA-graph replay
     of the whole step (routing on the device).  ws > 1: expert parallelism,

@@ -213,7 +213,7 @@ int r4q_kv_write_rows(const void* k, const void* v, long ld, void* k_cache, void
                       void* stream);
 
 /* ------------------------------------------------- mixture-of-experts FFN --- */
-/* No counterpart in the reference (its engine is dense); BASELINE config 4.
+/* No counterpart in the reference (its engine is dense); benchmark config 4.
  * Routing: per token softmax over router logits fp16 [B, E] (fp32), top-k
  * (ties to the lower expert), weights renormalised over the k -> ids int32
  * [B, topk], wts fp32 [B, topk]; entries t * topk + k grouped by expert in

@@ -606,7 +606,7 @@ def rmsnorm_unrounded(r, w, eps):
 
 
 # --------------------------------------------------------------------------
-# Mixture-of-experts FFN (no reference counterpart — the
+# Mixture-of-experts FFN (benchmark config 4; no reference counterpart — the
 # composition the B200 MoE kernels implement, built from the dense path's
 # pieces: routing softmax in fp32, top-k, renormalised weights; experts as
 # the dense gate_up / silu·up+FWHT / down chain; weighted sum, residual).

@@ -1,21 +1,27 @@
 // Tensor-parallel exchange over NVLink peer memory: the collective steps of the
 // TP decode (all-reduce after o_proj and down_proj, vocabulary gather after
-// lm_head).  The reference's TP is torch.distributed / RCCL all_reduce between
-// per-layer GEMVs (SURVEY configs 2-3; int4_engine_v5.py TP wrapper); here the
-// GEMV epilogues push fp32 partials into the peers' buffers and one small
-// kernel per exchange does signal + bounded wait + reduce + residual + sums of
-// squares, so an exchange costs one launch and one NVLink hop.
+// lm_head) and the standalone all-reduce of expert parallelism.  The
+// reference's TP is torch.distributed / RCCL all_reduce between per-layer
+// GEMVs (int4_engine_v5.py TP wrapper).  Here the producer GEMV's epilogue
+// pushes its fp32 partials into every rank's buffer and the consumer GEMV's
+// prologue reduces them (tp_exchange.cuh, gemv_tma.cu); this file owns the
+// buffers, the peer mappings, the step counter and the kernels for what the
+// GEMVs do not fuse: the reduce kernel for consumers that cannot read the
+// slots in their prologue, the vocabulary gather, the standalone all-reduce.
 //
-// Synchronisation.  flags[src] on every rank holds the last epoch rank src
-// signalled.  A sync kernel takes epoch e = seq + 1 (seq is this rank's local
-// count of completed sync kernels), block 0 publishes e to every peer with a
-// system-scope release store, and every block waits (acquire, bounded by time)
-// until flags[src] >= e for all src.  Monotone epochs make a late reader safe
+// Synchronisation.  Decode exchanges with a fused consumer carry tagged
+// 64-bit words (epoch << 32 | fp32 bits): a reader polls each word until its
+// tag is the exchange's epoch, so there is no fence and no flag.  The other
+// exchanges use flags: flags[src] on every rank holds the last epoch rank src
+// signalled, published with system-scope stores after a fence, and readers
+// wait (acquire, bounded by time) until flags[src] >= e for all src.  Epochs
+// only grow (static decode epochs: step counter * 256 + exchange index + 1;
+// the standalone all-reduce: completed calls + 1), so a late reader is safe
 // against a peer that has already moved on.  Buffers are double-buffered by
-// call parity; a slot is rewritten by a producer only after that producer has
-// passed the next sync, which needs every reader to have started it, i.e. to
-// have finished reading the slot.  Summation runs in rank order, so every rank
-// computes bit-identical replicated activations.
+// exchange parity; a slot is rewritten by a producer only after that producer
+// has consumed the next exchange, which needs every reader to have finished
+// reading the slot.  Summation runs in rank order, so every rank computes
+// bit-identical replicated activations.
 //
 // A wait that exceeds ~2 s records R4Q_ERR_TIMEOUT (with the missing ranks) in
 // a local status word (r4q_comm_status) and continues, so the context stays

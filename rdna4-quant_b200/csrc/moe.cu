@@ -1,4 +1,4 @@
-// Mixture-of-experts decode FFN (Qwen3-30B-A3B shape: 128
+// Mixture-of-experts decode FFN (benchmark config 4, Qwen3-30B-A3B shape: 128
 // experts, top-8 softmax routing, INT4 experts).  No counterpart in the
 // reference, whose engine is dense; the expert projections reuse the dense
 // path's conventions: INT4 runtime layout (nibbles [N, K/2], (scale, zero)

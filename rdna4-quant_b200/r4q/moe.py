@@ -1,4 +1,4 @@
-"""Mixture-of-experts decode (Qwen3-30B-A3B shape — 48
+"""Mixture-of-experts decode (benchmark config 4: Qwen3-30B-A3B shape — 48
 layers, hidden 2048, 32 query / 4 KV heads of 128, 128 experts with top-8
 softmax routing, expert intermediate 768, INT4 block-32 asymmetric experts).
 

@@ -94,7 +94,7 @@ def qwen3_14b_config(layers: int = 40) -> dict:
 def build_decode_model(cfg: dict, device, seed: int = 0, int8_frac: float = 0.2,
                        max_seq: int = 2304, batch: int = 1, lm_fp16: bool = True):
     """Random-init weights of a Qwen3-architecture decoder in the reference's
-    runtime layout: per layer the fused qkv / o / gate_up /
+    runtime layout (benchmark config 3): per layer the fused qkv / o / gate_up /
     down projections, ``int8_frac`` of the (layer, projection) groups INT8 and
     the rest INT4 (chosen by ``seed``), fp16 embedding and lm_head, FP8 KV caches
     [batch, Hk, max_seq, head_dim].  Returns the keyword arguments of

@@ -1,5 +1,5 @@
 """GPU parity of the split-K flash-decode attention over the FP8 cache
-(BASELINE config 2 shape: 40 query / 8 KV heads, head_dim 128; K/V ~ N(0,1)
+(benchmark config 2 shape: 40 query / 8 KV heads, head_dim 128; K/V ~ N(0,1)
 stored as E4M3 with a per-head fp32 scale; Q ~ N(0,1) fp16).  Reference: fp32
 softmax over the dequantised cache (oracle.attention_decode).  Tolerance 1e-3
 relative (max-norm and L2, as for the GEMV)."""

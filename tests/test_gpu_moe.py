@@ -1,4 +1,4 @@
-"""GPU: the mixture-of-experts decode step (BASELINE config 4 architecture at
+"""GPU: the mixture-of-experts decode step (benchmark config 4 architecture at
 a small size) against the oracle composition of the same pieces.
 
 Routing is a step function of the router logits: the device top-k must equal
