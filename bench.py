@@ -61,6 +61,8 @@ def parse():
     ap.add_argument("--moe-batches", default="1,16,64",
                     help="batches of the config-4 MoE decode measurement ('' skips it)")
     ap.add_argument("--moe-tokens", type=int, default=32)
+    ap.add_argument("--gemv-batches", default="4,16",
+                    help="extra batch sizes of the GEMV set (config 1 names B = 1, 4, 16); '' skips")
     ap.add_argument("--moe-probe", type=int, default=0,
                     help="ncu target: 3 eager MoE decode steps of a 2-layer config-4 model at this batch")
     ap.add_argument("--gemm-probe", action="store_true",
@@ -148,6 +150,51 @@ def build_layers(B, layers, device, seed=1234):
             L[name] = (w, s)
         out.append(L)
     return out
+
+
+def gemv_set_batches(a, dev, layers, peak, Lpro, ws):
+    """Config 1 at the other batch sizes it names: the same 40-layer GEMV set
+    (same weights) through a CUDA graph, B activation rows per GEMV; GB/s of
+    algorithmic bytes per GPU and the fraction of the measured copy peak."""
+    import torch
+    from r4q import ops
+    res = []
+    for B in [int(b) for b in a.gemv_batches.split(",") if b]:
+        g = torch.Generator(device=dev).manual_seed(7 + B)
+        x = torch.randn(B, HID, generator=g, device=dev).half()
+        att = torch.randn(B, NQ * HD, generator=g, device=dev).half()
+        qkv = torch.empty(B, QKV_N, device=dev, dtype=torch.float16)
+        o = torch.empty(B, HID, device=dev, dtype=torch.float16)
+        gu = torch.randn(B, 2 * INTER, generator=g, device=dev).half()
+        d = torch.empty(B, HID, device=dev, dtype=torch.float16)
+        bufs = (x, qkv, att, o, gu, d)
+        s = torch.cuda.Stream(dev)
+        with torch.cuda.stream(s):
+            for _ in range(2):
+                run_set(ops, Lpro, layers, bufs)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=s):
+            run_set(ops, Lpro, layers, bufs)
+        with torch.cuda.stream(s):
+            for _ in range(3):
+                graph.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = 5
+        with torch.cuda.stream(s):
+            e0.record(s)
+            for _ in range(reps):
+                graph.replay()
+            e1.record(s)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / reps
+        gbs = step_bytes(B, a.layers) / (ms * 1e-3) / 1e9
+        res.append({"batch": B, "GBps_per_gpu": round(gbs, 1), "ms_per_step": round(ms, 4),
+                    "frac": round(gbs / peak, 4)})
+        del graph
+    return {"workload": f"cfg1 GEMV set x{a.layers} layers (same weights as the headline)",
+            "gpus": ws, "parallelism": f"replicas x{ws}", "results": res}
 
 
 def run_set(ops, Lpro, layers, bufs):
@@ -334,6 +381,8 @@ def main_ours(a):
         "gpu_launches": nlaunch * a.steps,
         "clocks": clk.summary(),
     }
+    if a.gemv_batches:
+        line["gemv_batches"] = gemv_set_batches(a, dev, layers, peak, Lpro, ws)
     if a.decode_ctx:
         del layers
         torch.cuda.empty_cache()
