@@ -457,7 +457,15 @@ int launch_gemv(const GemvArgs& a, int fmt) {
     const char* e = getenv("R4Q_GEMV_PATH");
     return (e && e[0] == 'l') ? 1 : 0;
   }();
-  if (!force_ldg && gemv_tma_supported(a, fmt)) {
+  // Measured on B200 (INT4, graph replay): above 8 columns the TMA kernel's
+  // two-n-group instance spills (qkv 5120->7168 at B = 16: 75 us against 40
+  // us here), and a wide-K GEMV at B >= 8 must split its staged activations
+  // (down 17408->5120 at B = 8: 75 us against 42 us); wide-N shapes stay on
+  // TMA (gate_up at B = 16: 155 against 175 us).  Plain GEMVs only: the
+  // tensor-parallel exchanges keep the TMA kernel.
+  const bool ldg_better = fmt == W_INT4 && !a.tpx.nwait && !a.tpx.nsig && !a.tpx.ll_sig && !a.npush &&
+                          ((a.B > 8 && a.N <= 8192) || (a.B >= 8 && a.K > 8192));
+  if (!force_ldg && !ldg_better && gemv_tma_supported(a, fmt)) {
     st = launch_gemv_tma(a, fmt);
     if (st != R4Q_ERR_CAPACITY) return st;  // no TMA plan fits: take the LDG kernel
   }
