@@ -63,3 +63,24 @@ def test_misaligned_rejected(lib):
     p = ctypes.c_void_p(18)
     q = ctypes.c_void_p(32)
     assert lib.LIB.r4q_gemv_int4(p, 64, q, q, q, 64, 1, 64, 64, 0, None, 0, None) == -2
+
+
+def prototypes():
+    """name -> parameter count of every r4q_* prototype in include/*.h."""
+    out = {}
+    for h in (ROOT / "include").glob("*.h"):
+        text = re.sub(r"/\*.*?\*/", " ", h.read_text(), flags=re.S)
+        for m in re.finditer(r"\b(r4q_\w+)\s*\(([^;{]*?)\)\s*;", text):
+            params = m.group(2).strip()
+            out[m.group(1)] = 0 if params in ("", "void") else params.count(",") + 1
+    return out
+
+
+def test_ctypes_signatures_match_the_header(lib):
+    """Every ctypes binding in r4q/lib.py has as many arguments as the C
+    prototype: a parameter added on one side only is caught here."""
+    protos = prototypes()
+    assert len(protos) >= 20
+    for name, (_res, args) in lib._SIGS.items():
+        assert name in protos, f"{name} bound in r4q/lib.py but not declared in include/"
+        assert len(args) == protos[name], f"{name}: {len(args)} ctypes args, {protos[name]} in the header"
