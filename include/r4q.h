@@ -66,6 +66,20 @@ typedef struct r4q_gemv_fused {
                              [B, ldy] (y, residual and ss_out are then unused) */
 } r4q_gemv_fused;
 
+/* Status of the bounded device-side waits of the kernels that used the GEMV,
+ * GEMM or attention workspace `ws` (NULL: the static scratch of
+ * r4q_gemv_int4_noalloc on the current device).  Synchronises `stream`, then
+ * returns R4Q_ERR_TIMEOUT if a wait gave up since the word was last cleared
+ * (those kernels' outputs are not valid), else R4Q_OK; clear != 0 resets the
+ * word after a timeout.  The reference has no bounded waits and no status. */
+int r4q_ws_status(const void* ws, int clear, void* stream);
+
+/* Test hook: polls before a bounded mbarrier wait of the GEMV kernels gives
+ * up (default 2^26); polls <= 0 restores the default.  Returns the previous
+ * limit.  Lowering it makes waits time out so that the error path (status
+ * word, drain, R4Q_ERR_TIMEOUT) can be exercised without a hung kernel. */
+long r4q_debug_spin_limit(long polls);
+
 /* Message of the last failing call on this host thread ("" if none). */
 const char* r4q_last_error(void);
 /* Library version (major*10000 + minor*100 + patch). */
@@ -109,7 +123,8 @@ int r4q_gemv(int wfmt, const void* x, long ldx, const void* w, const void* s, vo
  * allocate, or a plugin whose host process owns all device memory).  No
  * counterpart in the reference.  Its split-K scratch is a fixed 4.06 MiB
  * static device array held by every GPU that loads the library; calls with
- * B * N > 524288 are rejected with R4Q_ERR_CAPACITY.  The first call on a
+ * B * N > 524288 are rejected with R4Q_ERR_CAPACITY.  A timed-out wait is
+ * reported by r4q_ws_status(NULL, ...).  The first call on a
  * device looks up the array's device address (cudaGetSymbolAddress), so make
  * it before any stream capture.  Every call clears the scratch's counters on
  * `stream`; all calls on one device share the array, so calls that overlap on
@@ -342,6 +357,11 @@ int r4q_decode_profile(r4q_decode_ctx* ctx, const void* hidden_in, int pos, floa
  * entry, producer CTA 0 done, producer's last CTA arrived; an exchange of
  * tagged words has no signal, so its events 1, 6 and 7 stay 0).  A profiling aid; R4Q_ERR_ARG when the context has no trace. */
 int r4q_decode_tp_trace(r4q_decode_ctx* ctx, unsigned long long* host);
+
+/* Timeout status of the context's GEMV and attention kernels (synchronises the
+ * device's legacy stream; see r4q_ws_status): R4Q_ERR_TIMEOUT if a bounded
+ * wait gave up since the last clear, else R4Q_OK. */
+int r4q_decode_status(r4q_decode_ctx* ctx, int clear);
 
 /* ------------------------------------------- tensor-parallel exchange --- */
 /* One comm per rank, one process per GPU.  It replaces the torch.distributed

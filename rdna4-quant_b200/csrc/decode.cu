@@ -681,3 +681,18 @@ extern "C" int r4q_decode_tp_trace(r4q_decode_ctx* c, unsigned long long* host) 
   cudaError_t e = cudaMemcpy(host, c->tp_trace, 8 * kTpExchangesPerStep * 8, cudaMemcpyDeviceToHost);
   return e == cudaSuccess ? R4Q_OK : set_error(R4Q_ERR_CUDA, "decode_tp_trace: %s", cudaGetErrorString(e));
 }
+
+// Timeouts of the context's GEMVs and attention kernels (their workspaces'
+// status words).  Synchronous on the context's device.
+extern "C" int r4q_decode_status(r4q_decode_ctx* c, int clear) {
+  if (!c) return set_error(R4Q_ERR_ARG, "decode_status: null context");
+  int cur = 0;
+  cudaGetDevice(&cur);
+  cudaSetDevice(c->dev);
+  cudaError_t e = cudaDeviceSynchronize();
+  int st = e == cudaSuccess ? R4Q_OK : set_error(R4Q_ERR_CUDA, "decode_status: %s", cudaGetErrorString(e));
+  if (!st) st = r4q_ws_status(c->gemv_ws, clear, nullptr);
+  const int st2 = (st == R4Q_ERR_CUDA) ? st : r4q_ws_status(c->attn_ws, clear, nullptr);
+  cudaSetDevice(cur);
+  return st ? st : st2;
+}

@@ -404,7 +404,7 @@ static int launch_gemv_t(const GemvArgs& a) {
   p.npush = a.npush;
   for (int q = 0; q < 8; ++q) p.y32p[q] = q < a.npush ? a.y32p[q] : nullptr;
   p.tpx = a.tpx;
-  p.cnt = reinterpret_cast<unsigned*>(a.ws);
+  p.cnt = gemv_counters(a.ws);
   p.part = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(a.ws) + gemv_cnt_bytes(a.N));
   if (pl.ksplit > 1 && a.ws == nullptr)
     return set_error(R4Q_ERR_CAPACITY, "gemv: workspace required for N=%d K=%d", a.N, a.K);
@@ -413,10 +413,16 @@ static int launch_gemv_t(const GemvArgs& a) {
   return check_launch("gemv_kernel");
 }
 
-// The counter region has a fixed size so that it never overlaps the partials
-// of a call with a different N (partials are left behind, counters are not).
+// Workspace layout: a 256-byte header whose first int is the status word (set
+// to 1 by a kernel whose bounded wait gave up; read by r4q_ws_status), then
+// the tile counters, then the fp32 split-K partials.  The counter region has
+// a fixed size so that it never overlaps the partials of a call with a
+// different N (partials are left behind, counters are not).
 constexpr int kMaxTiles16 = 16384;
-size_t gemv_cnt_bytes(int N) { (void)N; return (size_t)kMaxTiles16 * 4; }
+size_t gemv_cnt_bytes(int N) { (void)N; return kGemvHdrBytes + (size_t)kMaxTiles16 * 4; }
+unsigned* gemv_counters(void* ws) {
+  return ws ? reinterpret_cast<unsigned*>(reinterpret_cast<uint8_t*>(ws) + kGemvHdrBytes) : nullptr;
+}
 size_t gemv_ws_bytes_for(int B, int N, int ksplit) {
   return gemv_cnt_bytes(N) + (size_t)ksplit * B * N * sizeof(float);
 }
@@ -461,9 +467,11 @@ int launch_gemv(const GemvArgs& a, int fmt) {
   // two-n-group instance spills (qkv 5120->7168 at B = 16: 75 us against 40
   // us here), and a wide-K GEMV at B >= 8 must split its staged activations
   // (down 17408->5120 at B = 8: 75 us against 42 us); wide-N shapes stay on
-  // TMA (gate_up at B = 16: 155 against 175 us).  Plain GEMVs only: the
-  // tensor-parallel exchanges keep the TMA kernel.
-  const bool ldg_better = fmt == W_INT4 && !a.tpx.nwait && !a.tpx.nsig && !a.tpx.ll_sig && !a.npush &&
+  // TMA (gate_up at B = 16: 155 against 175 us).  The choice depends on the
+  // shape only, never on the output type (fp16 or fp32 partials), so that
+  // fp16(y32) == y16 holds bit for bit; only a tensor-parallel consumer
+  // (reduce-on-read prologue) needs the TMA kernel.
+  const bool ldg_better = fmt == W_INT4 && !a.tpx.nwait &&
                           ((a.B > 8 && a.N <= 8192) || (a.B >= 8 && a.K > 8192));
   if (!force_ldg && !ldg_better && gemv_tma_supported(a, fmt)) {
     st = launch_gemv_tma(a, fmt);

@@ -36,7 +36,16 @@ struct GemvArgs {
   TpExchange tpx;
 };
 
-size_t gemv_cnt_bytes(int N);
+// GEMV workspace: status word in a 256-byte header, tile counters, partials.
+constexpr size_t kGemvHdrBytes = 256;
+size_t gemv_cnt_bytes(int N);  // offset of the partials (header + counters)
+unsigned* gemv_counters(void* ws);
+// Polls before a bounded mbarrier wait of the TMA GEMV gives up (test hook:
+// gemv_set_spin_limit lowers it; <= 0 restores the default).  Returns the old value.
+long gemv_spin_limit();
+long gemv_set_spin_limit(long polls);
+// Device address of r4q_gemv_int4_noalloc's static scratch on the current device.
+int noalloc_scratch(void** out);
 size_t gemv_ws_bytes_for(int B, int N, int ksplit);
 int gemv_validate(const GemvArgs& a, int fmt);
 int launch_gemv(const GemvArgs& a, int fmt);

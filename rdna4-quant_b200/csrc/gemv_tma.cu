@@ -23,6 +23,7 @@
 //    outputs (activations, sums of squares, residual) comes after it.
 #include <cuda.h>
 
+#include <atomic>
 #include <cstdlib>
 #include <mutex>
 #include <unordered_map>
@@ -80,6 +81,7 @@ struct TmaParams {
   int xsum_bytes;  // per-block activation sums (block-diagonal path)
   int ns;          // ring depth (stages), sized to the shared memory left
   int* status;     // set to 1 when a bounded wait gives up
+  long spin;       // polls before a wait gives up (kSpinLimit unless lowered for a test)
 };
 
 // ------------------------------------------------------------ mbarrier ---
@@ -107,13 +109,29 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* b, unsigned parity) {
       : "memory");
   return ok != 0;
 }
-// Bounded wait: gives up after kSpinLimit polls, records the failure and
+// Bounded wait: gives up after `limit` polls, records the failure and
 // returns false so the kernel can drain and exit instead of hanging.
-__device__ __forceinline__ bool mbar_wait(uint64_t* b, unsigned parity, int* status) {
-  for (long i = 0; i < kSpinLimit; ++i)
+__device__ __forceinline__ bool mbar_wait(uint64_t* b, unsigned parity, int* status, long limit) {
+  for (long i = 0; i < limit; ++i)
     if (mbar_try_wait(b, parity)) return true;
   if (status) atomicExch(status, 1);
   return false;
+}
+
+// Drain wait (producer lane at exit): try_wait lets the hardware suspend the
+// lane between polls, so it takes no issue slots from the consumers.
+__device__ __forceinline__ void mbar_drain(uint64_t* b, unsigned parity, int* status) {
+  for (long i = 0; i < kSpinLimit; ++i) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+        " selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(b)), "r"(parity)
+        : "memory");
+    if (ok) return;
+  }
+  if (status) atomicExch(status, 1);
 }
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y,
@@ -250,7 +268,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
         for (int st = sg.sb; st < sg.se && ok; ++st, ++it) {
           const int slot = it % NS;
           const unsigned ph = (unsigned)(it / NS) & 1u;
-          if (it >= NS) ok = mbar_wait(&empty[slot], ph ^ 1u, tp.status);
+          if (it >= NS) ok = mbar_wait(&empty[slot], ph ^ 1u, tp.status, tp.spin);
           if (!ok) break;
           TRACE(1, it);
           const bool load_s = T::SBYTES && DBG_MODE != 3;
@@ -263,8 +281,17 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
             tma_load_2d(ring_s + slot * S_STAGE, &tms, st * T::SBYTES, tile * kTileRows, &full[slot]);
         }
       }
+      asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+      // Drain: the CTA must not exit while a copy into its shared memory is in
+      // flight.  Consumers that gave up on a wait stop releasing slots (so no
+      // slot is ever refilled before its previous copy landed); here the last
+      // copy issued into each slot is awaited.  Copies complete on their own
+      // within microseconds, so this wait keeps the full limit.
+      for (int j = (it > NS ? it - NS : 0); j < it; ++j)
+        mbar_drain(&full[j % NS], (unsigned)(j / NS) & 1u, tp.status);
+    } else {
+      asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     }
-    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     return;
   }
 
@@ -491,7 +518,9 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
         for (int i = 0; i < 4; ++i) acc[cg][h][i] = 0.0f;
 
     for (int st = cur.sb - st0; st < cur.se - st0; ++st) {  // st: stage index inside the staged x
-      if (ok) ok = mbar_wait(&full[slot], phase, tp.status);
+      // warp-uniform: after a timeout the warp no longer waits and no longer
+      // releases slots (the producer then stops refilling them and drains)
+      if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&full[slot], phase, tp.status, tp.spin));
       const uint32_t wst = ring_w_u + slot * W_STAGE;
       const uint32_t sst = ring_s_u + slot * S_STAGE;
       uint64_t* emp = &empty[slot];
@@ -501,7 +530,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
       }
       if (DBG_MODE == 1) {
         __syncwarp();
-        if (lane == 0) mbar_arrive(emp);
+        if (lane == 0 && ok) mbar_arrive(emp);
         continue;
       }
       if constexpr (DIAG) {
@@ -515,7 +544,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
           szb[v] = lds32(sst + soffB[v]);
         }
         __syncwarp();
-        if (lane == 0) mbar_arrive(emp);
+        if (lane == 0 && ok) mbar_arrive(emp);
         const uint32_t xst = xbase + st * xstep;
 #pragma unroll
         for (int v = 0; v < V; ++v) {
@@ -570,7 +599,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
         }
         // the slot is free once its bytes are in registers; the MMAs follow
         __syncwarp();
-        if (lane == 0) mbar_arrive(emp);
+        if (lane == 0 && ok) mbar_arrive(emp);
 #pragma unroll
         for (int v = 0; v < V; ++v) {
           const int off = (st * T::CPS + cidx[v]) * 16;
@@ -733,6 +762,12 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
 }
 
 // --------------------------------------------------------------- host ----
+static std::atomic<long> g_spin_limit{kSpinLimit};
+long gemv_spin_limit() { return g_spin_limit.load(std::memory_order_relaxed); }
+long gemv_set_spin_limit(long polls) {
+  return g_spin_limit.exchange(polls > 0 ? polls : kSpinLimit);
+}
+
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
@@ -888,7 +923,7 @@ static int launch_tma_t(const GemvArgs& a) {
   p.npush = a.npush;
   for (int q = 0; q < 8; ++q) p.y32p[q] = q < a.npush ? a.y32p[q] : nullptr;
   p.tpx = a.tpx;
-  p.cnt = reinterpret_cast<unsigned*>(a.ws);
+  p.cnt = gemv_counters(a.ws);
   p.part = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(a.ws) + gemv_cnt_bytes(a.N));
   tp.nstages = (a.K + T::SK - 1) / T::SK;
   tp.tiles = (a.N + kTileRows - 1) / kTileRows;
@@ -896,7 +931,8 @@ static int launch_tma_t(const GemvArgs& a) {
   tp.x_bytes = pl.x_bytes;
   tp.xsum_bytes = pl.xsum_bytes;
   tp.ns = pl.ns;
-  tp.status = a.ws ? reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(a.ws) + gemv_cnt_bytes(a.N) - 4) : nullptr;
+  tp.spin = gemv_spin_limit();
+  tp.status = reinterpret_cast<int*>(a.ws);   // header word 0 (null without a workspace)
 
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(pl.S * pl.gt);

@@ -14,9 +14,10 @@
 
 namespace r4q {
 
-// Scratch: 64 KiB of tile counters (+ the status word) followed by fp32 split-K
-// partials.  Every GPU that loads the library holds this array until exit.
-constexpr size_t kNoAllocCounterBytes = 64 * 1024;
+// Scratch: the GEMV workspace layout — a 256-byte header (status word), 64 KiB
+// of tile counters, then fp32 split-K partials.  Every GPU that loads the
+// library holds this array until exit.
+constexpr size_t kNoAllocCounterBytes = kGemvHdrBytes + 64 * 1024;
 constexpr size_t kNoAllocPartialBytes = 4 * 1024 * 1024;
 constexpr size_t kNoAllocBytes = kNoAllocCounterBytes + kNoAllocPartialBytes;
 // Largest B * N accepted: a two-way K split of one call must fit the partials.
@@ -27,7 +28,7 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocBytes];
 // Device address of the scratch on the current device.  Host code may not use
 // the symbol g_noalloc_scratch as a pointer (it names a host-side shadow), so
 // the address is looked up once per device with that device current.
-static int scratch_address(void** out) {
+int noalloc_scratch(void** out) {
   static std::mutex mu;
   static void* addr[64] = {};
   int dev = 0;
@@ -60,11 +61,14 @@ extern "C" int r4q_gemv_int4_noalloc(const void* x, long ldx, const void* w, con
                      "gemv_int4_noalloc: B*N = %ld exceeds the static scratch limit %ld "
                      "(use r4q_gemv_int4 with a workspace)", (long)B * N, kNoAllocMaxBN);
   void* ws = nullptr;
-  int st = scratch_address(&ws);
+  int st = noalloc_scratch(&ws);
   if (st) return st;
-  // Calls share the array and it keeps the previous call's contents: the
-  // counters (and status word) must start at zero, so clear them on the stream.
-  cudaError_t e = cudaMemsetAsync(ws, 0, kNoAllocCounterBytes, reinterpret_cast<cudaStream_t>(stream));
+  // Calls share the array and it keeps the previous call's contents: the tile
+  // counters must start at zero, so clear them on the stream.  The status word
+  // is left alone: a timeout stays recorded until r4q_ws_status(NULL, 1, ...)
+  // reads and clears it.
+  cudaError_t e = cudaMemsetAsync(static_cast<unsigned char*>(ws) + kGemvHdrBytes, 0,
+                                  kNoAllocCounterBytes - kGemvHdrBytes, reinterpret_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) {
     cudaGetLastError();
     return set_error(R4Q_ERR_CUDA, "gemv_int4_noalloc: clearing scratch: %s", cudaGetErrorString(e));

@@ -58,6 +58,11 @@ class DecodeContext:
                ops.stream_handle(hidden_in.device))
         return [float(v) for v in out]
 
+    def status(self, clear: bool = True) -> None:
+        """Raise ``R4QError`` (R4Q_ERR_TIMEOUT) if a bounded wait of one of this
+        context's kernels gave up since the last check (synchronises)."""
+        L.call("r4q_decode_status", self.handle, 1 if clear else 0)
+
     def __del__(self):
         try:
             if getattr(self, "handle", None):

@@ -65,6 +65,9 @@ class ModelDesc(C.Structure):
 _SIGS = {
     "r4q_last_error": (C.c_char_p, []),
     "r4q_version": (i32, []),
+    "r4q_ws_status": (i32, [vp, i32, vp]),
+    "r4q_debug_spin_limit": (i64, [i64]),
+    "r4q_decode_status": (i32, [vp, i32]),
     "r4q_gemv_workspace_bytes": (sz_t, [i32, i32, i32]),
     "r4q_gemv_int4": (i32, [vp, i64, vp, vp, vp, i64, i32, i32, i32, i32, vp, sz_t, vp]),
     "r4q_gemv_int8": (i32, [vp, i64, vp, vp, vp, i64, i32, i32, i32, i32, vp, sz_t, vp]),

@@ -54,6 +54,30 @@ def gemv_workspace(dev: torch.device, B: int, N: int, K: int) -> torch.Tensor:
         return _grown(_ws, key, need, 1 << 20, dev)
 
 
+def check_status(dev: torch.device | int | None = None, clear: bool = True) -> None:
+    """Raise ``R4QError`` (code R4Q_ERR_TIMEOUT) if a bounded device-side wait
+    of a GEMV, GEMM or attention kernel gave up since the last check on this
+    device: the outputs of those kernels are then not valid.  Reads the status
+    word of every workspace these wrappers hold for the device, and of the
+    allocation-free GEMV's static scratch (synchronises each stream)."""
+    if dev is None:
+        dev = torch.cuda.current_device()
+    idx = dev if isinstance(dev, int) else (dev.index if dev.index is not None else torch.cuda.current_device())
+    with _ws_lock:
+        items = [(k, t) for cache in (_ws, _gws, _aws) for k, t in cache.items() if k[0] == idx]
+    err = None
+    with torch.cuda.device(idx):
+        for (_, stream), t in items:
+            st = L.LIB.r4q_ws_status(t.data_ptr(), 1 if clear else 0, stream)
+            if st != 0 and err is None:
+                err = L.R4QError(st, "r4q_ws_status", L.last_error())
+        st = L.LIB.r4q_ws_status(None, 1 if clear else 0, None)
+        if st != 0 and err is None:
+            err = L.R4QError(st, "r4q_ws_status(noalloc scratch)", L.last_error())
+    if err is not None:
+        raise err
+
+
 def _ptr(t: torch.Tensor | None) -> int | None:
     return None if t is None else t.data_ptr()
 

@@ -124,8 +124,39 @@ def test_gemv_workspace_left_zero_and_repeatable(ops):
     torch.cuda.synchronize()
     assert torch.equal(y1, y2)              # deterministic split-K merge
     ws = ops.gemv_workspace(x.device, 1, N, K)
-    cnt_bytes = 16384 * 4
-    assert int(ws[:cnt_bytes].count_nonzero()) == 0
+    hdr_and_cnt = 256 + 16384 * 4           # status header + tile counters
+    assert int(ws[:hdr_and_cnt].count_nonzero()) == 0
+    ops.check_status(x.device)              # no wait gave up
+
+
+def test_gemv_timeout_is_reported_and_context_survives(ops):
+    """A bounded mbarrier wait that runs out (the poll limit lowered to a few
+    polls, so the TMA stages cannot land in time) must not hang or fault: the
+    kernel records the timeout in the workspace status word, drains its
+    in-flight copies and exits; check_status raises R4Q_ERR_TIMEOUT; the next
+    call with the normal limit is correct again."""
+    from r4q import lib as L
+    rng = np.random.default_rng(11)
+    N, K = 7168, 5120                       # TMA path, several stages per CTA
+    packed, sz = make_int4(rng, N, K)
+    x = cuda(rng.standard_normal((1, K)).astype(np.float16))
+    w, s = cuda(packed), cuda(sz)
+    ref = O.gemv_int4(x.cpu().numpy(), packed, sz)
+    ops.check_status(x.device)
+    old = L.LIB.r4q_debug_spin_limit(2)
+    try:
+        ops.gemv('int4', x, w, s, N, K)
+        torch.cuda.synchronize()
+    finally:
+        L.LIB.r4q_debug_spin_limit(0)
+    with pytest.raises(L.R4QError) as ei:
+        ops.check_status(x.device)
+    assert ei.value.code == -5 and "gave up" in str(ei.value)
+    ops.check_status(x.device)              # cleared by the previous check
+    y = ops.gemv('int4', x, w, s, N, K).cpu().numpy()
+    close(y, ref)
+    ops.check_status(x.device)
+    assert old > 1000
 
 
 def test_dequant_bit_exact(ops):
