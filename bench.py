@@ -5,13 +5,21 @@ Headline workload (benchmark config 1): the Qwen3-14B decode-layer INT4 GEMV
 set — qkv 5120->7168, o 5120->5120, gate_up 5120->34816, down 17408->5120 (the
 reference's fused runtime shapes, int4_engine_v5.py:136-162) — at batch 1, with
 the H32 FWHT (qkv/o/gate_up inputs) and SiLU*up+FWHT (down input) fused into
-the GEMV prologue.  One step runs that set over 40 distinct layers (8.3 GB of
-weights, far above the 126 MB L2, so every step streams from HBM).
+the GEMV prologue and the residual-add + RMSNorm (eps 1e-6) fused as in the
+decode step (residual epilogue of o/down writing per-tile sums of squares,
+RMSNorm+FWHT prologue of qkv/gate_up consuming them).  One step runs that set
+over 40 distinct layers (8.3 GB of weights, far above the 126 MB L2, so every
+step streams from HBM).  The same JSON line carries config 0 (the single
+5120x5120 GEMV), a per-shape roofline table at B = 1/4/16, config 2 (attention
+grid), config 3 (decode tok/s, tensor-parallel over N GPUs under torchrun) and
+config 4 (MoE decode), and CPU baselines of the reference's PyTorch math.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-N > 1 runs under torchrun as independent replicas (the GEMV set does not
-shard; no collective), value = bytes of all ranks / max-over-ranks time.
+N > 1 runs under torchrun: the GEMV set as independent replicas (it does not
+shard; no collective), value = bytes of all ranks / max-over-ranks time; the
+decode section is tensor-parallel over the N ranks (fused NVLink exchange, and
+an NCCL all-reduce arm for comparison).
 """
 from __future__ import annotations
 
@@ -37,9 +45,11 @@ LAYER_SHAPES = [  # (name, N, K, prologue)
     ("down", HID, INTER, "silu_fwht"),
 ]
 METRIC = "INT4 GEMV HBM GB/s (Qwen3-14B decode-layer GEMV set)"
-# dram__bytes_read.sum + dram__bytes_write.sum of one gate_up launch at B=1,
-# from the ncu capture summarised in profiles/gemv_tma_int4_gate_up_b1.md
-TRAFFIC_GATE_UP_B1 = 111478016 + 4093696
+# dram__bytes_read.sum + dram__bytes_write.sum of one gate_up launch at B=1
+# (gemv_unit_kernel), from the ncu capture summarised in
+# profiles/gemv_unit_int4_gate_up_b1.md; None until captured
+TRAFFIC_GATE_UP_B1 = None
+L2_BYTES = 126 * 1024 * 1024
 
 
 def parse():
@@ -61,6 +71,10 @@ def parse():
     ap.add_argument("--moe-batches", default="1,16,64",
                     help="batches of the config-4 MoE decode measurement ('' skips it)")
     ap.add_argument("--moe-tokens", type=int, default=32)
+    ap.add_argument("--no-extra", action="store_true",
+                    help="headline only: skip cfg0, the shape table, attention, decode and MoE")
+    ap.add_argument("--attn-grid", default="1,4,16:128,2048,32768",
+                    help="config 2 grid 'batches:contexts' ('' to skip)")
     ap.add_argument("--gemv-batches", default="4,16",
                     help="extra batch sizes of the GEMV set (config 1 names B = 1, 4, 16); '' skips")
     ap.add_argument("--moe-probe", type=int, default=0,
@@ -160,14 +174,7 @@ def gemv_set_batches(a, dev, layers, peak, Lpro, ws):
     from r4q import ops
     res = []
     for B in [int(b) for b in a.gemv_batches.split(",") if b]:
-        g = torch.Generator(device=dev).manual_seed(7 + B)
-        x = torch.randn(B, HID, generator=g, device=dev).half()
-        att = torch.randn(B, NQ * HD, generator=g, device=dev).half()
-        qkv = torch.empty(B, QKV_N, device=dev, dtype=torch.float16)
-        o = torch.empty(B, HID, device=dev, dtype=torch.float16)
-        gu = torch.randn(B, 2 * INTER, generator=g, device=dev).half()
-        d = torch.empty(B, HID, device=dev, dtype=torch.float16)
-        bufs = (x, qkv, att, o, gu, d)
+        bufs = SetBufs(B, dev, 7 + B)
         s = torch.cuda.Stream(dev)
         with torch.cuda.stream(s):
             for _ in range(2):
@@ -197,56 +204,253 @@ def gemv_set_batches(a, dev, layers, peak, Lpro, ws):
             "gpus": ws, "parallelism": f"replicas x{ws}", "results": res}
 
 
-def run_set(ops, Lpro, layers, bufs):
-    """Launch the GEMV set of every layer once (no host sync)."""
-    x, qkv, att, o, gu, d = bufs
+class SetBufs:
+    """Activations of the config-1 GEMV set: residual stream h [B, hidden],
+    attention output att, qkv and gate_up outputs, the per-16-row sums of
+    squares written by the residual epilogues (ss_post after o_proj, ss_h
+    after down_proj) and the two RMSNorm weights (~1 + N(0, 0.01))."""
+
+    def __init__(self, B, dev, seed):
+        import torch
+        g = torch.Generator(device=dev).manual_seed(seed)
+        self.h = torch.randn(B, HID, generator=g, device=dev).half()
+        self.att = torch.randn(B, NQ * HD, generator=g, device=dev).half()
+        self.qkv = torch.empty(B, QKV_N, device=dev, dtype=torch.float16)
+        self.gu = torch.randn(B, 2 * INTER, generator=g, device=dev).half()
+        self.ss_post = torch.full((HID // 16, B), 16.0, device=dev)
+        self.ss_h = torch.full((HID // 16, B), 16.0, device=dev)
+        self.in_norm = (1 + 0.01 * torch.randn(HID, generator=g, device=dev)).half()
+        self.post_norm = (1 + 0.01 * torch.randn(HID, generator=g, device=dev)).half()
+
+
+def run_set(ops, Lpro, layers, b):
+    """Launch the config-1 GEMV set of every layer once (no host sync):
+    qkv (RMSNorm+FWHT prologue from ss_h), o (FWHT; residual epilogue into h,
+    ss_post), gate_up (RMSNorm+FWHT from ss_post), down (SiLU*up+FWHT;
+    residual epilogue into h, ss_h) — the decode layer's GEMV chain."""
     for L in layers:
-        ops.gemv("int4", x, *L["qkv"], QKV_N, HID, prologue=Lpro["fwht"], out=qkv)
-        ops.gemv("int4", att, *L["o"], HID, NQ * HD, prologue=Lpro["fwht"], out=o)
-        ops.gemv("int4", x, *L["gate_up"], 2 * INTER, HID, prologue=Lpro["fwht"], out=gu)
-        ops.gemv("int4", gu, *L["down"], HID, INTER, prologue=Lpro["silu_fwht"], out=d)
+        ops.gemv("int4", b.h, *L["qkv"], QKV_N, HID, prologue=Lpro["rmsnorm_fwht"], out=b.qkv,
+                 norm_w=b.in_norm, eps=1e-6, ss_in=b.ss_h)
+        ops.gemv("int4", b.att, *L["o"], HID, NQ * HD, prologue=Lpro["fwht"], out=b.h, residual=b.h,
+                 ss_out=b.ss_post)
+        ops.gemv("int4", b.h, *L["gate_up"], 2 * INTER, HID, prologue=Lpro["rmsnorm_fwht"], out=b.gu,
+                 norm_w=b.post_norm, eps=1e-6, ss_in=b.ss_post)
+        ops.gemv("int4", b.gu, *L["down"], HID, INTER, prologue=Lpro["silu_fwht"], out=b.h, residual=b.h,
+                 ss_out=b.ss_h)
 
 
-def cpu_port_setup(B):
-    """Random nibbles/scales for one layer's GEMV set (values do not change the
-    CPU cost of dequant + matmul)."""
-    import numpy as np
-    sys.path.insert(0, str(ROOT / "oracle"))
-    import r4q_oracle as O
-    rng = np.random.default_rng(0)
+def graph_time(fn, dev, reps=5, warm=3):
+    """ms per replay of fn captured in a CUDA graph (CUDA events on the
+    capture stream; fn runs twice eagerly first, so workspaces exist)."""
+    import torch
+    s = torch.cuda.Stream(dev)
+    with torch.cuda.stream(s):
+        fn()
+        fn()
+    torch.cuda.synchronize()
+    gr = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gr, stream=s):
+        fn()
+    with torch.cuda.stream(s):
+        for _ in range(warm):
+            gr.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(s):
+        e0.record(s)
+        for _ in range(reps):
+            gr.replay()
+        e1.record(s)
+    torch.cuda.synchronize()
+    del gr
+    return e0.elapsed_time(e1) / reps
+
+
+def cfg0_line(dev, peak, launches=1000):
+    """Config 0: one INT4 GEMV 5120x5120 at B = 1 (x already H32-rotated, no
+    prologue), over enough rotated weight copies to exceed 2 x L2, launched
+    `launches` times inside one CUDA graph."""
+    import torch
+    from r4q import ops, synth
+    N = K = HID
+    by = synth.gemv_bytes("int4", 1, N, K)
+    copies = max(2, -(-2 * L2_BYTES // by) + 2)
+    g = torch.Generator(device=dev).manual_seed(0)
+    ws = [synth.linear_int4(N, K, g, dev)[1:] for _ in range(copies)]
+    x = ops.fwht_rows(torch.randn(1, K, generator=g, device=dev).half())
+    y = torch.empty(1, N, device=dev, dtype=torch.float16)
+
+    def fn():
+        for i in range(launches):
+            ops.gemv("int4", x, *ws[i % copies], N, K, out=y)
+    ms = graph_time(fn, dev, reps=3)
+    us = ms * 1e3 / launches
+    gbs = by / (us * 1e-6) / 1e9
+    return {"workload": "cfg0 INT4 GEMV 5120x5120, B=1, x pre-rotated", "copies": copies,
+            "copy_bytes": by, "launches_per_graph": launches, "us_per_launch": round(us, 3),
+            "GBps": round(gbs, 1), "frac": round(gbs / peak, 4),
+            "l2": f"{copies} weight copies = {copies * by / 1e6:.0f} MB > 2 x L2"}
+
+
+def shape_table(layers, dev, peak, Lpro, batches=(1, 4, 16)):
+    """Per-shape roofline of the config-1 GEMVs: each shape launched over the
+    40 layers' distinct weights in one graph; us per launch, GB/s of
+    algorithmic bytes, fraction of the measured copy peak."""
+    import torch
+    from r4q import ops, synth
+    out = []
+    for B in batches:
+        g = torch.Generator(device=dev).manual_seed(B)
+        x = torch.randn(B, 2 * INTER, generator=g, device=dev).half()
+        for name, N, K, pro in LAYER_SHAPES:
+            y = torch.empty(B, N, device=dev, dtype=torch.float16)
+
+            def fn(name=name, N=N, K=K, pro=pro, y=y):
+                for L in layers:
+                    ops.gemv("int4", x, *L[name], N, K, prologue=Lpro[pro], out=y)
+            us = graph_time(fn, dev) * 1e3 / len(layers)
+            by = synth.gemv_bytes("int4", B, N, K)
+            out.append({"shape": f"{name}:{K}->{N}", "batch": B, "us": round(us, 2),
+                        "GBps": round(by / us / 1e3, 1), "frac": round(by / us / 1e3 / peak, 4)})
+    return out
+
+
+def attention_grid(a, dev, peak):
+    """Config 2: split-K flash-decode GQA (40 q / 8 kv heads, head_dim 128)
+    over FP8 E4M3 caches with per-head fp32 scales, every (B, ctx) of the
+    grid.  Each launch reads a distinct cache copy (enough copies that one
+    graph replay streams > 2 x L2); GB/s = cache + q + o bytes per launch."""
+    import math
+    import torch
+    from r4q import ops
+    bs, cs = a.attn_grid.split(":")
+    H, Hk, D = NQ, NKV, HD
+    res = []
+    for B in [int(v) for v in bs.split(",") if v]:
+        for ctx in [int(v) for v in cs.split(",") if v]:
+            per = 2 * B * Hk * ctx * D
+            copies = max(1, min(256, math.ceil(2 * L2_BYTES / per)))
+            n = max(copies, 16)
+            g = torch.Generator(device=dev).manual_seed(B * 100003 + ctx)
+            kc = torch.randint(0, 256, (copies, B, Hk, ctx, D), generator=g, device=dev, dtype=torch.uint8)
+            vc = torch.randint(0, 256, (copies, B, Hk, ctx, D), generator=g, device=dev, dtype=torch.uint8)
+            kc &= 0xF7                     # bytes the reference encoder can emit (no exponent field 15)
+            vc &= 0xF7
+            q = torch.randn(B, H, D, generator=g, device=dev).half()
+            sc = torch.ones(B, Hk, device=dev)
+            o = torch.empty(B, H, D, device=dev, dtype=torch.float16)
+
+            def fn():
+                for i in range(n):
+                    ops.flash_decode(q, kc[i % copies], vc[i % copies], ctx, k_scale=sc, v_scale=sc, out=o)
+            us = graph_time(fn, dev, reps=3) * 1e3 / n
+            by = per + 2 * 2 * B * H * D + 2 * 4 * B * Hk
+            res.append({"batch": B, "ctx": ctx, "us": round(us, 2), "GBps": round(by / us / 1e3, 1),
+                        "frac": round(by / us / 1e3 / peak, 4), "copies": copies})
+            del kc, vc
+            torch.cuda.empty_cache()
+    return {"workload": "cfg2 flash-decode GQA 40q/8kv x128 over FP8 E4M3 KV, per-head scales",
+            "api": "r4q.ops.flash_decode (r4q_flash_decode)", "results": res}
+
+
+def cpu_set_setup(B):
+    """One layer's config-1 GEMV set as the reference stores it (packed
+    nibbles, fp16 scales, uint8 zero points; values do not change the cost)."""
+    import torch
+    g = torch.Generator().manual_seed(0)
     mats = []
     for _, N, K, _ in LAYER_SHAPES:
-        packed = rng.integers(0, 256, size=(N, K // 2), dtype=np.uint8)
-        s = (rng.random((N, K // 32)) * 0.01 + 1e-3).astype(np.float16)
-        z = rng.integers(0, 16, size=(N, K // 32)).astype(np.uint8)
-        mats.append((N, K, packed, O.interleave_scale_zero(s, z)))
-    x = rng.standard_normal((B, 2 * INTER)).astype(np.float16)
+        packed = torch.randint(0, 256, (N, K // 2), generator=g, dtype=torch.uint8)
+        s = (torch.rand(N, K // 32, generator=g) * 0.01 + 1e-3).half()
+        z = torch.randint(0, 16, (N, K // 32), generator=g, dtype=torch.uint8)
+        mats.append((N, K, packed, s, z))
+    x = torch.randn(B, 2 * INTER, generator=g).half()
     return mats, x, B
 
 
-def cpu_port_run(setup, threads, only=None):
-    """The reference's CPU math for the GEMV set — dequant to fp16
-    (int4_quant_v2.py:105-127) then fp32 matmul — through the oracle port,
-    threaded over row chunks.  Returns (algorithmic bytes, seconds)."""
-    import numpy as np
+def cpu_set_run(setup):
+    """The reference's CPU math for one layer's GEMV set: dequantize_int4_asym
+    (int4_quant_v2.py:105-127, restated op for op in the oracle) to fp16, then
+    the fp32 matmul, on every torch intra-op thread.  Returns (algorithmic
+    bytes, seconds)."""
+    import torch
+    sys.path.insert(0, str(ROOT / "oracle"))
     import r4q_oracle as O
-    from concurrent.futures import ThreadPoolExecutor
     from r4q.synth import gemv_bytes
     mats, x, B = setup
-    sel = mats if only is None else [mats[only]]
     t0 = time.perf_counter()
     nbytes = 0
-    with ThreadPoolExecutor(max_workers=threads) as pool:
-        for (N, K, packed, sz) in sel:
-            xin = x[:, :K].astype(np.float32)
-
-            def part(r, packed=packed, sz=sz, xin=xin):
-                W = O.dequant_int4_runtime(packed[r[0]:r[-1] + 1], sz[r[0]:r[-1] + 1])
-                return xin @ W.astype(np.float32).T
-            ys = list(pool.map(part, np.array_split(np.arange(N), threads)))
-            np.concatenate(ys, axis=1).astype(np.float16)
-            nbytes += gemv_bytes("int4", B, N, K)
+    for (N, K, packed, s, z) in mats:
+        W = O.dequant_int4_torch(packed, s, z)
+        (x[:, :K].float() @ W.float().t()).half()
+        nbytes += gemv_bytes("int4", B, N, K)
     return nbytes, time.perf_counter() - t0
+
+
+def cpu_attention_run(B, ctx, reps_s=3.0):
+    """fp32 softmax attention over a dequantised FP8 cache (the reference
+    codec's decode as a 256-entry table, int4_decode_step.hip:71-81) for one
+    (B, ctx) of config 2, in torch on every intra-op thread.  Returns (cache
+    bytes per call, seconds per call)."""
+    import math
+    import numpy as np
+    import torch
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import r4q_oracle as O
+    lut = torch.from_numpy(O.fp8_decode(np.arange(256, dtype=np.uint8)))
+    g = torch.Generator().manual_seed(1)
+    H, Hk, D = NQ, NKV, HD
+    kc = torch.randint(0, 256, (B, Hk, ctx, D), generator=g, dtype=torch.uint8) & 0xF7
+    vc = torch.randint(0, 256, (B, Hk, ctx, D), generator=g, dtype=torch.uint8) & 0xF7
+    q = torch.randn(B, H, D, generator=g)
+
+    def one():
+        K = lut[kc.long()]
+        V = lut[vc.long()]
+        Kx = K.repeat_interleave(H // Hk, dim=1)
+        Vx = V.repeat_interleave(H // Hk, dim=1)
+        s = torch.einsum('bhd,bhsd->bhs', q, Kx) / math.sqrt(D)
+        p = torch.softmax(s, -1)
+        return torch.einsum('bhs,bhsd->bhd', p, Vx).half()
+    one()
+    n, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < reps_s:
+        one()
+        n += 1
+    return 2 * B * Hk * ctx * D, (time.perf_counter() - t0) / n
+
+
+def cpu_baselines(a, B):
+    """CPU legs, rank 0 at N = 1: config 1 (the headline's unit), config 2
+    (attention at B=1, ctx 2048) and config 3 (one decode token, extrapolated
+    from one layer x 40 + the fp16 lm_head)."""
+    import torch
+    threads = torch.get_num_threads()
+    setup = cpu_set_setup(B)
+    cpu_set_run(setup)
+    nb, dt, reps = 0, 0.0, 0
+    while dt < 10.0 and reps < 200:          # about 10 s of host work
+        b_, t_ = cpu_set_run(setup)
+        nb, dt, reps = nb + b_, dt + t_, reps + 1
+    t_set = dt / reps
+    base = {"value": round(nb / dt / 1e9, 4), "unit": "GB/s", "cores": threads, "kind": "port",
+            "seconds": round(dt, 2),
+            "sample": f"{reps} passes over one layer's GEMV set (qkv,o,gate_up,down) of the {a.layers}, "
+                      f"B={B}: reference dequantize_int4_asym restated in torch + fp32 matmul"}
+    ab, at = cpu_attention_run(1, 2048)
+    base["attention"] = {"batch": 1, "ctx": 2048, "GBps": round(ab / at / 1e9, 4), "ms": round(at * 1e3, 2),
+                         "kind": "port", "sample": "fp32 softmax attention over the table-decoded FP8 cache"}
+    g = torch.Generator().manual_seed(2)
+    lm = torch.randn(151936, HID, generator=g).half()
+    xh = torch.randn(1, HID, generator=g).half()
+    t0 = time.perf_counter()
+    (xh.float() @ lm.float().t()).half()
+    t_lm = time.perf_counter() - t0
+    tok_ms = (40 * (t_set + at) + t_lm) * 1e3
+    base["decode"] = {"ctx": 2048, "tok_s": round(1e3 / tok_ms, 4), "ms_per_token": round(tok_ms, 1),
+                      "kind": "port", "sample": "extrapolated: 40 x (one INT4 layer's GEMV set + attention "
+                                                "at ctx 2048) + fp16 lm_head, batch 1"}
+    return base
 
 
 def main_ours(a):
@@ -261,15 +465,8 @@ def main_ours(a):
     dev = torch.device("cuda", local)
     B = a.batch
     layers = build_layers(B, a.layers, dev)
-    Lpro = {"fwht": Lb.PRO_FWHT, "silu_fwht": Lb.PRO_SILU_FWHT}
-    gx = torch.Generator(device=dev).manual_seed(7)
-    x = torch.randn(B, HID, generator=gx, device=dev).half()
-    att = torch.randn(B, NQ * HD, generator=gx, device=dev).half()
-    qkv = torch.empty(B, QKV_N, device=dev, dtype=torch.float16)
-    o = torch.empty(B, HID, device=dev, dtype=torch.float16)
-    gu = (torch.randn(B, 2 * INTER, generator=gx, device=dev)).half()
-    d = torch.empty(B, HID, device=dev, dtype=torch.float16)
-    bufs = (x, qkv, att, o, gu, d)
+    Lpro = {"fwht": Lb.PRO_FWHT, "silu_fwht": Lb.PRO_SILU_FWHT, "rmsnorm_fwht": Lb.PRO_RMSNORM_FWHT}
+    bufs = SetBufs(B, dev, 7)
     nlaunch = 4 * a.layers
 
     s = torch.cuda.Stream(dev)
@@ -310,13 +507,13 @@ def main_ours(a):
     value = per_rank * ws / (ms * 1e-3) / 1e9
 
     # ---- e2e through the public API with host buffers (pinned) ----
-    xh = x.cpu().pin_memory()
+    xh = bufs.h.cpu().pin_memory()
     yh = torch.empty(B, HID, dtype=torch.float16).pin_memory()
     with torch.cuda.stream(s):
         for _ in range(2):
-            x.copy_(xh, non_blocking=True)
+            bufs.h.copy_(xh, non_blocking=True)
             run_set(ops, Lpro, layers, bufs)
-            yh.copy_(d, non_blocking=True)
+            yh.copy_(bufs.h, non_blocking=True)
     torch.cuda.synchronize()
     if ws > 1:
         dist.barrier()
@@ -325,17 +522,30 @@ def main_ours(a):
     with torch.cuda.stream(s):
         ee0.record(s)
         for _ in range(e2e_steps):
-            x.copy_(xh, non_blocking=True)
+            bufs.h.copy_(xh, non_blocking=True)
             run_set(ops, Lpro, layers, bufs)
-            yh.copy_(d, non_blocking=True)
+            yh.copy_(bufs.h, non_blocking=True)
         ee1.record(s)
     torch.cuda.synchronize()
     e2e_ms = ee0.elapsed_time(ee1) / e2e_steps
+    # the same, with the set replayed from the CUDA graph (the API overhead of
+    # the per-call path above is then visible separately)
+    eg0, eg1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(s):
+        eg0.record(s)
+        for _ in range(e2e_steps):
+            bufs.h.copy_(xh, non_blocking=True)
+            graph.replay()
+            yh.copy_(bufs.h, non_blocking=True)
+        eg1.record(s)
+    torch.cuda.synchronize()
+    e2e_g_ms = eg0.elapsed_time(eg1) / e2e_steps
     if ws > 1:
-        t = torch.tensor([e2e_ms], device=dev)
+        t = torch.tensor([e2e_ms, e2e_g_ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t.item())
+        e2e_ms, e2e_g_ms = float(t[0].item()), float(t[1].item())
     e2e = per_rank * ws / (e2e_ms * 1e-3) / 1e9
+    e2e_g = per_rank * ws / (e2e_g_ms * 1e-3) / 1e9
 
     peak, peak_kind = peaks()
     # dominant kernel: the gate_up GEMV (54 % of the step's bytes), timed alone
@@ -344,7 +554,8 @@ def main_ours(a):
     gg = torch.cuda.CUDAGraph()
     with torch.cuda.graph(gg, stream=s):
         for L in layers:
-            ops.gemv("int4", x, *L["gate_up"], 2 * INTER, HID, prologue=Lpro["fwht"], out=gu)
+            ops.gemv("int4", bufs.h, *L["gate_up"], 2 * INTER, HID, prologue=Lpro["rmsnorm_fwht"], out=bufs.gu,
+                     norm_w=bufs.post_norm, eps=1e-6, ss_in=bufs.ss_post)
     with torch.cuda.stream(s):
         gg.replay()
     torch.cuda.synchronize()
@@ -366,41 +577,41 @@ def main_ours(a):
         "data": "synthetic (seeded N(0,0.02)+0.1% x20 outliers, H32-rotated, RTN INT4 asym)",
         "config": {"workload": f"cfg1 Qwen3-14B decode-layer GEMV set x{a.layers} layers, B={B}",
                    "batch": B, "layers": a.layers, "shapes": [f"{n}:{K}->{N}" for n, N, K, _ in LAYER_SHAPES],
-                   "prologues": "fwht on qkv/o/gate_up inputs, silu*up+fwht on down input",
+                   "fusions": "rmsnorm(eps 1e-6)+fwht prologue on qkv/gate_up, fwht on o, silu*up+fwht "
+                               "on down; residual-add epilogue (+ sums of squares) on o/down",
                    "l2": "inputs larger than L2 (8.3 GB distinct weights per step)",
                    "parallelism": f"replicas x{ws}", "timing": "CUDA graph replay, CUDA events"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": TRAFFIC_GATE_UP_B1 if B == 1 else None,
-                     "kernel": "gemv_tma_kernel<INT4> gate_up 5120->34816",
+                     "kernel": "gemv_unit_kernel<INT4> gate_up 5120->34816 (rmsnorm+fwht prologue)",
                      "launch_us": round(k_us, 2), "algorithmic_bytes_per_launch": k_bytes,
                      "peak_source": peak_kind + " (burst copy; of measured)",
                      "step_avg_GBps": round(per_rank / (ms * 1e-3) / 1e9, 1)},
         "e2e": {"value": round(e2e, 1), "unit": "GB/s", "h2d_bytes_per_step": 2 * B * HID,
                 "d2h_bytes_per_step": 2 * B * HID,
-                "api": "r4q.ops.gemv per call (ctypes C ABI), pinned host x in, y out"},
+                "api": "r4q.ops.gemv per call (ctypes C ABI), pinned host x in, y out",
+                "graph_replay": {"value": round(e2e_g, 1), "unit": "GB/s",
+                                 "api": "the same set replayed from a CUDA graph, pinned host x in, y out"}},
         "gpu_launches": nlaunch * a.steps,
         "clocks": clk.summary(),
     }
-    if a.gemv_batches:
+    if not a.no_extra:
+        line["cfg0"] = cfg0_line(dev, peak)
+        line["gemv_shapes"] = shape_table(layers, dev, peak, Lpro)
+    if a.gemv_batches and not a.no_extra:
         line["gemv_batches"] = gemv_set_batches(a, dev, layers, peak, Lpro, ws)
-    if a.decode_ctx:
+    if a.attn_grid and not a.no_extra:
+        torch.cuda.empty_cache()
+        line["attention"] = attention_grid(a, dev, peak)
+    if a.decode_ctx and not a.no_extra:
         del layers
         torch.cuda.empty_cache()
         line["decode"] = decode_tok_s(a, dev, peak, ws, rank)
-    if a.moe_batches:
+    if a.moe_batches and not a.no_extra:
         torch.cuda.empty_cache()
         line["moe"] = moe_tok_s(a, dev, peak, ws, rank)
     if rank == 0 and ws == 1 and not a.no_cpu_baseline:
-        threads = os.cpu_count() or 1
-        setup = cpu_port_setup(B)
-        nb, dt, reps = 0, 0.0, 0
-        while dt < 10.0 and reps < 200:          # about 10 s of host work
-            b_, t_ = cpu_port_run(setup, threads)
-            nb, dt, reps = nb + b_, dt + t_, reps + 1
-        line["cpu_baseline"] = {"value": round(nb / dt / 1e9, 4), "unit": "GB/s", "cores": threads,
-                                "kind": "port", "seconds": round(dt, 2),
-                                "sample": f"{reps} passes over one layer's GEMV set (qkv,o,gate_up,down) "
-                                          f"of the {a.layers}, B={B}"}
+        line["cpu_baseline"] = cpu_baselines(a, B)
     if rank == 0:
         print(json.dumps(line), flush=True)
     if ws > 1:
@@ -411,25 +622,27 @@ def main_reference(a):
     ws, rank, _ = dist_env()
     if rank != 0:
         return
-    threads = os.cpu_count() or 1
-    mats = cpu_port_setup(a.batch)
+    import torch
+    threads = torch.get_num_threads()
+    mats = cpu_set_setup(a.batch)
     tot_b, tot_t, per = 0, 0.0, []
     for i in range(a.warmup + a.steps):
-        nb, dt = cpu_port_run(mats, threads, only=i % len(LAYER_SHAPES))
+        nb, dt = cpu_set_run(mats)
         if i >= a.warmup:
             tot_b += nb
             tot_t += dt
             per.append(dt)
     value = tot_b / tot_t / 1e9
     ms = statistics.median(per) * 1e3
-    sample = "one GEMV of the layer set per step, cycling qkv/o/gate_up/down"
+    sample = ("one layer's whole GEMV set (qkv, o, gate_up, down) per step: the reference's "
+              "dequantize_int4_asym (restated op for op in torch) + fp32 matmul")
     line = {"impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "GB/s",
             "n_gpus": ws, "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(ms, 2),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "int4xfp16->fp32", "data": "synthetic random nibbles/scales",
             "config": {"workload": f"cfg1 Qwen3-14B decode-layer GEMV set, B={a.batch}",
                        "batch": a.batch, "shapes": [f"{n}:{K}->{N}" for n, N, K, _ in LAYER_SHAPES],
-                       "sample": "1 layer per step (of 40)"},
+                       "sample": "1 layer per step (of 40); GB/s is per-layer-invariant"},
             "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads,
                              "kind": "port", "sample": sample},
             "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
@@ -463,6 +676,7 @@ def decode_tok_s(a, dev, peak, ws=1, rank=0):
         comm = tp.Comm(rank, ws, max_batch=1, hidden=cfg['hidden'], vocab=cfg['vocab'])
         dec = tp.TPDecoder(m, cfg, comm, batch=1)
     res = []
+    nccl_dec = None
     from r4q import decode as rdec
     for ctx in ctxs:
         gen = torch.Generator(device=dev).manual_seed(ctx)
@@ -509,15 +723,37 @@ def decode_tok_s(a, dev, peak, ws=1, rank=0):
             ms = float(tt.item())
         kv = cfg['num_layers'] * 2 * cfg['num_kv_heads'] * cfg['head_dim'] * (ctx + a.decode_tokens // 2)
         byt = (wbytes + kv) // ws + 2 * cfg['hidden']          # per GPU
-        res.append({"ctx": ctx, "tok_s": round(1e3 / ms, 1), "ms_per_token": round(ms, 4),
-                    "bytes_per_token_per_gpu": byt, "GBps_per_gpu": round(byt / ms / 1e6, 1),
-                    "roofline_tok_s": round(peak * 1e9 / byt, 1),
-                    "frac": round((byt / ms / 1e6) / peak, 4)})
+        row = {"ctx": ctx, "tok_s": round(1e3 / ms, 1), "ms_per_token": round(ms, 4),
+               "bytes_per_token_per_gpu": byt, "GBps_per_gpu": round(byt / ms / 1e6, 1),
+               "roofline_tok_s": round(peak * 1e9 / byt, 1),
+               "frac": round((byt / ms / 1e6) / peak, 4)}
+        if ws > 1:
+            # comparison arm: the same shards and kernels with NCCL all-reduce
+            # / all-gather between the GEMVs instead of the fused exchange
+            from r4q.tp_nccl import NcclTPDecoder
+            if nccl_dec is None:
+                nccl_dec = NcclTPDecoder(m, cfg, rank, ws, batch=1)
+            nccl_dec.loop(m['embed'], h0, ctx, 3)
+            torch.cuda.synchronize()
+            dist.barrier()
+            n0, n1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            n0.record()
+            nccl_dec.loop(m['embed'], h0, ctx, a.decode_tokens)
+            n1.record()
+            torch.cuda.synchronize()
+            nms = n0.elapsed_time(n1) / a.decode_tokens
+            tt = torch.tensor([nms], device=dev)
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            nms = float(tt.item())
+            row["nccl_allreduce_arm"] = {"tok_s": round(1e3 / nms, 1), "ms_per_token": round(nms, 4),
+                                         "frac": round((byt / nms / 1e6) / peak, 4)}
+        res.append(row)
     pre = None
     if ws == 1 and a.prefill_tokens:
         pre = prefill_tok_s(a, dev, m, cfg)
     if dec is not None:
         dec = None
+        nccl_dec = None
         from r4q import decode
         decode.clear_contexts()
         dist.barrier()

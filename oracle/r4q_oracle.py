@@ -102,6 +102,23 @@ def dequant_int4_runtime(packed: np.ndarray, sz: np.ndarray) -> np.ndarray:
     return ((qb - pairs[..., 1:2]) * pairs[..., 0:1]).reshape(N, K).astype(np.float16)
 
 
+def dequant_int4_torch(packed, scale_fp16, zero_point, block_size: int = BLOCK):
+    """``dequantize_int4_asym`` (int4_quant_v2.py:105-127) restated with the
+    same torch operations in the same order — unpack (low nibble = even k,
+    int4_quant_v2.py:97-102), float, (q - z) * s per block, cast to fp16 — so
+    that the CPU baseline runs the reference's own PyTorch arithmetic.
+    packed uint8 [N, K/2], scale fp16 [N, K/32], zero uint8 [N, K/32] (torch
+    tensors); returns fp16 [N, K]."""
+    import torch
+    N = packed.shape[0]
+    K = packed.shape[1] * 2
+    lo = packed & 0x0F
+    hi = (packed >> 4) & 0x0F
+    q = torch.stack([lo, hi], dim=-1).reshape(N, K)
+    qb = q.reshape(N, K // block_size, block_size).float()
+    return ((qb - zero_point.float().unsqueeze(-1)) * scale_fp16.float().unsqueeze(-1)).reshape(N, K).half()
+
+
 def quantize_int4_sym(blocks: np.ndarray):
     """``quantize_to_int4_symmetric`` (int4_quant_v2.py:131-139): int8 in -8..7."""
     b = np.asarray(blocks, dtype=np.float32)

@@ -1,5 +1,6 @@
 // Internal GEMV launcher interface shared by the C ABI and the decode step.
 #pragma once
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stddef.h>
 
@@ -44,6 +45,9 @@ unsigned* gemv_counters(void* ws);
 // gemv_set_spin_limit lowers it; <= 0 restores the default).  Returns the old value.
 long gemv_spin_limit();
 long gemv_set_spin_limit(long polls);
+// 2-D byte tensor map [rows, row_bytes] with box [box_rows, box_bytes] (TMA).
+int make_map(CUtensorMap* m, const void* base, long rows, long row_bytes, int box_bytes, int box_rows,
+             CUtensorMapSwizzle sw);
 // Device address of r4q_gemv_int4_noalloc's static scratch on the current device.
 int noalloc_scratch(void** out);
 size_t gemv_ws_bytes_for(int B, int N, int ksplit);

@@ -41,6 +41,26 @@ def test_pack_unpack_dequant_bit_exact():
     assert np.array_equal(z2, G['q4_zero'])
 
 
+def test_torch_dequant_restatement_bit_exact():
+    """The torch restatement the CPU baseline times equals the reference's
+    dequantize_int4_asym output (golden vectors it wrote) bit for bit, and the
+    reference function itself where the reference tree is importable."""
+    import torch
+    packed = torch.from_numpy(G['q4_packed'])
+    s = torch.from_numpy(G['q4_scale'])
+    z = torch.from_numpy(G['q4_zero'])
+    deq = O.dequant_int4_torch(packed, s, z).numpy()
+    assert np.array_equal(deq.view(np.uint16), G['q4_deq'].view(np.uint16))
+    ref_dir = Path("/root/reference")
+    if (ref_dir / "int4_quant_v2.py").exists():
+        import importlib.util
+        spec = importlib.util.spec_from_file_location("ref_int4_quant_v2", ref_dir / "int4_quant_v2.py")
+        mod = importlib.util.module_from_spec(spec)
+        spec.loader.exec_module(mod)
+        ref = mod.dequantize_int4_asym(packed, s, z).numpy()
+        assert np.array_equal(deq.view(np.uint16), ref.view(np.uint16))
+
+
 def test_symmetric_lm_head_conversion():
     N, K = G['w_rot'].shape
     q, s = O.quantize_int4_sym(G['w_rot'].reshape(N, K // 32, 32))
