@@ -1,8 +1,9 @@
 // Tensor-parallel exchange over NVLink peer memory: the collective steps of the
 // TP decode (all-reduce after o_proj and down_proj, vocabulary gather after
 // lm_head) and the standalone all-reduce of expert parallelism.  The
-// reference's TP is torch.distributed / RCCL all_reduce between per-layer
-// GEMVs (int4_engine_v5.py TP wrapper).  Here the producer GEMV's epilogue
+// reference runs on one GPU and has no collectives; the split is new here,
+// and r4q/tp_nccl.py keeps an NCCL all-reduce arm of the same step for
+// comparison.  Here the producer GEMV's epilogue
 // pushes its fp32 partials into every rank's buffer and the consumer GEMV's
 // prologue reduces them (tp_exchange.cuh, gemv_tma.cu); this file owns the
 // buffers, the peer mappings, the step counter and the kernels for what the

@@ -40,16 +40,18 @@ constexpr int kTmaMaxSplit = 32;
 constexpr int kTpPre = 3;      // staging items per thread held in registers by a TP consumer
 
 #ifdef R4Q_TRACE
-// Development-only event trace (compiled only with -DR4Q_TRACE).
-__device__ unsigned long long g_trace[8][256];
+// Development-only event trace (compiled only with -DR4Q_TRACE): per launch
+// parity (two consecutive launches), event, CTA: a global-timer stamp.
+// Events: 0 CTA start, 1 griddepcontrol.wait returned, 2 activations
+// staged, 3 first stage landed, 4 consumers done, 5 producer issued all.
+__device__ unsigned long long g_trace[2][8][256];
 __device__ __forceinline__ unsigned long long gtime() {
   unsigned long long t;
   asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
   return t;
 }
 __device__ int g_dbg_mode;  // 1: consumers only wait/release, 2: dequant without MMA
-#define TRACE(slot, idx) do { int _c = (blockIdx.x == 0) ? 0 : (blockIdx.x == 70 ? 1 : -1); \
-  if (_c >= 0 && (idx) < 256) g_trace[_c * 4 + (slot)][(idx)] = gtime(); } while (0)
+#define TRACE(slot, idx) do { if (blockIdx.x < 256) g_trace[tp.trace_par][(slot)][blockIdx.x] = gtime(); } while (0)
 #define DBG_MODE g_dbg_mode
 #else
 #define TRACE(slot, idx) do {} while (0)
@@ -66,7 +68,9 @@ struct TmaParams {
   int ns;          // ring depth (stages), sized to the shared memory left
   int* status;     // set to 1 when a bounded wait gives up
   long spin;       // polls before a wait gives up (kSpinLimit unless lowered for a test)
+  int trace_par;   // R4Q_TRACE builds: trace buffer of this launch
 };
+
 
 __device__ __forceinline__ void consumer_sync() {
   asm volatile("bar.sync 1, %0;" ::"n"(kTmaConsumers * 32) : "memory");
@@ -160,7 +164,6 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
           const unsigned ph = (unsigned)(it / NS) & 1u;
           if (it >= NS) ok = mbar_wait(&empty[slot], ph ^ 1u, tp.status, tp.spin);
           if (!ok) break;
-          TRACE(1, it);
           const bool load_s = T::SBYTES && DBG_MODE != 3;
           mbar_expect_tx(&full[slot], W_STAGE + (load_s ? S_STAGE : 0));
 #pragma unroll
@@ -171,6 +174,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
             tma_load_2d(ring_s + slot * S_STAGE, &tms, st * T::SBYTES, tile * kTileRows, &full[slot]);
         }
       }
+      TRACE(5, 0);
       asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
       // Drain: the CTA must not exit while a copy into its shared memory is in
       // flight.  Consumers that gave up on a wait stop releasing slots (so no
@@ -188,6 +192,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
   // ------------------------------------------------------------ consumers
   // everything below may read outputs of the previous kernel in the stream
   asm volatile("griddepcontrol.wait;" ::: "memory");
+  if (tid == 0) TRACE(1, 0);
   const int ctid = tid;  // 0 .. kTmaConsumers*32-1
   const int ncolx = p.B;
   const int nch_pad = nst * T::CPS;
@@ -338,7 +343,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
     if (ctid < 4) reinterpret_cast<uint32_t*>(zero16)[ctid] = 0u;
   }
   consumer_sync();
-  if (ctid == 0) TRACE(0, 1);
+  if (ctid == 0) TRACE(2, 0);
   if (stamp && p.tpx.nwait) tp_stamp(p.tpx, 4, p.tpx.wait_idx);
 
   // warp -> (k quarter, m-tile); every stage is consumed by all 16 warps
@@ -411,6 +416,9 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
       // warp-uniform: after a timeout the warp no longer waits and no longer
       // releases slots (the producer then stops refilling them and drains)
       if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&full[slot], phase, tp.status, tp.spin));
+#ifdef R4Q_TRACE
+      if (ctid == 0 && uidx == 0 && st == cur.sb - st0) TRACE(3, 0);
+#endif
       const uint32_t wst = ring_w_u + slot * W_STAGE;
       const uint32_t sst = ring_s_u + slot * S_STAGE;
       uint64_t* emp = &empty[slot];
@@ -470,28 +478,31 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
           }
         }
       } else {
-        uint32_t frag[V][NM][4];
+        // raw chunks of every v first (the slot is free once they are in
+        // registers), then dequantise and multiply one chunk at a time: only
+        // one chunk's fragments are live, which keeps the B > 8 instance
+        // (two column groups) out of local memory
+        RowChunk A[V], Bq[V];
 #pragma unroll
         for (int v = 0; v < V; ++v) {
-          RowChunk A, Bq;
-          A.w = lds128(wst + offA[v]);
-          Bq.w = lds128(wst + offB[v]);
+          A[v].w = lds128(wst + offA[v]);
+          Bq[v].w = lds128(wst + offB[v]);
           if constexpr (FMT == W_INT4) {
-            A.s = lds32(sst + soffA[v]);
-            Bq.s = lds32(sst + soffB[v]);
+            A[v].s = lds32(sst + soffA[v]);
+            Bq[v].s = lds32(sst + soffB[v]);
           } else if constexpr (FMT == W_INT8) {
-            A.s = lds16(sst + soffA[v]);
-            Bq.s = lds16(sst + soffB[v]);
+            A[v].s = lds16(sst + soffA[v]);
+            Bq[v].s = lds16(sst + soffB[v]);
           } else {
-            A.s = Bq.s = 0;
+            A[v].s = Bq[v].s = 0;
           }
-          chunk_dequant<FMT>(A, Bq, frag[v]);
         }
-        // the slot is free once its bytes are in registers; the MMAs follow
         __syncwarp();
         if (lane == 0 && ok) mbar_arrive(emp);
 #pragma unroll
         for (int v = 0; v < V; ++v) {
+          uint32_t frag[NM][4];
+          chunk_dequant<FMT>(A[v], Bq[v], frag);
           const int off = (st * T::CPS + cidx[v]) * 16;
 #pragma unroll
           for (int cg = 0; cg < NG; ++cg) {
@@ -499,8 +510,8 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
             for (int sub = 0; sub < NM / 2; ++sub) {
               const uint4 xf = lds128(xrow[cg] + off + sub * xsub);
               const int j = 2 * sub;
-              mma16816(acc[cg][0], frag[v][j][0], frag[v][j][1], frag[v][j][2], frag[v][j][3], xf.x, xf.y);
-              mma16816(acc[cg][1], frag[v][j + 1][0], frag[v][j + 1][1], frag[v][j + 1][2], frag[v][j + 1][3], xf.z, xf.w);
+              mma16816(acc[cg][0], frag[j][0], frag[j][1], frag[j][2], frag[j][3], xf.x, xf.y);
+              mma16816(acc[cg][1], frag[j + 1][0], frag[j + 1][1], frag[j + 1][2], frag[j + 1][3], xf.z, xf.w);
             }
           }
         }
@@ -637,7 +648,6 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
         if (lane == 0) p.cnt[row0 >> 4] = 0u;
       }
     }
-    if (ctid == 0) TRACE(3, uidx);
   }
   // outputs pushed into peer memory: the last CTA signals the exchange to
   // every rank once all CTAs' pushes are fenced at system scope
@@ -648,7 +658,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
   } else if (p.npush > 1 && !p.tpx.ll_sig) {
     __threadfence_system();
   }
-  if (ctid == 0) TRACE(0, 2);
+  if (ctid == 0) TRACE(4, 0);
 }
 
 // --------------------------------------------------------------- host ----
@@ -822,6 +832,10 @@ static int launch_tma_t(const GemvArgs& a) {
   tp.xsum_bytes = pl.xsum_bytes;
   tp.ns = pl.ns;
   tp.spin = gemv_spin_limit();
+#ifdef R4Q_TRACE
+  static int trace_launch = 0;
+  tp.trace_par = (trace_launch++) & 1;
+#endif
   tp.status = reinterpret_cast<int*>(a.ws);   // header word 0 (null without a workspace)
 
   cudaLaunchConfig_t cfg{};
@@ -843,14 +857,14 @@ static int launch_tma_t(const GemvArgs& a) {
 }
 
 #ifdef R4Q_TRACE
-extern "C" int r4q_trace_read(unsigned long long* host) {
+extern "C" int r4q_trace_read(unsigned long long* host) {  // [2][8][256]
   return cudaMemcpyFromSymbol(host, g_trace, sizeof(g_trace)) == cudaSuccess ? 0 : -4;
 }
 extern "C" int r4q_trace_mode(int m) {
   return cudaMemcpyToSymbol(g_dbg_mode, &m, sizeof(int)) == cudaSuccess ? 0 : -4;
 }
 extern "C" int r4q_trace_clear() {
-  static unsigned long long z[8][256];
+  static unsigned long long z[2][8][256];
   return cudaMemcpyToSymbol(g_trace, z, sizeof(g_trace)) == cudaSuccess ? 0 : -4;
 }
 #endif
