@@ -321,37 +321,51 @@ __device__ __forceinline__ void chunk_mma(const RowChunk& ra, const RowChunk& rb
 // Activation staging with 4 lanes per 32-block: lane q of a quad owns k =
 // 8q..8q+7, applies the prologue, runs the FWHT (strides 1,2,4 in registers,
 // 8 and 16 across the quad, same stage order as the 32-register form) and
-// stores its 8 values as one 16-byte sub-row of the permuted layout.  All 32
-// lanes of the warp must call it (shuffles); `valid` masks the stores.
-// have_raw: the 8 input values are given (a TP consumer read them already).
-template <int FMT, bool DIAG>
-__device__ __forceinline__ void stage_quad(const GemvParams& p, int col, int k0, int q, float rrms,
-                                           uint8_t* xs_col, int nch_pad, int blk, bool valid,
-                                           float2* xsum_slot, bool have_raw = false,
-                                           uint4 raw_in = uint4{0, 0, 0, 0}) {
-  __half v[8];
-  const bool in = valid && k0 < p.K;
+// stores its 8 values as one 16-byte sub-row of the permuted layout.
+// Split in two so that a thread can issue the loads of several items before
+// it waits for any of them (one memory round trip for the whole staging):
+// stage_load reads the raw inputs, stage_finish computes and stores.  All 32
+// lanes of the warp must call stage_finish (shuffles); `valid` masks stores.
+struct QuadIn {
+  uint4 a;   // 8 fp16 of x (SiLU prologue: the gate half)
+  uint4 b;   // SiLU prologue: the 8 matching values of the up half
+  uint4 w;   // RMSNorm prologue: the 8 norm weights
+};
+
+__device__ __forceinline__ QuadIn stage_load(const GemvParams& p, int col, int k0, int q, bool valid,
+                                             bool have_raw = false, uint4 raw_in = uint4{0, 0, 0, 0}) {
+  QuadIn in{};
+  if (!(valid && k0 < p.K)) return in;
   const __half* xr = p.x + (long)col * p.ldx + k0 + 8 * q;
+  if (have_raw) in.a = raw_in;
+  else if (p.tpx.nwait && p.prologue != R4Q_PRO_NONE) in.a = tp_row8(p, col, k0 + 8 * q);
+  else in.a = *reinterpret_cast<const uint4*>(xr);
+  if (p.prologue == R4Q_PRO_SILU_FWHT) in.b = *reinterpret_cast<const uint4*>(xr + p.K);
+  if (p.prologue == R4Q_PRO_RMSNORM_FWHT) in.w = __ldg(reinterpret_cast<const uint4*>(p.norm_w + k0 + 8 * q));
+  return in;
+}
+
+template <int FMT, bool DIAG>
+__device__ __forceinline__ void stage_finish(const GemvParams& p, const QuadIn& in, int k0, int q, float rrms,
+                                             uint8_t* xs_col, int nch_pad, int blk, bool valid,
+                                             float2* xsum_slot) {
+  __half v[8];
+  const bool inr = valid && k0 < p.K;
   if (p.prologue == R4Q_PRO_NONE) {
-    uint4 raw = in ? *reinterpret_cast<const uint4*>(xr) : make_uint4(0, 0, 0, 0);
-    *reinterpret_cast<uint4*>(v) = raw;
+    *reinterpret_cast<uint4*>(v) = in.a;
   } else {
     float f[8];
-    if (in) {
-      const uint4 raw = have_raw ? raw_in
-                        : p.tpx.nwait ? tp_row8(p, col, k0 + 8 * q) : *reinterpret_cast<const uint4*>(xr);
-      const __half* h = reinterpret_cast<const __half*>(&raw);
+    if (inr) {
+      const __half* h = reinterpret_cast<const __half*>(&in.a);
       if (p.prologue == R4Q_PRO_SILU_FWHT) {
-        const uint4 ru = *reinterpret_cast<const uint4*>(xr + p.K);
-        const __half* hu = reinterpret_cast<const __half*>(&ru);
+        const __half* hu = reinterpret_cast<const __half*>(&in.b);
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           const float g = __half2float(h[j]);
           f[j] = g / (1.0f + expf(-g)) * __half2float(hu[j]);
         }
       } else if (p.prologue == R4Q_PRO_RMSNORM_FWHT) {
-        const uint4 rw = __ldg(reinterpret_cast<const uint4*>(p.norm_w + k0 + 8 * q));
-        const __half* hw = reinterpret_cast<const __half*>(&rw);
+        const __half* hw = reinterpret_cast<const __half*>(&in.w);
 #pragma unroll
         for (int j = 0; j < 8; ++j) f[j] = __half2float(h[j]) * rrms * __half2float(hw[j]);
       } else {

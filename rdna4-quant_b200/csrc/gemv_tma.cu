@@ -38,13 +38,17 @@ constexpr int kTmaThreads = (kTmaConsumers + 1) * 32;
 constexpr int kTileRows = 64;
 constexpr int kTmaMaxSplit = 32;
 constexpr int kTpPre = 3;      // staging items per thread held in registers by a TP consumer
+constexpr int kStageBatch = 2; // staging rounds whose loads are in flight together
+constexpr int kStagedBar = 10; // named barrier (1: consumers, 2-9: m groups): activations staged (consumers arrive, producer waits)
+constexpr int kPrewait = 4;    // ring stages requested before the previous kernel completes
 
 #ifdef R4Q_TRACE
 // Development-only event trace (compiled only with -DR4Q_TRACE): per launch
-// parity (two consecutive launches), event, CTA: a global-timer stamp.
+// slot (eight consecutive launches), event, CTA: a global-timer stamp.
 // Events: 0 CTA start, 1 griddepcontrol.wait returned, 2 activations
-// staged, 3 first stage landed, 4 consumers done, 5 producer issued all.
-__device__ unsigned long long g_trace[2][8][256];
+// staged, 3 first stage landed, 4 consumers done, 5 producer issued all,
+// 6 RMSNorm scale known (staging starts), 7 first staging batch stored.
+__device__ unsigned long long g_trace[8][8][256];
 __device__ __forceinline__ unsigned long long gtime() {
   unsigned long long t;
   asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
@@ -69,8 +73,15 @@ struct TmaParams {
   int* status;     // set to 1 when a bounded wait gives up
   long spin;       // polls before a wait gives up (kSpinLimit unless lowered for a test)
   int trace_par;   // R4Q_TRACE builds: trace buffer of this launch
+  int prewait;     // stages the producer requests before the previous kernel completes
 };
 
+
+// Floats of the k-part reduction buffer: 4 m-tiles x (P - 1) writer parts x
+// NG column groups x 4 accumulators x 32 lanes (P = 8 on the block-diagonal
+// path, whose warps own two m-tiles, else 4).
+template <int NG, bool DIAG>
+__host__ __device__ constexpr int red_floats() { return 4 * ((DIAG ? 8 : 4) - 1) * NG * 4 * 32; }  // >= any MPW's need
 
 __device__ __forceinline__ void consumer_sync() {
   asm volatile("bar.sync 1, %0;" ::"n"(kTmaConsumers * 32) : "memory");
@@ -123,8 +134,8 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
   uint8_t* xs = ring_s + NS * S_STAGE;
   float2* xsum = reinterpret_cast<float2*>(xs + tp.x_bytes);        // [B][chunks] (X, E)
   uint8_t* zero16 = xs + tp.x_bytes + tp.xsum_bytes;
-  float* red = reinterpret_cast<float*>(zero16 + 16);               // [4 m-tiles][3][NG*4][32]
-  uint64_t* full = reinterpret_cast<uint64_t*>(red + 4 * 3 * NG * 4 * 32);
+  float* red = reinterpret_cast<float*>(zero16 + 16);               // [4 m-tiles][P-1][NG*4][32]
+  uint64_t* full = reinterpret_cast<uint64_t*>(red + red_floats<NG, DIAG>());
   uint64_t* empty = full + NS;
   __shared__ float s_rrms[16];
 
@@ -150,42 +161,60 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
 
   // ------------------------------------------------------------ producer
   if (warp == kTmaConsumers) {
+    // The whole warp runs the schedule (its lanes poll together, so `ok`
+    // stays warp-uniform); lane 0 issues the copies.
     if (lane == 0) {
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmw)) : "memory");
       if (T::SBYTES) asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tms)) : "memory");
-      int it = 0;
-      bool ok = true;
-      SegIter iter = iter0;
-      Seg sg;
-      while (ok && iter.next(sg)) {
-        const int tile = sg.tile;
-        for (int st = sg.sb; st < sg.se && ok; ++st, ++it) {
-          const int slot = it % NS;
-          const unsigned ph = (unsigned)(it / NS) & 1u;
-          if (it >= NS) ok = mbar_wait(&empty[slot], ph ^ 1u, tp.status, tp.spin);
-          if (!ok) break;
+    }
+    // weights are read once: evict-first in L2, so the stream does not push
+    // out the activations, norm weights and sums of squares the next kernels
+    // read right after their griddepcontrol.wait
+    const uint64_t l2_stream = l2_policy_evict_first();
+    int it = 0;
+    bool ok = true, held = false;
+    SegIter iter = iter0;
+    Seg sg;
+    while (ok && iter.next(sg)) {
+      const int tile = sg.tile;
+      for (int st = sg.sb; st < sg.se && ok; ++st, ++it) {
+        const int slot = it % NS;
+        const unsigned ph = (unsigned)(it / NS) & 1u;
+        if (it == tp.prewait) {
+          // Only `prewait` stages go out before the previous kernel is done;
+          // the rest wait until the consumers have staged the activations, so
+          // those loads do not queue behind a full ring of weight requests
+          // (with every SM's ring in flight, any new request waits ~3-4 us).
+          asm volatile("griddepcontrol.wait;" ::: "memory");
+          named_sync(kStagedBar, kTmaThreads);
+          held = true;
+        }
+        if (it >= NS) ok = __all_sync(0xffffffffu, mbar_wait(&empty[slot], ph ^ 1u, tp.status, tp.spin));
+        if (!ok) break;
+        if (lane == 0) {
           const bool load_s = T::SBYTES && DBG_MODE != 3;
           mbar_expect_tx(&full[slot], W_STAGE + (load_s ? S_STAGE : 0));
 #pragma unroll
           for (int b = 0; b < T::BOXES; ++b)
-            tma_load_2d(ring_w + slot * W_STAGE + b * (kTileRows * 128), &tmw,
-                        st * (T::CPS * 16) + b * 128, tile * kTileRows, &full[slot]);
+            tma_load_2d_hint(ring_w + slot * W_STAGE + b * (kTileRows * 128), &tmw,
+                             st * (T::CPS * 16) + b * 128, tile * kTileRows, &full[slot], l2_stream);
           if (load_s)
-            tma_load_2d(ring_s + slot * S_STAGE, &tms, st * T::SBYTES, tile * kTileRows, &full[slot]);
+            tma_load_2d_hint(ring_s + slot * S_STAGE, &tms, st * T::SBYTES, tile * kTileRows, &full[slot],
+                             l2_stream);
         }
       }
-      TRACE(5, 0);
-      asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-      // Drain: the CTA must not exit while a copy into its shared memory is in
-      // flight.  Consumers that gave up on a wait stop releasing slots (so no
-      // slot is ever refilled before its previous copy landed); here the last
-      // copy issued into each slot is awaited.  Copies complete on their own
-      // within microseconds, so this wait keeps the full limit.
+    }
+    if (lane == 0) TRACE(5, 0);
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    if (!held) named_sync(kStagedBar, kTmaThreads);   // the consumers arrive once in every case
+    // Drain: the CTA must not exit while a copy into its shared memory is in
+    // flight.  Consumers that gave up on a wait stop releasing slots (so no
+    // slot is ever refilled before its previous copy landed); here the last
+    // copy issued into each slot is awaited.  Copies complete on their own
+    // within microseconds, so this wait keeps the full limit.
+    if (lane == 0)
       for (int j = (it > NS ? it - NS : 0); j < it; ++j)
         mbar_drain(&full[j % NS], (unsigned)(j / NS) & 1u, tp.status);
-    } else {
-      asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-    }
     return;
   }
 
@@ -193,6 +222,16 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
   // everything below may read outputs of the previous kernel in the stream
   asm volatile("griddepcontrol.wait;" ::: "memory");
   if (tid == 0) TRACE(1, 0);
+#ifdef R4Q_TRACE_PROBE
+  // latency probe: two dependent loads of the activations (event 6, 7)
+  if (tid == 0) {
+    volatile const unsigned short* xv = reinterpret_cast<volatile const unsigned short*>(p.x);
+    unsigned short a = xv[0];
+    TRACE(6, (int)a);
+    unsigned short b = xv[64 + (a & 1)];
+    TRACE(7, (int)b);
+  }
+#endif
   const int ctid = tid;  // 0 .. kTmaConsumers*32-1
   const int ncolx = p.B;
   const int nch_pad = nst * T::CPS;
@@ -301,55 +340,99 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
       s_rrms[lane] = rsqrtf(ss / (float)p.K + p.eps);
     }
     consumer_sync();
-  } else if (p.prologue == R4Q_PRO_RMSNORM_FWHT) {
-    for (int c = warp; c < ncolx; c += kTmaConsumers) {
-      float ss = 0.0f;
-      if (p.ss_in) {
-        for (int i = lane; i < p.ss_in_parts; i += 32) ss += p.ss_in[(long)i * ncolx + c];
-      } else {
-        const __half2* xr = reinterpret_cast<const __half2*>(p.x + (long)c * p.ldx);
-        for (int i = lane; i < (p.K >> 1); i += 32) {
-          const float2 f = __half22float2(xr[i]);
-          ss += f.x * f.x + f.y * f.y;
-        }
-      }
-      ss = warp_sum(ss);
-      if (lane == 0) s_rrms[c] = rsqrtf(ss / (float)p.K + p.eps);
-    }
-    consumer_sync();
   }
   {
+    // (column, block, quarter) items, round r of thread t = item
+    // t + r * 512; the loads of up to kStageBatch rounds are issued before
+    // any of them is used, so staging costs one memory round trip per batch
     const int nblk = nch_pad * F::CK / 32;
     const int k_base = st0 * T::SK;
-    const int total = ncolx * nblk * 4;                  // (column, block, quarter) items
-    for (int base = warp * 32; base < total; base += kTmaConsumers * 32) {
-      const int item = base + lane;
-      const bool valid = item < total;
-      const int it2 = valid ? item : 0;
-      const int q = it2 & 3, cb = it2 >> 2;
-      const int col = cb / nblk, blk = cb - col * nblk;
-      const int rnd = (base - warp * 32) / (kTmaConsumers * 32);         // round of this item
-      uint4 raw_in = make_uint4(0, 0, 0, 0);
-      if (tp_one) {
+    const int total = ncolx * nblk * 4;
+    const int nthr = kTmaConsumers * 32;
+    const int rounds = (total + nthr - 1) / nthr;
+    for (int r0 = 0; r0 < rounds; r0 += kStageBatch) {
+      QuadIn in[kStageBatch];
 #pragma unroll
-        for (int r = 0; r < kTpPre; ++r)
-          if (r == rnd) raw_in = tp_raw[r];
+      for (int j = 0; j < kStageBatch; ++j) {
+        const int item = (r0 + j) * nthr + ctid;
+        const bool valid = r0 + j < rounds && item < total;
+        const int it2 = valid ? item : 0;
+        const int q = it2 & 3, cb = it2 >> 2;
+        const int col = cb / nblk, blk = cb - col * nblk;
+        uint4 raw_in = make_uint4(0, 0, 0, 0);
+        if (tp_one) {
+#pragma unroll
+          for (int r = 0; r < kTpPre; ++r)
+            if (r == r0 + j) raw_in = tp_raw[r];
+        }
+        in[j] = stage_load(p, col, k_base + blk * 32, q, valid, tp_one, raw_in);
       }
-      stage_quad<FMT, DIAG>(p, col, k_base + blk * 32, q,
-                            p.prologue == R4Q_PRO_RMSNORM_FWHT ? s_rrms[col] : 1.0f,
-                            xs + (long)col * colstride, nch_pad, blk, valid,
-                            xsum + col * nch_pad + blk, tp_one, raw_in);
+      if (r0 == 0 && !p.tpx.nwait && p.prologue == R4Q_PRO_RMSNORM_FWHT) {
+        // the RMSNorm scale of each column, while the first batch's loads
+        // are in flight (one memory round trip for both)
+        for (int c = warp; c < ncolx; c += kTmaConsumers) {
+          float ss = 0.0f;
+          if (p.ss_in) {
+            for (int i = lane; i < p.ss_in_parts; i += 32) ss += p.ss_in[(long)i * ncolx + c];
+          } else {
+            const __half2* xr = reinterpret_cast<const __half2*>(p.x + (long)c * p.ldx);
+            for (int i = lane; i < (p.K >> 1); i += 32) {
+              const float2 f = __half22float2(xr[i]);
+              ss += f.x * f.x + f.y * f.y;
+            }
+          }
+          ss = warp_sum(ss);
+          if (lane == 0) s_rrms[c] = rsqrtf(ss / (float)p.K + p.eps);
+        }
+        consumer_sync();
+#ifndef R4Q_TRACE_PROBE
+        if (ctid == 0) TRACE(6, 0);
+#endif
+      }
+#pragma unroll
+      for (int j = 0; j < kStageBatch; ++j) {
+        if (r0 + j >= rounds) break;                       // warp-uniform
+        const int item = (r0 + j) * nthr + ctid;
+        const bool valid = item < total;
+        const int it2 = valid ? item : 0;
+        const int q = it2 & 3, cb = it2 >> 2;
+        const int col = cb / nblk, blk = cb - col * nblk;
+        stage_finish<FMT, DIAG>(p, in[j], k_base + blk * 32, q,
+                                p.prologue == R4Q_PRO_RMSNORM_FWHT ? s_rrms[col] : 1.0f,
+                                xs + (long)col * colstride, nch_pad, blk, valid, xsum + col * nch_pad + blk);
+      }
+#ifndef R4Q_TRACE_PROBE
+      if (ctid == 0 && r0 == 0) TRACE(7, 0);
+#endif
     }
     if (ctid < 4) reinterpret_cast<uint32_t*>(zero16)[ctid] = 0u;
   }
   consumer_sync();
+  named_arrive(kStagedBar, kTmaThreads);                  // releases the rest of the ring
   if (ctid == 0) TRACE(2, 0);
   if (stamp && p.tpx.nwait) tp_stamp(p.tpx, 4, p.tpx.wait_idx);
 
-  // warp -> (k quarter, m-tile); every stage is consumed by all 16 warps
+  // warp -> (m group, k part); every stage is consumed by all 16 warps.  A
+  // warp owns MPW m-tiles of 16 rows and 1/P of each stage's chunks; with
+  // MPW = 2 (block-diagonal path) one activation fragment feeds the MMAs of
+  // two m-tiles, halving the shared-memory reads of activations.
+#ifndef R4Q_DIAG_MPW
+#define R4Q_DIAG_MPW 1
+#endif
+  constexpr int MPW = DIAG ? R4Q_DIAG_MPW : 1;              // m-tiles per warp
+  constexpr int NGRP = 4 / MPW;                             // m groups per stage
+  constexpr int P = kTmaConsumers / NGRP;                   // k parts
+  constexpr int SPT = T::CPS / P;                           // chunks per part per row per stage
+  constexpr int VV = SPT / 4;                               // chunks per lane per row per stage
+  static_assert(VV >= 1, "too many k parts");
   const int g = lane >> 2, t = lane & 3;
-  const int mt = warp & 3, part = warp >> 2;
-  const int ra = mt * 16 + row_perm(g), rb = ra + 8;       // rows inside the 64-row tile
+  const int mgrp = warp % NGRP, part = warp / NGRP;
+  int ra[MPW], rb[MPW];                                     // rows inside the 64-row tile
+#pragma unroll
+  for (int mi = 0; mi < MPW; ++mi) {
+    ra[mi] = (mgrp * MPW + mi) * 16 + row_perm(g);
+    rb[mi] = ra[mi] + 8;
+  }
   int colx[NG];
 #pragma unroll
   for (int cg = 0; cg < NG; ++cg) colx[cg] = min(cg * 8 + g, p.B - 1);
@@ -358,28 +441,31 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
   const uint8_t* xfeed = feed ? xs + (long)(g & 1) * colstride : nullptr;
 
   // Stage-invariant shared-memory offsets of this thread's chunks (the stage
-  // slot base is added per stage).  Chunk v of row r sits in 128-byte box
+  // slot base is added per stage).  Chunk c of row r sits in 128-byte box
   // c >> 3 at 16-byte unit (c & 7) ^ (r & 7) (128-byte swizzle).
-  constexpr int SPT = T::CPS / 4;                           // chunks per warp per row per stage
-  int offA[V], offB[V], soffA[V], soffB[V], cidx[V];
+  int offA[MPW][VV], offB[MPW][VV], soffA[MPW][VV], soffB[MPW][VV], cidx[VV];
 #pragma unroll
-  for (int v = 0; v < V; ++v) {
+  for (int v = 0; v < VV; ++v) {
     const int c = part * SPT + 4 * v + t;
     cidx[v] = c;
     const int box = c >> 3, cb = c & 7;
-    offA[v] = box * (kTileRows * 128) + ra * 128 + ((cb ^ (ra & 7)) << 4);
-    offB[v] = box * (kTileRows * 128) + rb * 128 + ((cb ^ (rb & 7)) << 4);
-    if constexpr (FMT == W_INT4) {
-      // 128-byte scale rows, 128-byte swizzle: (scale, zero) of block c
-      soffA[v] = ra * 128 + (((c >> 2) ^ (ra & 7)) << 4) + (c & 3) * 4;
-      soffB[v] = rb * 128 + (((c >> 2) ^ (rb & 7)) << 4) + (c & 3) * 4;
-    } else if constexpr (FMT == W_INT8) {
-      // 32-byte scale rows, 32-byte swizzle: fp16 scale of block c >> 1
-      const int bk = c >> 1;
-      soffA[v] = ra * 32 + (((bk >> 3) ^ ((ra >> 2) & 1)) << 4) + (bk & 7) * 2;
-      soffB[v] = rb * 32 + (((bk >> 3) ^ ((rb >> 2) & 1)) << 4) + (bk & 7) * 2;
-    } else {
-      soffA[v] = soffB[v] = 0;
+#pragma unroll
+    for (int mi = 0; mi < MPW; ++mi) {
+      const int a = ra[mi], b = rb[mi];
+      offA[mi][v] = box * (kTileRows * 128) + a * 128 + ((cb ^ (a & 7)) << 4);
+      offB[mi][v] = box * (kTileRows * 128) + b * 128 + ((cb ^ (b & 7)) << 4);
+      if constexpr (FMT == W_INT4) {
+        // 128-byte scale rows, 128-byte swizzle: (scale, zero) of block c
+        soffA[mi][v] = a * 128 + (((c >> 2) ^ (a & 7)) << 4) + (c & 3) * 4;
+        soffB[mi][v] = b * 128 + (((c >> 2) ^ (b & 7)) << 4) + (c & 3) * 4;
+      } else if constexpr (FMT == W_INT8) {
+        // 32-byte scale rows, 32-byte swizzle: fp16 scale of block c >> 1
+        const int bk = c >> 1;
+        soffA[mi][v] = a * 32 + (((bk >> 3) ^ ((a >> 2) & 1)) << 4) + (bk & 7) * 2;
+        soffB[mi][v] = b * 32 + (((bk >> 3) ^ ((b >> 2) & 1)) << 4) + (bk & 7) * 2;
+      } else {
+        soffA[mi][v] = soffB[mi][v] = 0;
+      }
     }
   }
   // activation pointers (block-diagonal path: lanes that feed nothing read a
@@ -404,13 +490,15 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
     const Seg cur = sg;
     more = iter.next(sg);                                   // is there a next unit?
     const int tile = cur.tile;
-    float acc[NG][2][4];
+    float acc[MPW][NG][2][4];
 #pragma unroll
-    for (int cg = 0; cg < NG; ++cg)
+    for (int mi = 0; mi < MPW; ++mi)
 #pragma unroll
-      for (int h = 0; h < 2; ++h)
+      for (int cg = 0; cg < NG; ++cg)
 #pragma unroll
-        for (int i = 0; i < 4; ++i) acc[cg][h][i] = 0.0f;
+        for (int h = 0; h < 2; ++h)
+#pragma unroll
+          for (int i = 0; i < 4; ++i) acc[mi][cg][h][i] = 0.0f;
 
     for (int st = cur.sb - st0; st < cur.se - st0; ++st) {  // st: stage index inside the staged x
       // warp-uniform: after a timeout the warp no longer waits and no longer
@@ -432,49 +520,61 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
         continue;
       }
       if constexpr (DIAG) {
-        uint4 wa[V], wb[V];
-        uint32_t sza[V], szb[V];
+        uint4 wa[MPW][VV], wb[MPW][VV];
+        uint32_t sza[MPW][VV], szb[MPW][VV];
 #pragma unroll
-        for (int v = 0; v < V; ++v) {
-          wa[v] = lds128(wst + offA[v]);
-          wb[v] = lds128(wst + offB[v]);
-          sza[v] = lds32(sst + soffA[v]);
-          szb[v] = lds32(sst + soffB[v]);
-        }
+        for (int mi = 0; mi < MPW; ++mi)
+#pragma unroll
+          for (int v = 0; v < VV; ++v) {
+            wa[mi][v] = lds128(wst + offA[mi][v]);
+            wb[mi][v] = lds128(wst + offB[mi][v]);
+            sza[mi][v] = lds32(sst + soffA[mi][v]);
+            szb[mi][v] = lds32(sst + soffB[mi][v]);
+          }
         __syncwarp();
         if (lane == 0 && ok) mbar_arrive(emp);
         const uint32_t xst = xbase + st * xstep;
 #pragma unroll
-        for (int v = 0; v < V; ++v) {
-          const uint32_t wa_[4] = {wa[v].x, wa[v].y, wa[v].z, wa[v].w};
-          const uint32_t wb_[4] = {wb[v].x, wb[v].y, wb[v].z, wb[v].w};
+        for (int v = 0; v < VV; ++v) {
           const uint32_t xv = xst + (feed ? 4 * v * 16 : 0);
-          float c0[4] = {0.f, 0.f, 0.f, 0.f}, c1[4] = {0.f, 0.f, 0.f, 0.f};
+          float c0[MPW][4], c1[MPW][4];
+#pragma unroll
+          for (int mi = 0; mi < MPW; ++mi)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) c0[mi][i] = c1[mi][i] = 0.0f;
 #pragma unroll
           for (int m = 0; m < 4; ++m) {
-            const uint32_t a8 = wa_[m] >> 8, b8 = wb_[m] >> 8;
-            const uint32_t alo = lop3_and_or(wa_[m], 0x000F000Fu, 0x64006400u);
-            const uint32_t ahi = lop3_and_or(wa_[m], 0x00F000F0u, 0x54005400u);
-            const uint32_t blo = lop3_and_or(wb_[m], 0x000F000Fu, 0x64006400u);
-            const uint32_t bhi = lop3_and_or(wb_[m], 0x00F000F0u, 0x54005400u);
-            const uint32_t alo2 = lop3_and_or(a8, 0x000F000Fu, 0x64006400u);
-            const uint32_t ahi2 = lop3_and_or(a8, 0x00F000F0u, 0x54005400u);
-            const uint32_t blo2 = lop3_and_or(b8, 0x000F000Fu, 0x64006400u);
-            const uint32_t bhi2 = lop3_and_or(b8, 0x00F000F0u, 0x54005400u);
             const uint4 xf = lds128(xv + m * xsub);
-            mma16816(c0, alo, blo, ahi, bhi, xf.x, xf.y);
-            mma16816(c1, alo2, blo2, ahi2, bhi2, xf.z, xf.w);
+#pragma unroll
+            for (int mi = 0; mi < MPW; ++mi) {
+              const uint32_t wam = m == 0 ? wa[mi][v].x : m == 1 ? wa[mi][v].y : m == 2 ? wa[mi][v].z : wa[mi][v].w;
+              const uint32_t wbm = m == 0 ? wb[mi][v].x : m == 1 ? wb[mi][v].y : m == 2 ? wb[mi][v].z : wb[mi][v].w;
+              const uint32_t a8 = wam >> 8, b8 = wbm >> 8;
+              const uint32_t alo = lop3_and_or(wam, 0x000F000Fu, 0x64006400u);
+              const uint32_t ahi = lop3_and_or(wam, 0x00F000F0u, 0x54005400u);
+              const uint32_t blo = lop3_and_or(wbm, 0x000F000Fu, 0x64006400u);
+              const uint32_t bhi = lop3_and_or(wbm, 0x00F000F0u, 0x54005400u);
+              const uint32_t alo2 = lop3_and_or(a8, 0x000F000Fu, 0x64006400u);
+              const uint32_t ahi2 = lop3_and_or(a8, 0x00F000F0u, 0x54005400u);
+              const uint32_t blo2 = lop3_and_or(b8, 0x000F000Fu, 0x64006400u);
+              const uint32_t bhi2 = lop3_and_or(b8, 0x00F000F0u, 0x54005400u);
+              mma16816(c0[mi], alo, blo, ahi, bhi, xf.x, xf.y);
+              mma16816(c1[mi], alo2, blo2, ahi2, bhi2, xf.z, xf.w);
+            }
           }
           // accumulator column 2t + b = (block of lane t, batch b)
           const uint32_t xso = (st * T::CPS + 4 * v) * 8;
-          const float2 fa = __half22float2(u32_as_h2(sza[v])), fb = __half22float2(u32_as_h2(szb[v]));
           const float2 xe0 = lds_f2(xsum0 + xso);
-          acc[0][0][0] += fa.x * ((c0[0] + c1[0]) - fmaf(fa.y, xe0.x, xe0.y));
-          acc[0][0][2] += fb.x * ((c0[2] + c1[2]) - fmaf(fb.y, xe0.x, xe0.y));
-          if (p.B > 1) {
-            const float2 xe1 = lds_f2(xsum1 + xso);
-            acc[0][0][1] += fa.x * ((c0[1] + c1[1]) - fmaf(fa.y, xe1.x, xe1.y));
-            acc[0][0][3] += fb.x * ((c0[3] + c1[3]) - fmaf(fb.y, xe1.x, xe1.y));
+          const float2 xe1 = p.B > 1 ? lds_f2(xsum1 + xso) : make_float2(0.f, 0.f);
+#pragma unroll
+          for (int mi = 0; mi < MPW; ++mi) {
+            const float2 fa = __half22float2(u32_as_h2(sza[mi][v])), fb = __half22float2(u32_as_h2(szb[mi][v]));
+            acc[mi][0][0][0] += fa.x * ((c0[mi][0] + c1[mi][0]) - fmaf(fa.y, xe0.x, xe0.y));
+            acc[mi][0][0][2] += fb.x * ((c0[mi][2] + c1[mi][2]) - fmaf(fb.y, xe0.x, xe0.y));
+            if (p.B > 1) {
+              acc[mi][0][0][1] += fa.x * ((c0[mi][1] + c1[mi][1]) - fmaf(fa.y, xe1.x, xe1.y));
+              acc[mi][0][0][3] += fb.x * ((c0[mi][3] + c1[mi][3]) - fmaf(fb.y, xe1.x, xe1.y));
+            }
           }
         }
       } else {
@@ -482,17 +582,17 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
         // registers), then dequantise and multiply one chunk at a time: only
         // one chunk's fragments are live, which keeps the B > 8 instance
         // (two column groups) out of local memory
-        RowChunk A[V], Bq[V];
+        RowChunk A[VV], Bq[VV];
 #pragma unroll
-        for (int v = 0; v < V; ++v) {
-          A[v].w = lds128(wst + offA[v]);
-          Bq[v].w = lds128(wst + offB[v]);
+        for (int v = 0; v < VV; ++v) {
+          A[v].w = lds128(wst + offA[0][v]);
+          Bq[v].w = lds128(wst + offB[0][v]);
           if constexpr (FMT == W_INT4) {
-            A[v].s = lds32(sst + soffA[v]);
-            Bq[v].s = lds32(sst + soffB[v]);
+            A[v].s = lds32(sst + soffA[0][v]);
+            Bq[v].s = lds32(sst + soffB[0][v]);
           } else if constexpr (FMT == W_INT8) {
-            A[v].s = lds16(sst + soffA[v]);
-            Bq[v].s = lds16(sst + soffB[v]);
+            A[v].s = lds16(sst + soffA[0][v]);
+            Bq[v].s = lds16(sst + soffB[0][v]);
           } else {
             A[v].s = Bq[v].s = 0;
           }
@@ -500,7 +600,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
         __syncwarp();
         if (lane == 0 && ok) mbar_arrive(emp);
 #pragma unroll
-        for (int v = 0; v < V; ++v) {
+        for (int v = 0; v < VV; ++v) {
           uint32_t frag[NM][4];
           chunk_dequant<FMT>(A[v], Bq[v], frag);
           const int off = (st * T::CPS + cidx[v]) * 16;
@@ -510,8 +610,8 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
             for (int sub = 0; sub < NM / 2; ++sub) {
               const uint4 xf = lds128(xrow[cg] + off + sub * xsub);
               const int j = 2 * sub;
-              mma16816(acc[cg][0], frag[j][0], frag[j][1], frag[j][2], frag[j][3], xf.x, xf.y);
-              mma16816(acc[cg][1], frag[j + 1][0], frag[j + 1][1], frag[j + 1][2], frag[j + 1][3], xf.z, xf.w);
+              mma16816(acc[0][cg][0], frag[j][0], frag[j][1], frag[j][2], frag[j][3], xf.x, xf.y);
+              mma16816(acc[0][cg][1], frag[j + 1][0], frag[j + 1][1], frag[j + 1][2], frag[j + 1][3], xf.z, xf.w);
             }
           }
         }
@@ -520,132 +620,146 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
     if constexpr (DIAG) {
       // the 4 lanes of a group hold different blocks: sum them
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        float v = acc[0][0][i];
-        v += __shfl_xor_sync(0xffffffffu, v, 1);
-        v += __shfl_xor_sync(0xffffffffu, v, 2);
-        acc[0][0][i] = v;
-      }
+      for (int mi = 0; mi < MPW; ++mi)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          float v = acc[mi][0][0][i];
+          v += __shfl_xor_sync(0xffffffffu, v, 1);
+          v += __shfl_xor_sync(0xffffffffu, v, 2);
+          acc[mi][0][0][i] = v;
+        }
     } else {
 #pragma unroll
-      for (int cg = 0; cg < NG; ++cg)
+      for (int mi = 0; mi < MPW; ++mi)
 #pragma unroll
-        for (int i = 0; i < 4; ++i) acc[cg][0][i] += acc[cg][1][i];
+        for (int cg = 0; cg < NG; ++cg)
+#pragma unroll
+          for (int i = 0; i < 4; ++i) acc[mi][cg][0][i] += acc[mi][cg][1][i];
     }
 
-    // ---- combine the 4 k-quarter partials of this m-tile (fixed order).
-    // Only the 4 warps of the m-tile synchronise: writers arrive on barrier
-    // 2+mt, the reader waits on it; the reader arrives on 6+mt once red[] is
-    // consumed, which the writers wait for before their next write.
+    // ---- combine the P k-part partials of each m-tile (fixed order).
+    // Only the P warps of an m group synchronise: writers arrive on barrier
+    // 2+mgrp, the reader waits on it; the reader arrives on 6+mgrp once red[]
+    // is consumed, which the writers wait for before their next write.
     ++uidx;
+    constexpr int GT = P * 32;                               // threads of an m group
     if (part != 0) {
-      if (uidx > 1) named_sync(6 + mt, 128);
+      if (uidx > 1) named_sync(6 + mgrp, GT);
 #pragma unroll
-      for (int cg = 0; cg < NG; ++cg)
+      for (int mi = 0; mi < MPW; ++mi)
 #pragma unroll
-        for (int i = 0; i < 4; ++i) red[(((mt * 3 + part - 1) * NG + cg) * 4 + i) * 32 + lane] = acc[cg][0][i];
-      named_arrive(2 + mt, 128);
+        for (int cg = 0; cg < NG; ++cg)
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            red[((((mgrp * MPW + mi) * (P - 1) + part - 1) * NG + cg) * 4 + i) * 32 + lane] = acc[mi][cg][0][i];
+      named_arrive(2 + mgrp, GT);
       continue;
     }
-    named_sync(2 + mt, 128);
-    float r[NG][4];
+    named_sync(2 + mgrp, GT);
+    float r[MPW][NG][4];
 #pragma unroll
-    for (int cg = 0; cg < NG; ++cg)
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        float v = acc[cg][0][i];
-#pragma unroll
-        for (int q = 0; q < 3; ++q) v += red[(((mt * 3 + q) * NG + cg) * 4 + i) * 32 + lane];
-        r[cg][i] = v;
-      }
-    if (more) named_arrive(6 + mt, 128);
-    const int row0 = tile * kTileRows + mt * 16;
-    if (row0 >= p.N) continue;
-    const int row_a = tile * kTileRows + ra, row_b = tile * kTileRows + rb;
-    if (cur.n == 1) {
-#pragma unroll
-      for (int cg = 0; cg < NG; ++cg) {
-        float sq[2] = {0.0f, 0.0f};
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const int c = cg * 8 + 2 * t + h;
-          if (c < p.B && p.npush) {
-            for (int q = 0; q < p.npush; ++q) {
-              if (p.tpx.ll_sig) {
-                tp_push_word(p.y32p[q], (long)c * p.ldy + row_a, ll_tag, r[cg][h]);
-                tp_push_word(p.y32p[q], (long)c * p.ldy + row_b, ll_tag, r[cg][2 + h]);
-              } else {
-                p.y32p[q][(long)c * p.ldy + row_a] = r[cg][h];
-                p.y32p[q][(long)c * p.ldy + row_b] = r[cg][2 + h];
-              }
-            }
-          } else if (c < p.B) {
-            float va = __half2float(__float2half(r[cg][h]));
-            float vb = __half2float(__float2half(r[cg][2 + h]));
-            if (p.res) {
-              va += __half2float(p.res[(long)c * p.ldres + row_a]);
-              vb += __half2float(p.res[(long)c * p.ldres + row_b]);
-            }
-            sq[h] = va * va + vb * vb;
-            p.y[(long)c * p.ldy + row_a] = __float2half(va);
-            p.y[(long)c * p.ldy + row_b] = __float2half(vb);
-          }
-        }
-        if (p.ss_out) {
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            float v = sq[h];
-            v += __shfl_xor_sync(0xffffffffu, v, 4);
-            v += __shfl_xor_sync(0xffffffffu, v, 8);
-            v += __shfl_xor_sync(0xffffffffu, v, 16);
-            const int c = cg * 8 + 2 * t + h;
-            if (g == 0 && c < p.B) p.ss_out[(long)(row0 >> 4) * p.B + c] = v;
-          }
-        }
-      }
-    } else {
-      // split K: store this split's partial for the 16 rows; the warp that
-      // arrives last for this m-tile sums the partials in split order
-      float* prt = p.part + (long)cur.j * p.B * p.N;
+    for (int mi = 0; mi < MPW; ++mi)
 #pragma unroll
       for (int cg = 0; cg < NG; ++cg)
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const int c = cg * 8 + 2 * t + h;
-          if (c < p.B) {
-            prt[(long)c * p.N + row_a] = r[cg][h];
-            prt[(long)c * p.N + row_b] = r[cg][2 + h];
-          }
+        for (int i = 0; i < 4; ++i) {
+          float v = acc[mi][cg][0][i];
+#pragma unroll
+          for (int q = 0; q < P - 1; ++q) v += red[((((mgrp * MPW + mi) * (P - 1) + q) * NG + cg) * 4 + i) * 32 + lane];
+          r[mi][cg][i] = v;
         }
-      __syncwarp();
-      unsigned last = 0;
-      if (lane == 0) {
-        unsigned old;
-        asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(old) : "l"(p.cnt + (row0 >> 4)) : "memory");
-        last = (old == (unsigned)cur.n - 1) ? 1u : 0u;
-      }
-      last = __shfl_sync(0xffffffffu, last, 0);
-      if (last) {
-        const int rr = row0 + (lane & 15);
-        for (int col = 0; col < p.B; ++col) {
-          float v = 0.0f;
-          for (int k2 = 0; k2 < cur.n; ++k2) v += __ldcg(p.part + ((long)k2 * p.B + col) * p.N + rr);
-          if (p.npush) {
-            if (lane < 16)
+    if (more) named_arrive(6 + mgrp, GT);
+#pragma unroll
+    for (int mi = 0; mi < MPW; ++mi) {
+      const int mt = mgrp * MPW + mi;
+      const int row0 = tile * kTileRows + mt * 16;
+      if (row0 >= p.N) continue;
+      const int row_a = tile * kTileRows + ra[mi], row_b = tile * kTileRows + rb[mi];
+      if (cur.n == 1) {
+#pragma unroll
+        for (int cg = 0; cg < NG; ++cg) {
+          float sq[2] = {0.0f, 0.0f};
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const int c = cg * 8 + 2 * t + h;
+            if (c < p.B && p.npush) {
               for (int q = 0; q < p.npush; ++q) {
-                if (p.tpx.ll_sig) tp_push_word(p.y32p[q], (long)col * p.ldy + rr, ll_tag, v);
-                else p.y32p[q][(long)col * p.ldy + rr] = v;
+                if (p.tpx.ll_sig) {
+                  tp_push_word(p.y32p[q], (long)c * p.ldy + row_a, ll_tag, r[mi][cg][h]);
+                  tp_push_word(p.y32p[q], (long)c * p.ldy + row_b, ll_tag, r[mi][cg][2 + h]);
+                } else {
+                  p.y32p[q][(long)c * p.ldy + row_a] = r[mi][cg][h];
+                  p.y32p[q][(long)c * p.ldy + row_b] = r[mi][cg][2 + h];
+                }
               }
-            continue;
+            } else if (c < p.B) {
+              float va = __half2float(__float2half(r[mi][cg][h]));
+              float vb = __half2float(__float2half(r[mi][cg][2 + h]));
+              if (p.res) {
+                va += __half2float(p.res[(long)c * p.ldres + row_a]);
+                vb += __half2float(p.res[(long)c * p.ldres + row_b]);
+              }
+              sq[h] = va * va + vb * vb;
+              p.y[(long)c * p.ldy + row_a] = __float2half(va);
+              p.y[(long)c * p.ldy + row_b] = __float2half(vb);
+            }
           }
-          v = __half2float(__float2half(v));
-          if (p.res) v += __half2float(p.res[(long)col * p.ldres + rr]);
-          if (lane < 16) p.y[(long)col * p.ldy + rr] = __float2half(v);
-          float sq = (lane < 16) ? v * v : 0.0f;
-          sq = warp_sum(sq);
-          if (p.ss_out && lane == 0) p.ss_out[(long)(row0 >> 4) * p.B + col] = sq;
+          if (p.ss_out) {
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              float v = sq[h];
+              v += __shfl_xor_sync(0xffffffffu, v, 4);
+              v += __shfl_xor_sync(0xffffffffu, v, 8);
+              v += __shfl_xor_sync(0xffffffffu, v, 16);
+              const int c = cg * 8 + 2 * t + h;
+              if (g == 0 && c < p.B) p.ss_out[(long)(row0 >> 4) * p.B + c] = v;
+            }
+          }
         }
-        if (lane == 0) p.cnt[row0 >> 4] = 0u;
+      } else {
+        // split K: store this split's partial for the 16 rows; the warp that
+        // arrives last for this m-tile sums the partials in split order
+        float* prt = p.part + (long)cur.j * p.B * p.N;
+#pragma unroll
+        for (int cg = 0; cg < NG; ++cg)
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const int c = cg * 8 + 2 * t + h;
+            if (c < p.B) {
+              prt[(long)c * p.N + row_a] = r[mi][cg][h];
+              prt[(long)c * p.N + row_b] = r[mi][cg][2 + h];
+            }
+          }
+        __syncwarp();
+        unsigned last = 0;
+        if (lane == 0) {
+          unsigned old;
+          asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(old) : "l"(p.cnt + (row0 >> 4)) : "memory");
+          last = (old == (unsigned)cur.n - 1) ? 1u : 0u;
+        }
+        last = __shfl_sync(0xffffffffu, last, 0);
+        if (last) {
+          const int rr = row0 + (lane & 15);
+          for (int col = 0; col < p.B; ++col) {
+            float v = 0.0f;
+            for (int k2 = 0; k2 < cur.n; ++k2) v += __ldcg(p.part + ((long)k2 * p.B + col) * p.N + rr);
+            if (p.npush) {
+              if (lane < 16)
+                for (int q = 0; q < p.npush; ++q) {
+                  if (p.tpx.ll_sig) tp_push_word(p.y32p[q], (long)col * p.ldy + rr, ll_tag, v);
+                  else p.y32p[q][(long)col * p.ldy + rr] = v;
+                }
+              continue;
+            }
+            v = __half2float(__float2half(v));
+            if (p.res) v += __half2float(p.res[(long)col * p.ldres + rr]);
+            if (lane < 16) p.y[(long)col * p.ldy + rr] = __float2half(v);
+            float sq = (lane < 16) ? v * v : 0.0f;
+            sq = warp_sum(sq);
+            if (p.ss_out && lane == 0) p.ss_out[(long)(row0 >> 4) * p.B + col] = sq;
+          }
+          if (lane == 0) p.cnt[row0 >> 4] = 0u;
+        }
       }
     }
   }
@@ -663,6 +777,9 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
 
 // --------------------------------------------------------------- host ----
 static std::atomic<long> g_spin_limit{kSpinLimit};
+#ifdef R4Q_TRACE
+static int g_trace_launch = 0;
+#endif
 long gemv_spin_limit() { return g_spin_limit.load(std::memory_order_relaxed); }
 long gemv_set_spin_limit(long polls) {
   return g_spin_limit.exchange(polls > 0 ? polls : kSpinLimit);
@@ -750,7 +867,7 @@ static TmaPlan plan_tma(int B, int N, int K, size_t ws_bytes) {
   const int tiles = (N + kTileRows - 1) / kTileRows;
   const int nst = (K + T::SK - 1) / T::SK;
   const size_t stage = (size_t)kTileRows * T::CPS * 16 + (size_t)kTileRows * T::SBYTES;
-  const size_t fixed = 1024 + 4 * 3 * NG * 4 * 32 * 4 + 2 * T::NS * 8 + 16;
+  const size_t fixed = 1024 + (size_t)red_floats<NG, DIAG>() * 4 + 2 * T::NS * 8 + 16;
   const size_t smem_limit = tma_smem_limit<FMT, NG, DIAG>();
   TmaPlan best{1, 1, 0, 0, 0, 0};
   double best_cost = 1e30;
@@ -832,9 +949,17 @@ static int launch_tma_t(const GemvArgs& a) {
   tp.xsum_bytes = pl.xsum_bytes;
   tp.ns = pl.ns;
   tp.spin = gemv_spin_limit();
+  {
+    // R4Q_GEMV_PREWAIT=n: request only n stages before the activations are
+    // staged (measurement only; default kPrewait)
+    static const int pw = [] {
+      const char* e = getenv("R4Q_GEMV_PREWAIT");
+      return e ? atoi(e) : -1;
+    }();
+    tp.prewait = pw >= 0 ? pw : kPrewait;
+  }
 #ifdef R4Q_TRACE
-  static int trace_launch = 0;
-  tp.trace_par = (trace_launch++) & 1;
+  tp.trace_par = (g_trace_launch++) & 7;
 #endif
   tp.status = reinterpret_cast<int*>(a.ws);   // header word 0 (null without a workspace)
 
@@ -857,14 +982,18 @@ static int launch_tma_t(const GemvArgs& a) {
 }
 
 #ifdef R4Q_TRACE
-extern "C" int r4q_trace_read(unsigned long long* host) {  // [2][8][256]
+extern "C" int r4q_trace_read(unsigned long long* host) {  // [8][8][256]
   return cudaMemcpyFromSymbol(host, g_trace, sizeof(g_trace)) == cudaSuccess ? 0 : -4;
 }
 extern "C" int r4q_trace_mode(int m) {
   return cudaMemcpyToSymbol(g_dbg_mode, &m, sizeof(int)) == cudaSuccess ? 0 : -4;
 }
+extern "C" int r4q_trace_reset_counter() {
+  g_trace_launch = 0;
+  return 0;
+}
 extern "C" int r4q_trace_clear() {
-  static unsigned long long z[2][8][256];
+  static unsigned long long z[8][8][256];
   return cudaMemcpyToSymbol(g_trace, z, sizeof(g_trace)) == cudaSuccess ? 0 : -4;
 }
 #endif

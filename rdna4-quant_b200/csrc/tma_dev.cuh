@@ -63,6 +63,13 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* b, unsigned parity, int* sta
   return false;
 }
 
+// L2 cache policy for data read exactly once (streamed weights).
+__device__ __forceinline__ uint64_t l2_policy_evict_first() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+
 // Drain wait (producer lane at exit): try_wait lets the hardware suspend the
 // lane between polls, so it takes no issue slots from the consumers.
 __device__ __forceinline__ void mbar_drain(uint64_t* b, unsigned parity, int* status) {
@@ -77,6 +84,15 @@ __device__ __forceinline__ void mbar_drain(uint64_t* b, unsigned parity, int* st
     if (ok) return;
   }
   if (status) atomicExch(status, 1);
+}
+
+__device__ __forceinline__ void tma_load_2d_hint(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar,
+                                                 uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
 }
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y,

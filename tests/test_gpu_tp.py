@@ -145,3 +145,50 @@ def test_tp2_decode_vs_oracle_and_single_gpu(tmp_path, B):
                                   cos, sin, final, lm, write_kv=False)
     close(res[0]['graph_a'], ref, STEP_TOL)
     close(res[0]['graph_a'], res[0]['single'], STEP_TOL)
+
+
+def _nccl_rank(rank, world, port, out_path):
+    """The NCCL all-reduce arm (r4q.tp_nccl) against the fused exchange on the
+    same shards: logits of one token at the decode-step tolerance, and the
+    greedy tokens of a short loop."""
+    from r4q import decode, synth, tp
+    from r4q.tp_nccl import NcclTPDecoder
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev)
+    try:
+        cfg = dict(num_layers=2, hidden=1024, intermediate=2048, num_heads=8, num_kv_heads=2, head_dim=128,
+                   vocab=4096, rms_eps=1e-6, rope_theta=1e6)
+        m = synth.build_decode_model(cfg, dev, seed=5, max_seq=96)
+        synth.fill_kv_synthetic(m, 40, seed=2)
+        sh = tp.shard_decode_model(m, cfg, rank, world)
+        comm = tp.Comm(rank, world, max_batch=1, hidden=cfg['hidden'], vocab=cfg['vocab'])
+        fused = tp.TPDecoder(sh, cfg, comm, batch=1)
+        nccl = NcclTPDecoder(sh, cfg, rank, world, batch=1)
+        h0 = m['embed'][7].reshape(1, -1).contiguous()
+        lf = fused.step(h0, 40, use_graph=False).float().cpu().numpy()
+        nccl.loop(sh['embed'], h0, 40, 1)
+        ln = nccl.lg_all.permute(1, 0, 2).reshape(1, -1).float().cpu().numpy()
+        tf = fused.loop(sh['embed'], h0, 41, 4).cpu().numpy()
+        tn = nccl.loop(sh['embed'], h0, 41, 4).cpu().numpy()
+        torch.cuda.synchronize()
+        comm.status()
+        np.savez(f"{out_path}.{rank}.npz", lf=lf, ln=ln, tf=tf, tn=tn)
+        decode.clear_contexts()
+        del fused, nccl
+        comm.close()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_tp2_nccl_arm_matches_fused_exchange(tmp_path):
+    world = 2
+    mp.spawn(_nccl_rank, args=(world, free_port(), str(tmp_path / "n")), nprocs=world, join=True)
+    res = [np.load(tmp_path / f"n.{r}.npz") for r in range(world)]
+    for r in range(world):
+        close(res[r]['ln'], res[r]['lf'], STEP_TOL)
+        assert np.array_equal(res[r]['tn'], res[0]['tn'])          # replicated tokens
+    assert (res[0]['tn'] == res[0]['tf']).mean() >= 0.75
