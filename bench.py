@@ -83,6 +83,10 @@ def parse():
                     help="run the INT4 tcgen05 prefill GEMM (M=512, qkv shape) 4 times and exit (for ncu)")
     ap.add_argument("--kernel-probe", default=None, choices=[n for n, *_ in LAYER_SHAPES],
                     help="run one GEMV of this shape 4 times and exit (for ncu captures)")
+    ap.add_argument("--probe-fmt", default="int4", choices=["int4", "int8"],
+                    help="weight format of --kernel-probe")
+    ap.add_argument("--attn-probe", default=None,
+                    help="'B,ctx': run the fused decode attention 4 times and exit (for ncu captures)")
     return ap.parse_args()
 
 
@@ -887,14 +891,38 @@ def kernel_probe(a):
     dev = torch.device("cuda", 0)
     name, N, K, pro = next(t for t in LAYER_SHAPES if t[0] == a.kernel_probe)
     g = torch.Generator(device=dev).manual_seed(0)
-    _, w, sc = synth.linear_int4(N, K, g, dev)
+    mk = synth.linear_int8 if a.probe_fmt == "int8" else synth.linear_int4
+    _, w, sc = mk(N, K, g, dev)
     kin = 2 * K if pro == "silu_fwht" else K
     x = torch.randn(a.batch, kin, device=dev, generator=g).half()
     prol = Lb.PRO_SILU_FWHT if pro == "silu_fwht" else Lb.PRO_FWHT
     for _ in range(4):
-        ops.gemv("int4", x, w, sc, N, K, prologue=prol)
+        ops.gemv(a.probe_fmt, x, w, sc, N, K, prologue=prol)
     torch.cuda.synchronize()
-    print(f"probe {name} N={N} K={K} B={a.batch} ok")
+    ops.check_status(dev)
+    print(f"probe {name} {a.probe_fmt} N={N} K={K} B={a.batch} ok")
+
+
+def attn_probe(a):
+    """Config-2 shape: the fused decode attention (head norm + RoPE + FP8 K/V
+    write + split-K attention + FWHT) at (B, ctx), 4 launches, for ncu."""
+    import torch
+    from r4q import ops
+    dev = torch.device("cuda", 0)
+    B, ctx = [int(v) for v in a.attn_probe.split(",")]
+    g = torch.Generator(device=dev).manual_seed(0)
+    kc = ops.fp16_to_fp8(torch.randn(B, NKV, ctx + 8, HD, generator=g, device=dev).half())
+    vc = ops.fp16_to_fp8(torch.randn(B, NKV, ctx + 8, HD, generator=g, device=dev).half())
+    qkv = torch.randn(B, QKV_N, generator=g, device=dev).half()
+    nw = torch.ones(HD, device=dev).half()
+    f = torch.outer(torch.arange(ctx + 16, device=dev).float(), torch.ones(HD // 2, device=dev))
+    cos, sin = f.cos().half(), f.sin().half()
+    seq = torch.full((B,), ctx, dtype=torch.int64, device=dev)
+    for _ in range(4):
+        ops.attn_decode_fused(qkv, kc, vc, nw, nw, cos, sin, NQ, NKV, 0, fwht=True, seq_dev=seq)
+    torch.cuda.synchronize()
+    ops.check_status(dev)
+    print(f"attn probe B={B} ctx={ctx} ok")
 
 
 def decode_probe(a):
@@ -943,6 +971,8 @@ if __name__ == "__main__":
         decode_probe(args)
     elif args.kernel_probe:
         kernel_probe(args)
+    elif args.attn_probe:
+        attn_probe(args)
     elif args.moe_probe:
         moe_probe(args)
     elif args.impl == "reference":

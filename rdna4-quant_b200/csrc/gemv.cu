@@ -459,21 +459,16 @@ int gemv_validate(const GemvArgs& a, int fmt) {
 int launch_gemv(const GemvArgs& a, int fmt) {
   int st = gemv_validate(a, fmt);
   if (st) return st;
-  static const int force_ldg = [] {
+  // The TMA kernel takes every shape it supports (measured on B200 at B =
+  // 1..16 against this file's register-staged kernel, which stays for the
+  // shapes TMA cannot take); the choice depends on the shape only, never on
+  // the output type, so fp16(y32) == y16 holds bit for bit.
+  // R4Q_GEMV_PATH=ldg forces the register-staged kernel (testing only).
+  static const bool force_ldg = [] {
     const char* e = getenv("R4Q_GEMV_PATH");
-    return (e && e[0] == 'l') ? 1 : 0;
+    return e && e[0] == 'l';
   }();
-  // Measured on B200 (INT4, graph replay): above 8 columns the TMA kernel's
-  // two-n-group instance spills (qkv 5120->7168 at B = 16: 75 us against 40
-  // us here), and a wide-K GEMV at B >= 8 must split its staged activations
-  // (down 17408->5120 at B = 8: 75 us against 42 us); wide-N shapes stay on
-  // TMA (gate_up at B = 16: 155 against 175 us).  The choice depends on the
-  // shape only, never on the output type (fp16 or fp32 partials), so that
-  // fp16(y32) == y16 holds bit for bit; only a tensor-parallel consumer
-  // (reduce-on-read prologue) needs the TMA kernel.
-  const bool ldg_better = fmt == W_INT4 && !a.tpx.nwait &&
-                          ((a.B > 8 && a.N <= 8192) || (a.B >= 8 && a.K > 8192));
-  if (!force_ldg && !ldg_better && gemv_tma_supported(a, fmt)) {
+  if (!force_ldg && gemv_tma_supported(a, fmt)) {
     st = launch_gemv_tma(a, fmt);
     if (st != R4Q_ERR_CAPACITY) return st;  // no TMA plan fits: take the LDG kernel
   }

@@ -341,6 +341,68 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
     }
     consumer_sync();
   }
+  if (!p.tpx.nwait) {
+    // One thread per (column, 32-block): the RMSNorm scale first, then each
+    // thread loads its 32 activations (one memory round trip), applies the
+    // prologue and the FWHT in registers (the butterfly order of the
+    // reference, no shuffles) and writes the block into the permuted layout.
+    if (p.prologue == R4Q_PRO_RMSNORM_FWHT) {
+      for (int c = warp; c < ncolx; c += kTmaConsumers) {
+        float ss = 0.0f;
+        if (p.ss_in) {
+          // eight loads in flight per lane, summed in index order
+          for (int i0 = lane; i0 < p.ss_in_parts; i0 += 256) {
+            float tv[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+              tv[u] = (i0 + 32 * u < p.ss_in_parts) ? p.ss_in[(long)(i0 + 32 * u) * ncolx + c] : 0.0f;
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+              if (i0 + 32 * u < p.ss_in_parts) ss += tv[u];
+          }
+        } else {
+          const __half2* xr = reinterpret_cast<const __half2*>(p.x + (long)c * p.ldx);
+          for (int i = lane; i < (p.K >> 1); i += 32) {
+            const float2 f = __half22float2(xr[i]);
+            ss += f.x * f.x + f.y * f.y;
+          }
+        }
+        ss = warp_sum(ss);
+        if (lane == 0) s_rrms[c] = rsqrtf(ss / (float)p.K + p.eps);
+      }
+      consumer_sync();
+      if (ctid == 0) TRACE(6, 0);
+    }
+    const int nblk = nch_pad * F::CK / 32;
+    const int k_base = st0 * T::SK;
+    const int total = ncolx * nblk;
+    for (int item = ctid; item < total; item += kTmaConsumers * 32) {
+      const int col = item / nblk, blk = item - col * nblk;
+      __half v[32];
+      load_block32(p, col, k_base + blk * 32, p.prologue == R4Q_PRO_RMSNORM_FWHT ? s_rrms[col] : 1.0f, v);
+      if constexpr (DIAG) {
+        // block sums of the even and odd k, added in the order of the
+        // 4-lane form: per quarter in k order, then (q0 + q1) + (q2 + q3)
+        float se[4], so[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          se[q] = 0.0f;
+          so[q] = 0.0f;
+#pragma unroll
+          for (int jj = 0; jj < 8; jj += 2) {
+            se[q] += __half2float(v[8 * q + jj]);
+            so[q] += __half2float(v[8 * q + jj + 1]);
+          }
+        }
+        const float e = (se[0] + se[1]) + (se[2] + se[3]);
+        const float o = (so[0] + so[1]) + (so[2] + so[3]);
+        xsum[col * nch_pad + blk] = make_float2(e + o, 1024.0f * e + 64.0f * o);
+      }
+      store_block32<FMT>(xs + (long)col * colstride, nch_pad, blk, v);
+    }
+    if (ctid == 0) TRACE(7, 0);
+    if (ctid < 4) reinterpret_cast<uint32_t*>(zero16)[ctid] = 0u;
+  } else
   {
     // (column, block, quarter) items, round r of thread t = item
     // t + r * 512; the loads of up to kStageBatch rounds are issued before
@@ -366,28 +428,6 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
             if (r == r0 + j) raw_in = tp_raw[r];
         }
         in[j] = stage_load(p, col, k_base + blk * 32, q, valid, tp_one, raw_in);
-      }
-      if (r0 == 0 && !p.tpx.nwait && p.prologue == R4Q_PRO_RMSNORM_FWHT) {
-        // the RMSNorm scale of each column, while the first batch's loads
-        // are in flight (one memory round trip for both)
-        for (int c = warp; c < ncolx; c += kTmaConsumers) {
-          float ss = 0.0f;
-          if (p.ss_in) {
-            for (int i = lane; i < p.ss_in_parts; i += 32) ss += p.ss_in[(long)i * ncolx + c];
-          } else {
-            const __half2* xr = reinterpret_cast<const __half2*>(p.x + (long)c * p.ldx);
-            for (int i = lane; i < (p.K >> 1); i += 32) {
-              const float2 f = __half22float2(xr[i]);
-              ss += f.x * f.x + f.y * f.y;
-            }
-          }
-          ss = warp_sum(ss);
-          if (lane == 0) s_rrms[c] = rsqrtf(ss / (float)p.K + p.eps);
-        }
-        consumer_sync();
-#ifndef R4Q_TRACE_PROBE
-        if (ctid == 0) TRACE(6, 0);
-#endif
       }
 #pragma unroll
       for (int j = 0; j < kStageBatch; ++j) {
@@ -739,24 +779,55 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
         }
         last = __shfl_sync(0xffffffffu, last, 0);
         if (last) {
-          const int rr = row0 + (lane & 15);
-          for (int col = 0; col < p.B; ++col) {
-            float v = 0.0f;
-            for (int k2 = 0; k2 < cur.n; ++k2) v += __ldcg(p.part + ((long)k2 * p.B + col) * p.N + rr);
-            if (p.npush) {
-              if (lane < 16)
+          // lane -> (row lane & 15, columns (lane >> 4) + 2 j): every lane
+          // loads its partials of up to 4 splits at once before summing
+          // them in split order, so the merge costs a few memory round trips
+          // instead of one per (column, split)
+          constexpr int CJ = NG * 4;
+          const int rr = row0 + (lane & 15), ch = lane >> 4;
+          float v[CJ];
+#pragma unroll
+          for (int j = 0; j < CJ; ++j) v[j] = 0.0f;
+          for (int k0 = 0; k0 < cur.n; k0 += 4) {
+            float tv[4][CJ];
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk)
+#pragma unroll
+              for (int j = 0; j < CJ; ++j) {
+                const int c = ch + 2 * j;
+                tv[kk][j] = (k0 + kk < cur.n && c < p.B)
+                                ? __ldcg(p.part + ((long)(k0 + kk) * p.B + c) * p.N + rr) : 0.0f;
+              }
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk)
+              if (k0 + kk < cur.n)
+#pragma unroll
+                for (int j = 0; j < CJ; ++j) v[j] += tv[kk][j];
+          }
+#pragma unroll
+          for (int j = 0; j < CJ; ++j) {
+            const int c = ch + 2 * j;
+            float sq = 0.0f;
+            if (c < p.B) {
+              if (p.npush) {
                 for (int q = 0; q < p.npush; ++q) {
-                  if (p.tpx.ll_sig) tp_push_word(p.y32p[q], (long)col * p.ldy + rr, ll_tag, v);
-                  else p.y32p[q][(long)col * p.ldy + rr] = v;
+                  if (p.tpx.ll_sig) tp_push_word(p.y32p[q], (long)c * p.ldy + rr, ll_tag, v[j]);
+                  else p.y32p[q][(long)c * p.ldy + rr] = v[j];
                 }
-              continue;
+              } else {
+                float o = __half2float(__float2half(v[j]));
+                if (p.res) o += __half2float(p.res[(long)c * p.ldres + rr]);
+                p.y[(long)c * p.ldy + rr] = __float2half(o);
+                sq = o * o;
+              }
             }
-            v = __half2float(__float2half(v));
-            if (p.res) v += __half2float(p.res[(long)col * p.ldres + rr]);
-            if (lane < 16) p.y[(long)col * p.ldy + rr] = __float2half(v);
-            float sq = (lane < 16) ? v * v : 0.0f;
-            sq = warp_sum(sq);
-            if (p.ss_out && lane == 0) p.ss_out[(long)(row0 >> 4) * p.B + col] = sq;
+            if (p.ss_out && !p.npush) {
+              sq += __shfl_xor_sync(0xffffffffu, sq, 1);
+              sq += __shfl_xor_sync(0xffffffffu, sq, 2);
+              sq += __shfl_xor_sync(0xffffffffu, sq, 4);
+              sq += __shfl_xor_sync(0xffffffffu, sq, 8);
+              if ((lane & 15) == 0 && c < p.B) p.ss_out[(long)(row0 >> 4) * p.B + c] = sq;
+            }
           }
           if (lane == 0) p.cnt[row0 >> 4] = 0u;
         }
