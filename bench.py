@@ -46,8 +46,8 @@ LAYER_SHAPES = [  # (name, N, K, prologue)
 ]
 METRIC = "INT4 GEMV HBM GB/s (Qwen3-14B decode-layer GEMV set)"
 # dram__bytes_read.sum + dram__bytes_write.sum of one gate_up launch at B=1
-# (gemv_unit_kernel), from the ncu capture summarised in
-# profiles/gemv_unit_int4_gate_up_b1.md; None until captured
+# (gemv_tma_kernel), from the ncu capture summarised in
+# profiles/gemv_tma_int4_gate_up_b1.md
 TRAFFIC_GATE_UP_B1 = None
 L2_BYTES = 126 * 1024 * 1024
 
@@ -587,7 +587,7 @@ def main_ours(a):
                    "parallelism": f"replicas x{ws}", "timing": "CUDA graph replay, CUDA events"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": TRAFFIC_GATE_UP_B1 if B == 1 else None,
-                     "kernel": "gemv_unit_kernel<INT4> gate_up 5120->34816 (rmsnorm+fwht prologue)",
+                     "kernel": "gemv_tma_kernel<INT4,1,diag> gate_up 5120->34816 (rmsnorm+fwht prologue)",
                      "launch_us": round(k_us, 2), "algorithmic_bytes_per_launch": k_bytes,
                      "peak_source": peak_kind + " (burst copy; of measured)",
                      "step_avg_GBps": round(per_rank / (ms * 1e-3) / 1e9, 1)},

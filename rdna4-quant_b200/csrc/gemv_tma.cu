@@ -24,6 +24,7 @@
 #include <cuda.h>
 
 #include <atomic>
+#include <cstdio>
 #include <cstdlib>
 #include <mutex>
 #include <unordered_map>
@@ -341,7 +342,13 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
     }
     consumer_sync();
   }
+#ifdef R4Q_TRACE_PROBE2
+  for (int rep = 0; rep < 2; ++rep)
+#endif
   if (!p.tpx.nwait) {
+#ifdef R4Q_TRACE_PROBE2
+    if (rep == 1) { consumer_sync(); if (ctid == 0) TRACE(6, 0); }
+#endif
     // One thread per (column, 32-block): the RMSNorm scale first, then each
     // thread loads its 32 activations (one memory round trip), applies the
     // prologue and the FWHT in registers (the butterfly order of the
@@ -371,7 +378,9 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
         if (lane == 0) s_rrms[c] = rsqrtf(ss / (float)p.K + p.eps);
       }
       consumer_sync();
+#ifndef R4Q_TRACE_PROBE2
       if (ctid == 0) TRACE(6, 0);
+#endif
     }
     const int nblk = nch_pad * F::CK / 32;
     const int k_base = st0 * T::SK;
@@ -456,10 +465,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
   // warp owns MPW m-tiles of 16 rows and 1/P of each stage's chunks; with
   // MPW = 2 (block-diagonal path) one activation fragment feeds the MMAs of
   // two m-tiles, halving the shared-memory reads of activations.
-#ifndef R4Q_DIAG_MPW
-#define R4Q_DIAG_MPW 1
-#endif
-  constexpr int MPW = DIAG ? R4Q_DIAG_MPW : 1;              // m-tiles per warp
+  constexpr int MPW = 1;                                    // m-tiles per warp
   constexpr int NGRP = 4 / MPW;                             // m groups per stage
   constexpr int P = kTmaConsumers / NGRP;                   // k parts
   constexpr int SPT = T::CPS / P;                           // chunks per part per row per stage
@@ -930,6 +936,15 @@ static size_t tma_smem_limit() {
   return v;
 }
 
+// R4Q_GEMV_PLAN_LOG=1 prints every candidate plan (measurement only).
+static bool plan_log() {
+  static const bool v = [] {
+    const char* e = getenv("R4Q_GEMV_PLAN_LOG");
+    return e && e[0] == '1';
+  }();
+  return v;
+}
+
 template <int FMT, int NG, bool DIAG>
 static TmaPlan plan_tma(int B, int N, int K, size_t ws_bytes) {
   using T = TmaFmt<FMT>;
@@ -965,12 +980,17 @@ static TmaPlan plan_tma(int B, int N, int K, size_t ws_bytes) {
     // busiest CTA streams rounds * per stages (slower with a shallow ring);
     // S > 1 adds a partial merge per tile
     const double depth_pen = ns < 8 ? (8.0 - ns) * 0.08 : 0.0;
-    const double cost = (double)rounds * per * (1.0 + depth_pen) + (S > 1 ? 1.0 * rounds : 0.0) + 0.02 * S;
+    // (a unit boundary with a split-K merge costs about two stages: measured
+    // on B200 with forced splits at B = 1 and 16)
+    const double cost = (double)rounds * per * (1.0 + depth_pen) + (S > 1 ? 2.0 * rounds : 0.0) + 0.02 * S;
+    if (plan_log()) fprintf(stderr, "r4q plan B=%d N=%d K=%d S=%d gt=%d ns=%d rounds=%d per=%d cost=%.2f\n", B, N, K,
+                            S, gt, ns, rounds, per, cost);
     if (cost < best_cost) {
       best_cost = cost;
       best = TmaPlan{S, gt, fixed + xb + xsb + (size_t)ns * stage, (int)xb, (int)xsb, ns};
     }
   }
+  if (plan_log()) fprintf(stderr, "r4q plan B=%d N=%d K=%d -> S=%d\n", B, N, K, best.S);
   return best;
 }
 

@@ -150,6 +150,10 @@ __device__ __forceinline__ void tp_signal_cta(const TpExchange& x) {
   if (old != gridDim.x * gridDim.y * gridDim.z - 1) return;
   tp_stamp(x, 7, x.sig_idx);
   *x.sig_done = 0u;
+  // the other CTAs' pushes were released to this thread by the counter (gpu
+  // scope); this fence makes them cumulative into the system-scope flag
+  // stores below (one fence per exchange, in the last CTA only)
+  asm volatile("fence.acq_rel.sys;" ::: "memory");
   const unsigned long long e = tp_epoch(x, x.sig_idx);
   for (int q = 0; q < x.nsig; ++q)
     asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(x.sig[q]), "l"(e) : "memory");
