@@ -126,16 +126,18 @@ __host__ __device__ inline int x_colstride(int nsteps, int nsub, int u) {
 
 // ------------------------------------------------------------ prologue ----
 // Loads 32 activations of column `col` starting at k0, applies the prologue
-// and returns them as fp16 in v[0..31].
-__device__ __forceinline__ void load_block32(const GemvParams& p, int col, int k0, float rrms,
-                                             __half (&v)[32]) {
+// PRO (compile-time, so a kernel carries only its own prologue's code) and
+// returns them as fp16 in v[0..31].
+template <int PRO>
+__device__ __forceinline__ void load_block32_t(const GemvParams& p, int col, int k0, float rrms,
+                                               __half (&v)[32]) {
   const __half* xr = p.x + (long)col * p.ldx;
   if (k0 >= p.K) {
 #pragma unroll
     for (int i = 0; i < 32; ++i) v[i] = __float2half(0.0f);
     return;
   }
-  if (p.prologue == R4Q_PRO_NONE) {
+  if constexpr (PRO == R4Q_PRO_NONE) {
     const uint4* src = reinterpret_cast<const uint4*>(xr + k0);
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
@@ -143,47 +145,56 @@ __device__ __forceinline__ void load_block32(const GemvParams& p, int col, int k
       *reinterpret_cast<uint4*>(&v[8 * i]) = q;
     }
     return;
-  }
-  float f[32];
-  if (p.prologue == R4Q_PRO_RMSNORM_FWHT) {
-    // fp16(x) * rrms * w, then H32 (fused_res_norm_fwht phase 2, hip:1178-1190)
-    const uint4* src = reinterpret_cast<const uint4*>(xr + k0);
-    const uint4* ws = reinterpret_cast<const uint4*>(p.norm_w + k0);
+  } else {
+    float f[32];
+    if constexpr (PRO == R4Q_PRO_RMSNORM_FWHT) {
+      // fp16(x) * rrms * w, then H32 (fused_res_norm_fwht phase 2, hip:1178-1190)
+      const uint4* src = reinterpret_cast<const uint4*>(xr + k0);
+      const uint4* ws = reinterpret_cast<const uint4*>(p.norm_w + k0);
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      uint4 q = src[i], wq = __ldg(ws + i);
-      const __half* h = reinterpret_cast<const __half*>(&q);
-      const __half* wh = reinterpret_cast<const __half*>(&wq);
+      for (int i = 0; i < 4; ++i) {
+        uint4 q = src[i], wq = __ldg(ws + i);
+        const __half* h = reinterpret_cast<const __half*>(&q);
+        const __half* wh = reinterpret_cast<const __half*>(&wq);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) f[8 * i + j] = __half2float(h[j]) * rrms * __half2float(wh[j]);
-    }
-  } else if (p.prologue == R4Q_PRO_FWHT) {
-    const uint4* src = reinterpret_cast<const uint4*>(xr + k0);
+        for (int j = 0; j < 8; ++j) f[8 * i + j] = __half2float(h[j]) * rrms * __half2float(wh[j]);
+      }
+    } else if constexpr (PRO == R4Q_PRO_FWHT) {
+      const uint4* src = reinterpret_cast<const uint4*>(xr + k0);
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      uint4 q = src[i];
-      const __half* h = reinterpret_cast<const __half*>(&q);
+      for (int i = 0; i < 4; ++i) {
+        uint4 q = src[i];
+        const __half* h = reinterpret_cast<const __half*>(&q);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) f[8 * i + j] = __half2float(h[j]);
-    }
-  } else {  // R4Q_PRO_SILU_FWHT: g = x[:, k], u = x[:, K + k]   (hip:1031-1051)
-    const uint4* sg = reinterpret_cast<const uint4*>(xr + k0);
-    const uint4* su = reinterpret_cast<const uint4*>(xr + p.K + k0);
+        for (int j = 0; j < 8; ++j) f[8 * i + j] = __half2float(h[j]);
+      }
+    } else {  // R4Q_PRO_SILU_FWHT: g = x[:, k], u = x[:, K + k]   (hip:1031-1051)
+      const uint4* sg = reinterpret_cast<const uint4*>(xr + k0);
+      const uint4* su = reinterpret_cast<const uint4*>(xr + p.K + k0);
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      uint4 qg = sg[i], qu = su[i];
-      const __half* hg = reinterpret_cast<const __half*>(&qg);
-      const __half* hu = reinterpret_cast<const __half*>(&qu);
+      for (int i = 0; i < 4; ++i) {
+        uint4 qg = sg[i], qu = su[i];
+        const __half* hg = reinterpret_cast<const __half*>(&qg);
+        const __half* hu = reinterpret_cast<const __half*>(&qu);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        float g = __half2float(hg[j]);
-        f[8 * i + j] = g / (1.0f + expf(-g)) * __half2float(hu[j]);
+        for (int j = 0; j < 8; ++j) f[8 * i + j] = silu_f(__half2float(hg[j])) * __half2float(hu[j]);
       }
     }
-  }
-  fwht32_regs(f);
+    fwht32_regs(f);
 #pragma unroll
-  for (int i = 0; i < 32; ++i) v[i] = __float2half(f[i]);
+    for (int i = 0; i < 32; ++i) v[i] = __float2half(f[i]);
+  }
+}
+
+// Runtime-prologue form (the register-staged kernel).
+__device__ __forceinline__ void load_block32(const GemvParams& p, int col, int k0, float rrms,
+                                             __half (&v)[32]) {
+  switch (p.prologue) {
+    case R4Q_PRO_FWHT: load_block32_t<R4Q_PRO_FWHT>(p, col, k0, rrms, v); return;
+    case R4Q_PRO_SILU_FWHT: load_block32_t<R4Q_PRO_SILU_FWHT>(p, col, k0, rrms, v); return;
+    case R4Q_PRO_RMSNORM_FWHT: load_block32_t<R4Q_PRO_RMSNORM_FWHT>(p, col, k0, rrms, v); return;
+    default: load_block32_t<R4Q_PRO_NONE>(p, col, k0, rrms, v); return;
+  }
 }
 
 // Writes one 32-block of activations into the permuted shared layout.
@@ -361,8 +372,7 @@ __device__ __forceinline__ void stage_finish(const GemvParams& p, const QuadIn& 
         const __half* hu = reinterpret_cast<const __half*>(&in.b);
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-          const float g = __half2float(h[j]);
-          f[j] = g / (1.0f + expf(-g)) * __half2float(hu[j]);
+          f[j] = silu_f(__half2float(h[j])) * __half2float(hu[j]);
         }
       } else if (p.prologue == R4Q_PRO_RMSNORM_FWHT) {
         const __half* hw = reinterpret_cast<const __half*>(&in.w);

@@ -115,7 +115,11 @@ struct SegIter {
 // 64 + q for odd k: one LOP3 per pair, no subtract, no scale multiply) and the
 // bias, zero point and scale are applied once per block in fp32:
 //   sum_k (q - z) x = C - (1024 X_even + 64 X_odd) - z X,  times s.
-template <int FMT, int NG, bool DIAG>
+// PRO (the activation prologue) and TPC (tensor-parallel consumer: the
+// prologue reads the exchange slots) are compile-time so that each instance
+// carries only the code it runs: the kernel's once-per-CTA paths (staging,
+// epilogue) are otherwise large enough to stall warps on instruction fetch.
+template <int FMT, int NG, bool DIAG, int PRO, bool TPC>
 __global__ void __launch_bounds__(kTmaThreads, 1)
     gemv_tma_kernel(const __grid_constant__ CUtensorMap tmw, const __grid_constant__ CUtensorMap tms,
                     const TmaParams tp) {
@@ -223,16 +227,6 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
   // everything below may read outputs of the previous kernel in the stream
   asm volatile("griddepcontrol.wait;" ::: "memory");
   if (tid == 0) TRACE(1, 0);
-#ifdef R4Q_TRACE_PROBE
-  // latency probe: two dependent loads of the activations (event 6, 7)
-  if (tid == 0) {
-    volatile const unsigned short* xv = reinterpret_cast<volatile const unsigned short*>(p.x);
-    unsigned short a = xv[0];
-    TRACE(6, (int)a);
-    unsigned short b = xv[64 + (a & 1)];
-    TRACE(7, (int)b);
-  }
-#endif
   const int ctid = tid;  // 0 .. kTmaConsumers*32-1
   const int ncolx = p.B;
   const int nch_pad = nst * T::CPS;
@@ -246,10 +240,10 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
   // per thread: read the exchange buffer once (see below)
   const int tp_nblk = nch_pad * F::CK / 32;
   const int tp_items = ncolx * tp_nblk * 4;
-  const bool tp_one = p.tpx.nwait && DIAG && st0 == 0 && nst == tp.nstages &&
+  const bool tp_one = TPC && DIAG && st0 == 0 && nst == tp.nstages &&
                       tp_items <= kTmaConsumers * 32 * kTpPre;
   uint4 tp_raw[kTpPre];
-  if (p.tpx.nwait) {
+  if constexpr (TPC) {
     // tensor-parallel consumer: wait for every rank's partials, then r and
     // its sum of squares straight from the exchange buffer (CTA 0 stores r)
     if (stamp) tp_stamp(p.tpx, 2, p.tpx.wait_idx);
@@ -342,18 +336,12 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
     }
     consumer_sync();
   }
-#ifdef R4Q_TRACE_PROBE2
-  for (int rep = 0; rep < 2; ++rep)
-#endif
-  if (!p.tpx.nwait) {
-#ifdef R4Q_TRACE_PROBE2
-    if (rep == 1) { consumer_sync(); if (ctid == 0) TRACE(6, 0); }
-#endif
+  if constexpr (!TPC) {
     // One thread per (column, 32-block): the RMSNorm scale first, then each
     // thread loads its 32 activations (one memory round trip), applies the
     // prologue and the FWHT in registers (the butterfly order of the
     // reference, no shuffles) and writes the block into the permuted layout.
-    if (p.prologue == R4Q_PRO_RMSNORM_FWHT) {
+    if constexpr (PRO == R4Q_PRO_RMSNORM_FWHT) {
       for (int c = warp; c < ncolx; c += kTmaConsumers) {
         float ss = 0.0f;
         if (p.ss_in) {
@@ -378,9 +366,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
         if (lane == 0) s_rrms[c] = rsqrtf(ss / (float)p.K + p.eps);
       }
       consumer_sync();
-#ifndef R4Q_TRACE_PROBE2
       if (ctid == 0) TRACE(6, 0);
-#endif
     }
     const int nblk = nch_pad * F::CK / 32;
     const int k_base = st0 * T::SK;
@@ -388,7 +374,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
     for (int item = ctid; item < total; item += kTmaConsumers * 32) {
       const int col = item / nblk, blk = item - col * nblk;
       __half v[32];
-      load_block32(p, col, k_base + blk * 32, p.prologue == R4Q_PRO_RMSNORM_FWHT ? s_rrms[col] : 1.0f, v);
+      load_block32_t<PRO>(p, col, k_base + blk * 32, PRO == R4Q_PRO_RMSNORM_FWHT ? s_rrms[col] : 1.0f, v);
       if constexpr (DIAG) {
         // block sums of the even and odd k, added in the order of the
         // 4-lane form: per quarter in k order, then (q0 + q1) + (q2 + q3)
@@ -450,9 +436,6 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
                                 p.prologue == R4Q_PRO_RMSNORM_FWHT ? s_rrms[col] : 1.0f,
                                 xs + (long)col * colstride, nch_pad, blk, valid, xsum + col * nch_pad + blk);
       }
-#ifndef R4Q_TRACE_PROBE
-      if (ctid == 0 && r0 == 0) TRACE(7, 0);
-#endif
     }
     if (ctid < 4) reinterpret_cast<uint32_t*>(zero16)[ctid] = 0u;
   }
@@ -912,7 +895,7 @@ struct TmaPlan {
 
 // Largest dynamic shared memory this kernel may use: the per-block opt-in
 // limit minus its static shared memory.  Sets the attribute once per device.
-template <int FMT, int NG, bool DIAG>
+template <int FMT, int NG, bool DIAG, int PRO, bool TPC>
 static size_t tma_smem_limit() {
   static std::mutex mu;
   static std::unordered_map<int, size_t> lim;
@@ -925,9 +908,9 @@ static size_t tma_smem_limit() {
   cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
   cudaFuncAttributes fa{};
   size_t v = 0;
-  if (optin > 0 && cudaFuncGetAttributes(&fa, gemv_tma_kernel<FMT, NG, DIAG>) == cudaSuccess) {
+  if (optin > 0 && cudaFuncGetAttributes(&fa, gemv_tma_kernel<FMT, NG, DIAG, PRO, TPC>) == cudaSuccess) {
     v = (size_t)optin - fa.sharedSizeBytes;
-    if (cudaFuncSetAttribute(gemv_tma_kernel<FMT, NG, DIAG>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    if (cudaFuncSetAttribute(gemv_tma_kernel<FMT, NG, DIAG, PRO, TPC>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)v) != cudaSuccess)
       v = 0;
   }
@@ -945,7 +928,7 @@ static bool plan_log() {
   return v;
 }
 
-template <int FMT, int NG, bool DIAG>
+template <int FMT, int NG, bool DIAG, int PRO, bool TPC>
 static TmaPlan plan_tma(int B, int N, int K, size_t ws_bytes) {
   using T = TmaFmt<FMT>;
   using F = Fmt<FMT>;
@@ -954,7 +937,7 @@ static TmaPlan plan_tma(int B, int N, int K, size_t ws_bytes) {
   const int nst = (K + T::SK - 1) / T::SK;
   const size_t stage = (size_t)kTileRows * T::CPS * 16 + (size_t)kTileRows * T::SBYTES;
   const size_t fixed = 1024 + (size_t)red_floats<NG, DIAG>() * 4 + 2 * T::NS * 8 + 16;
-  const size_t smem_limit = tma_smem_limit<FMT, NG, DIAG>();
+  const size_t smem_limit = tma_smem_limit<FMT, NG, DIAG, PRO, TPC>();
   TmaPlan best{1, 1, 0, 0, 0, 0};
   double best_cost = 1e30;
   // R4Q_GEMV_SPLIT forces the K split count (measurement only)
@@ -994,10 +977,10 @@ static TmaPlan plan_tma(int B, int N, int K, size_t ws_bytes) {
   return best;
 }
 
-template <int FMT, int NG, bool DIAG>
+template <int FMT, int NG, bool DIAG, int PRO, bool TPC>
 static int launch_tma_t(const GemvArgs& a) {
   using T = TmaFmt<FMT>;
-  const TmaPlan pl = plan_tma<FMT, NG, DIAG>(a.B, a.N, a.K, a.ws_bytes);
+  const TmaPlan pl = plan_tma<FMT, NG, DIAG, PRO, TPC>(a.B, a.N, a.K, a.ws_bytes);
   if (pl.smem == 0) return set_error(R4Q_ERR_CAPACITY, "gemv: no TMA plan fits shared memory");
   if (pl.S > 1 && !a.ws) return set_error(R4Q_ERR_CAPACITY, "gemv: workspace required");
   CUtensorMap tmw, tms;
@@ -1064,7 +1047,7 @@ static int launch_tma_t(const GemvArgs& a) {
   attrs[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attrs;
   cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, gemv_tma_kernel<FMT, NG, DIAG>, tmw, tms, tp);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, gemv_tma_kernel<FMT, NG, DIAG, PRO, TPC>, tmw, tms, tp);
   if (e != cudaSuccess) {
     cudaGetLastError();
     return set_error(R4Q_ERR_CUDA, "gemv_tma_kernel (smem %zu): %s", pl.smem, cudaGetErrorString(e));
@@ -1089,14 +1072,31 @@ extern "C" int r4q_trace_clear() {
 }
 #endif
 
+// Instance per (format, column groups, block-diagonal) x (prologue) and the
+// tensor-parallel consumer (always an RMSNorm+FWHT prologue).
+template <int FMT, int NG, bool DIAG>
+static int launch_tma_pro(const GemvArgs& a) {
+  if (a.tpx.nwait) {
+    if (a.prologue != R4Q_PRO_RMSNORM_FWHT)
+      return set_error(R4Q_ERR_ARG, "gemv: a tensor-parallel consumer needs the RMSNorm+FWHT prologue");
+    return launch_tma_t<FMT, NG, DIAG, R4Q_PRO_RMSNORM_FWHT, true>(a);
+  }
+  switch (a.prologue) {
+    case R4Q_PRO_FWHT: return launch_tma_t<FMT, NG, DIAG, R4Q_PRO_FWHT, false>(a);
+    case R4Q_PRO_SILU_FWHT: return launch_tma_t<FMT, NG, DIAG, R4Q_PRO_SILU_FWHT, false>(a);
+    case R4Q_PRO_RMSNORM_FWHT: return launch_tma_t<FMT, NG, DIAG, R4Q_PRO_RMSNORM_FWHT, false>(a);
+    default: return launch_tma_t<FMT, NG, DIAG, R4Q_PRO_NONE, false>(a);
+  }
+}
+
 int launch_gemv_tma(const GemvArgs& a, int fmt) {
   const bool two = a.B > 8;
   switch (fmt) {
     case W_INT4:
-      if (a.B <= 2) return launch_tma_t<W_INT4, 1, true>(a);
-      return two ? launch_tma_t<W_INT4, 2, false>(a) : launch_tma_t<W_INT4, 1, false>(a);
-    case W_INT8: return two ? launch_tma_t<W_INT8, 2, false>(a) : launch_tma_t<W_INT8, 1, false>(a);
-    case W_FP16: return two ? launch_tma_t<W_FP16, 2, false>(a) : launch_tma_t<W_FP16, 1, false>(a);
+      if (a.B <= 2) return launch_tma_pro<W_INT4, 1, true>(a);
+      return two ? launch_tma_pro<W_INT4, 2, false>(a) : launch_tma_pro<W_INT4, 1, false>(a);
+    case W_INT8: return two ? launch_tma_pro<W_INT8, 2, false>(a) : launch_tma_pro<W_INT8, 1, false>(a);
+    case W_FP16: return two ? launch_tma_pro<W_FP16, 2, false>(a) : launch_tma_pro<W_FP16, 1, false>(a);
   }
   return set_error(R4Q_ERR_ARG, "gemv: unknown weight format %d", fmt);
 }
