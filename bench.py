@@ -599,12 +599,14 @@ def main_ours(a):
         "gpu_launches": nlaunch * a.steps,
         "clocks": clk.summary(),
     }
-    if not a.no_extra:
+    # single-GPU sections (the multi-GPU run reports the headline as replicas
+    # and the sharded decode / MoE below)
+    if not a.no_extra and ws == 1:
         line["cfg0"] = cfg0_line(dev, peak)
         line["gemv_shapes"] = shape_table(layers, dev, peak, Lpro)
-    if a.gemv_batches and not a.no_extra:
+    if a.gemv_batches and not a.no_extra and ws == 1:
         line["gemv_batches"] = gemv_set_batches(a, dev, layers, peak, Lpro, ws)
-    if a.attn_grid and not a.no_extra:
+    if a.attn_grid and not a.no_extra and ws == 1:
         torch.cuda.empty_cache()
         line["attention"] = attention_grid(a, dev, peak)
     if a.decode_ctx and not a.no_extra:
