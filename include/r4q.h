@@ -332,6 +332,16 @@ void r4q_decode_ctx_destroy(r4q_decode_ctx* ctx);
 int r4q_decode_step(r4q_decode_ctx* ctx, const void* hidden_in, int pos, void* hidden_out,
                     void* logits_out, int use_graph, void* stream);
 
+/* r4q_decode_step with a position per row (host int array [batch]): row b's
+ * token is decoded at pos[b], its K/V written there and its attention runs
+ * over [0, pos[b]], so each row can be a different request of a continuously
+ * batched server (r4q/serve.py).  Same graph as r4q_decode_step (positions
+ * are device values).  The reference serialises requests behind one lock and
+ * decodes one sequence at a time (api_server.py:40, 58-150); this entry
+ * point has no direct counterpart there. */
+int r4q_decode_step_rows(r4q_decode_ctx* ctx, const void* hidden_in, const int* pos, void* hidden_out,
+                         void* logits_out, int use_graph, void* stream);
+
 /* Greedy decode of num_tokens tokens entirely on the device: token t runs the
  * step at position start_pos + t with logits, takes the argmax (first maximum,
  * NaN skipped) and feeds the embedding row of that token (embed fp16
@@ -364,8 +374,10 @@ int r4q_decode_tp_trace(r4q_decode_ctx* ctx, unsigned long long* host);
 int r4q_decode_status(r4q_decode_ctx* ctx, int clear);
 
 /* ------------------------------------------- tensor-parallel exchange --- */
-/* One comm per rank, one process per GPU.  It replaces the torch.distributed
- * all_reduce the reference's TP path runs between per-layer GEMVs: each rank
+/* One comm per rank, one process per GPU.  The reference runs on one GPU and
+ * has no collectives; this is the all-reduce of a Megatron-style tensor-
+ * parallel split between the per-layer GEMVs (an NCCL all_reduce arm of the
+ * same step lives in r4q/tp_nccl.py for comparison): each rank
  * owns a peer-visible buffer, producers push fp32 partials straight into the
  * peers' buffers over NVLink and a sync kernel (signal, bounded wait, reduce in
  * rank order) finishes the exchange.  Set-up: r4q_comm_create on every rank,

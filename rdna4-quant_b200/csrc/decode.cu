@@ -560,6 +560,18 @@ static int run_kind(r4q_decode_ctx* c, int kind, bool use_graph, cudaStream_t st
   return R4Q_OK;
 }
 
+// Per-row positions (continuous batching: each row is its own sequence).
+struct RowPositions {
+  int p[16];
+};
+__global__ void set_positions_rows(long long* pos, long long* seq, int B, RowPositions rp) {
+  const int i = threadIdx.x;
+  if (i < B) {
+    pos[i] = rp.p[i];
+    seq[i] = rp.p[i] + 1;
+  }
+}
+
 static int set_pos(r4q_decode_ctx* c, int pos, cudaStream_t st) {
   set_positions<<<1, 32, 0, st>>>(c->pos_dev, c->seq_dev, c->m.batch, pos);
   return check_launch("set_positions");
@@ -588,6 +600,38 @@ extern "C" int r4q_decode_step(r4q_decode_ctx* c, const void* hidden_in, int pos
     e = cudaMemcpyAsync(logits_out, c->logits, (size_t)B * c->m.lm_n * c->m.tp_size * 2,
                         cudaMemcpyDeviceToDevice, st);
     if (e != cudaSuccess) return set_error(R4Q_ERR_CUDA, "decode_step: copy logits: %s", cudaGetErrorString(e));
+  }
+  return R4Q_OK;
+}
+
+extern "C" int r4q_decode_step_rows(r4q_decode_ctx* c, const void* hidden_in, const int* pos,
+                                    void* hidden_out, void* logits_out, int use_graph, void* stream) {
+  if (!c || !hidden_in || !pos) return set_error(R4Q_ERR_ARG, "decode_step_rows: null argument");
+  const int B = c->m.batch, D = c->m.hidden;
+  RowPositions rp{};
+  for (int b = 0; b < B; ++b) {
+    if (pos[b] < 0 || pos[b] >= c->m.max_seq)
+      return set_error(R4Q_ERR_CAPACITY, "decode_step_rows: row %d pos %d outside the KV cache (max_seq %d)", b,
+                       pos[b], c->m.max_seq);
+    rp.p[b] = pos[b];
+  }
+  cudaStream_t st = (cudaStream_t)stream;
+  cudaError_t e = cudaMemcpyAsync(c->h_in, hidden_in, (size_t)B * D * 2, cudaMemcpyDeviceToDevice, st);
+  if (e != cudaSuccess) return set_error(R4Q_ERR_CUDA, "decode_step_rows: copy in: %s", cudaGetErrorString(e));
+  set_positions_rows<<<1, 32, 0, st>>>(c->pos_dev, c->seq_dev, B, rp);
+  int rc = check_launch("set_positions_rows");
+  if (!rc) rc = run_kind(c, logits_out ? 1 : 0, use_graph != 0, st);
+  if (rc) return rc;
+  const __half* hfinal = c->m.num_layers > 0 ? c->h : c->h_in;
+  if (hidden_out) {
+    e = cudaMemcpyAsync(hidden_out, hfinal, (size_t)B * D * 2, cudaMemcpyDeviceToDevice, st);
+    if (e != cudaSuccess) return set_error(R4Q_ERR_CUDA, "decode_step_rows: copy out: %s", cudaGetErrorString(e));
+  }
+  if (logits_out) {
+    e = cudaMemcpyAsync(logits_out, c->logits, (size_t)B * c->m.lm_n * c->m.tp_size * 2,
+                        cudaMemcpyDeviceToDevice, st);
+    if (e != cudaSuccess)
+      return set_error(R4Q_ERR_CUDA, "decode_step_rows: copy logits: %s", cudaGetErrorString(e));
   }
   return R4Q_OK;
 }

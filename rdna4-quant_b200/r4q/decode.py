@@ -42,6 +42,17 @@ class DecodeContext:
                None if logits_out is None else logits_out.data_ptr(), 1 if use_graph else 0,
                ops.stream_handle(dev))
 
+    def step_rows(self, hidden_in, positions, hidden_out=None, logits_out=None, use_graph=True):
+        """One step with a position per row (r4q_decode_step_rows)."""
+        B = self.model.batch
+        if len(positions) != B:
+            raise ValueError(f"{len(positions)} positions for a batch of {B}")
+        pos = (C.c_int * B)(*[int(p) for p in positions])
+        L.call("r4q_decode_step_rows", self.handle, hidden_in.data_ptr(), pos,
+               None if hidden_out is None else hidden_out.data_ptr(),
+               None if logits_out is None else logits_out.data_ptr(), 1 if use_graph else 0,
+               ops.stream_handle(hidden_in.device))
+
     def loop(self, embed, hidden_first, start_pos, num_tokens, use_graph=True):
         """Greedy tokens [num_tokens, batch] int64 on the device (r4q_decode_loop)."""
         dev = hidden_first.device

@@ -102,6 +102,7 @@ _SIGS = {
     "r4q_decode_ctx_create": (i32, [C.POINTER(ModelDesc), C.POINTER(LayerDesc), C.POINTER(C.c_void_p)]),
     "r4q_decode_ctx_destroy": (None, [vp]),
     "r4q_decode_step": (i32, [vp, vp, i32, vp, vp, i32, vp]),
+    "r4q_decode_step_rows": (i32, [vp, vp, vp, vp, vp, i32, vp]),
     "r4q_decode_tp_trace": (i32, [vp, vp]),
     "r4q_decode_loop": (i32, [vp, vp, vp, i32, i32, vp, i32, vp]),
     "r4q_decode_profile": (i32, [vp, vp, i32, vp, vp]),

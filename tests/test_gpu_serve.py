@@ -1,0 +1,133 @@
+"""GPU parity of the continuously batched server (r4q.serve) and of the
+per-row-position decode step (r4q_decode_step_rows) it runs on.
+
+* step_rows with every row at one position is bit-equal to r4q_decode_step;
+* a batched run of several greedy requests (more requests than slots, prompts
+  of different lengths, so rows sit at different positions and slots are
+  reused) gives every request the logits it gets when served alone through
+  the B = 1 path (prefill into a private cache + decode_step), fed the same
+  tokens, within the decode-step tolerance (2e-3 relative, max-norm and L2:
+  B = 1 and B = 4 take different GEMV instances whose fp32 sums round apart);
+* the tokens are the argmax of those logits."""
+import numpy as np
+import pytest
+import torch
+
+from test_gpu_gemv import close
+
+pytestmark = pytest.mark.gpu
+STEP_TOL = 2e-3
+CFG = dict(num_layers=2, hidden=512, intermediate=1024, num_heads=4, num_kv_heads=2, head_dim=128,
+           vocab=1008, rms_eps=1e-6, rope_theta=1e6)
+MAXS = 48
+
+
+def _model(batch, seed=7):
+    from r4q import synth
+    return synth.build_decode_model(CFG, torch.device("cuda", 0), seed=seed, max_seq=MAXS, batch=batch)
+
+
+def _with_caches(m, batch):
+    """The same weights with fresh KV caches of another batch size."""
+    out = dict(m)
+    out['k_caches'] = [torch.zeros(batch, *k.shape[1:], dtype=k.dtype, device=k.device) for k in m['k_caches']]
+    out['v_caches'] = [torch.zeros(batch, *v.shape[1:], dtype=v.dtype, device=v.device) for v in m['v_caches']]
+    return out
+
+
+def test_step_rows_equal_positions_matches_decode_step():
+    from r4q import decode, serve, synth
+    m = _model(3)
+    synth.fill_kv_synthetic(m, 20, seed=2)
+    be = serve.SlotBackend(m, CFG, batch=3)
+    h = (torch.randn(3, CFG['hidden'], device='cuda', generator=torch.Generator('cuda').manual_seed(1)) * 0.5).half()
+    a = torch.empty(3, CFG['vocab'], dtype=torch.float16, device='cuda')
+    b = torch.empty_like(a)
+    kc0 = [k.clone() for k in m['k_caches']]
+    be.ctx.step(h, 20, logits_out=a)
+    ka = [k.clone() for k in m['k_caches']]
+    for k, k0 in zip(m['k_caches'], kc0):
+        k.copy_(k0)
+    be.ctx.step_rows(h, [20, 20, 20], logits_out=b)
+    torch.cuda.synchronize()
+    assert torch.equal(a, b)
+    for k, k2 in zip(ka, m['k_caches']):
+        assert torch.equal(k, k2)
+    # one row at a different position changes only that row's cache column
+    be.ctx.step_rows(h, [20, 7, 20], logits_out=b)
+    torch.cuda.synchronize()
+    assert torch.equal(a[0], b[0]) and torch.equal(a[2], b[2])
+    with pytest.raises(Exception):
+        be.ctx.step_rows(h, [20, MAXS, 1], logits_out=b)
+    decode.clear_contexts()
+
+
+class RecordingBackend:
+    """Wraps a SlotBackend and keeps, per request, the logits rows it produced."""
+
+    def __init__(self, be):
+        self.be = be
+        self.batch, self.max_seq, self.logits = be.batch, be.max_seq, be.logits
+        self.eng = None
+        self.seen = {}
+
+    def prefill(self, slot, prompt):
+        lg = self.be.prefill(slot, prompt)
+        self.seen.setdefault(self.eng.slots[slot].id, []).append(lg.float().cpu())
+        return lg
+
+    def step(self, tokens, positions):
+        lg = self.be.step(tokens, positions)
+        for s, r in enumerate(self.eng.slots):
+            if r is not None:
+                self.seen[r.id].append(lg[s].float().cpu())
+        return lg
+
+
+def test_batched_requests_match_each_request_alone():
+    from r4q import decode, serve
+    from r4q import prefill as P
+    m4 = _model(4)
+    rec = RecordingBackend(serve.SlotBackend(m4, CFG, batch=4))
+    eng = serve.BatchedEngine(rec)
+    rec.eng = eng
+    rng = np.random.default_rng(4)
+    prompts = [rng.integers(0, CFG['vocab'], size=n).tolist() for n in (5, 9, 3, 12, 7, 4)]
+    lens = [6, 4, 9, 5, 7, 3]
+    reqs = [eng.submit(p, max_new_tokens=n) for p, n in zip(prompts, lens)]
+    eng.run()
+    assert all(r.finish_reason == "length" and len(r.tokens) == n for r, n in zip(reqs, lens))
+
+    # each request alone: B = 1 caches, prefill + decode_step fed the same tokens
+    m1 = _with_caches(m4, 1)
+    c = CFG
+    ctx = decode.get_context(m1['qkv_w'], m1['qkv_s'], m1['o_w'], m1['o_s'], m1['gu_w'], m1['gu_s'],
+                             m1['down_w'], m1['down_s'], m1['in_norm_w'], m1['post_norm_w'], m1['q_norm_w'],
+                             m1['k_norm_w'], m1['rope_cos'], m1['rope_sin'], c['num_heads'], c['num_kv_heads'],
+                             c['head_dim'], c['hidden'], c['intermediate'], c['rms_eps'], m1['k_caches'],
+                             m1['v_caches'], m1['final_norm_w'], m1['lm_w'], m1['lm_s'], c['vocab'], batch=1)
+    out = torch.empty(1, c['vocab'], dtype=torch.float16, device='cuda')
+    for r, p in zip(reqs, prompts):
+        for k in (*m1['k_caches'], *m1['v_caches']):
+            k.zero_()
+        ids = torch.tensor(p, device='cuda')
+        lg = P.prefill_logits(m1['embed'][ids], m1['qkv_w'], m1['qkv_s'], m1['o_w'], m1['o_s'], m1['gu_w'],
+                              m1['gu_s'], m1['down_w'], m1['down_s'], m1['in_norm_w'], m1['post_norm_w'],
+                              m1['q_norm_w'], m1['k_norm_w'], m1['rope_cos'], m1['rope_sin'], c['num_heads'],
+                              c['num_kv_heads'], c['head_dim'], c['hidden'], c['intermediate'], c['rms_eps'],
+                              m1['final_norm_w'], m1['lm_w'], m1['lm_s'], c['vocab'], k_caches=m1['k_caches'],
+                              v_caches=m1['v_caches'], batch_row=0, last_only=True)
+        alone = [lg.reshape(-1).float().cpu()]
+        for t, tok in enumerate(r.tokens[:-1]):
+            h = m1['embed'][tok].reshape(1, -1).contiguous()
+            ctx.step(h, len(p) + t, logits_out=out)
+            alone.append(out.reshape(-1).float().cpu())
+        got = rec.seen[r.id]
+        assert len(got) == len(alone) == len(r.tokens)
+        # the prefill logits are the same computation in both runs
+        assert torch.equal(got[0], alone[0])
+        for g, a in zip(got[1:], alone[1:]):
+            close(g.numpy()[None], a.numpy()[None], STEP_TOL)
+        for g, tok in zip(got, r.tokens):
+            assert int(torch.argmax(g)) == tok
+    decode.clear_contexts()
