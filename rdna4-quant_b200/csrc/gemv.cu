@@ -468,6 +468,14 @@ int launch_gemv(const GemvArgs& a, int fmt) {
     const char* e = getenv("R4Q_GEMV_PATH");
     return e && e[0] == 'l';
   }();
+  // R4Q_GEMV_TC=1: INT4 at B = 3..16 through the tcgen05 kernel (weights
+  // dequantised into tensor memory; measured slower than the TMA kernel, so
+  // opt-in); it declines (capacity) when the workspace cannot hold its
+  // prepared activations, and takes no tensor-parallel exchange.
+  if (!force_ldg && gemv_tc_eligible(a, fmt)) {
+    st = launch_gemv_tc(a);
+    if (st != R4Q_ERR_CAPACITY) return st;
+  }
   if (!force_ldg && gemv_tma_supported(a, fmt)) {
     st = launch_gemv_tma(a, fmt);
     if (st != R4Q_ERR_CAPACITY) return st;  // no TMA plan fits: take the LDG kernel
@@ -489,7 +497,6 @@ int launch_gemv(const GemvArgs& a, int fmt) {
 using namespace r4q;
 
 extern "C" size_t r4q_gemv_workspace_bytes(int B, int N, int K) {
-  (void)K;
   if (B < 1) B = 1;
   if (N < 16) N = 16;
   // enough partial slots for the K splits the planners pick (they cap the
@@ -497,7 +504,7 @@ extern "C" size_t r4q_gemv_workspace_bytes(int B, int N, int K) {
   long cap = ((long)num_sms() * 64 * 8 + N - 1) / N;
   if (cap < kMaxSplit) cap = kMaxSplit;
   if (cap > 32) cap = 32;
-  return gemv_ws_bytes_for(B, N, (int)cap);
+  return gemv_ws_bytes_for(B, N, (int)cap) + (B >= 3 ? gemv_tc_extra_bytes(B, K < 128 ? 128 : K) : 0);
 }
 
 static GemvArgs mk(const void* x, long ldx, const void* w, const void* s, void* y, long ldy, int B,

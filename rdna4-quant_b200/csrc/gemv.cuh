@@ -55,5 +55,11 @@ int gemv_validate(const GemvArgs& a, int fmt);
 int launch_gemv(const GemvArgs& a, int fmt);
 bool gemv_tma_supported(const GemvArgs& a, int fmt);
 int launch_gemv_tma(const GemvArgs& a, int fmt);
+// tcgen05 GEMV for INT4 at B = 3..16 (gemv_tc.cu): eligibility, launch
+// (R4Q_ERR_CAPACITY without an error message when the workspace is too small),
+// and the workspace bytes it needs beyond the split-K partials.
+bool gemv_tc_eligible(const GemvArgs& a, int fmt);
+int launch_gemv_tc(const GemvArgs& a);
+size_t gemv_tc_extra_bytes(int B, int K);
 
 }  // namespace r4q

@@ -129,17 +129,19 @@ def test_gemv_workspace_left_zero_and_repeatable(ops):
     ops.check_status(x.device)              # no wait gave up
 
 
-def test_gemv_timeout_is_reported_and_context_survives(ops):
+@pytest.mark.parametrize("B", [1, 4])
+def test_gemv_timeout_is_reported_and_context_survives(ops, B):
     """A bounded mbarrier wait that runs out (the poll limit lowered to a few
     polls, so the TMA stages cannot land in time) must not hang or fault: the
     kernel records the timeout in the workspace status word, drains its
-    in-flight copies and exits; check_status raises R4Q_ERR_TIMEOUT; the next
-    call with the normal limit is correct again."""
+    in-flight copies (and, in the tensor-memory kernel taken at B = 4, its
+    MMAs) and exits; check_status raises R4Q_ERR_TIMEOUT; the next call with
+    the normal limit is correct again."""
     from r4q import lib as L
     rng = np.random.default_rng(11)
     N, K = 7168, 5120                       # TMA path, several stages per CTA
     packed, sz = make_int4(rng, N, K)
-    x = cuda(rng.standard_normal((1, K)).astype(np.float16))
+    x = cuda(rng.standard_normal((B, K)).astype(np.float16))
     w, s = cuda(packed), cuda(sz)
     ref = O.gemv_int4(x.cpu().numpy(), packed, sz)
     ops.check_status(x.device)
@@ -290,6 +292,48 @@ close(y, ref)
 print('ok')
 """
     env = dict(os.environ, R4Q_GEMV_PATH="ldg")
+    r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True,
+                       cwd=str(Path(__file__).parent))
+    assert r.returncode == 0 and "ok" in r.stdout, r.stdout + r.stderr
+
+
+@pytest.mark.parametrize("B,N,K,pro", [(4, 5120, 5120, "fwht"), (16, 1024, 17408, "silu_fwht"),
+                                       (9, 4096, 2048, "rmsnorm_fwht")])
+def test_tensor_memory_gemv_forced(B, N, K, pro):
+    """The opt-in tcgen05 GEMV (R4Q_GEMV_TC=1: weights dequantised into tensor
+    memory, activations prepared once by a prologue pass) meets the bar on the
+    same data as the default kernel, with each prologue, split-K or not;
+    forced in a subprocess."""
+    import os
+    import subprocess
+    import sys
+    from pathlib import Path
+    code = f"""
+import sys, numpy as np, torch
+sys.path[:0] = {[str(p) for p in sys.path[:4]]!r}
+import r4q_oracle as O
+from test_gpu_gemv import close, cuda, make_int4
+from r4q import ops, lib as L
+rng = np.random.default_rng(7)
+B, N, K = {B}, {N}, {K}
+p, s = make_int4(rng, N, K)
+kin = 2 * K if '{pro}' == 'silu_fwht' else K
+x = rng.standard_normal((B, kin)).astype(np.float16)
+if '{pro}' == 'fwht':
+    xin = O.fwht32(x.astype(np.float32)).astype(np.float16)
+    y = ops.gemv('int4', cuda(x), cuda(p), cuda(s), N, K, prologue=L.PRO_FWHT)
+elif '{pro}' == 'silu_fwht':
+    xin = O.silu_fwht(x[:, :K], x[:, K:])
+    y = ops.gemv('int4', cuda(x), cuda(p), cuda(s), N, K, prologue=L.PRO_SILU_FWHT)
+else:
+    w = (1 + 0.1 * rng.standard_normal(K)).astype(np.float16)
+    xin = O.rmsnorm_fwht(x, w, 1e-6)
+    y = ops.gemv('int4', cuda(x), cuda(p), cuda(s), N, K, prologue=L.PRO_RMSNORM_FWHT, norm_w=cuda(w), eps=1e-6)
+close(y.cpu().numpy(), O.gemv_int4(xin, p, s))
+ops.check_status(y.device)
+print('ok')
+"""
+    env = dict(os.environ, R4Q_GEMV_TC="1")
     r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True,
                        cwd=str(Path(__file__).parent))
     assert r.returncode == 0 and "ok" in r.stdout, r.stdout + r.stderr
