@@ -5,22 +5,27 @@
 // and call rocBLAS (int4_prefill_logits, :2127-2320; int4_engine_v5.py:
 // 214-266):  Y[M, N] = X[M, K] · W[N, K]ᵀ, fp16 in, fp32 accumulate, fp16 out.
 //
-// B200 design (one 128 x 256 output tile per CTA, 8 warps):
-//  * warp 0, one lane: TMA producer.  X tiles [128 x 64] and W tiles
-//    [256 x 64] (fp16, K-major, 128-byte swizzle) into a 3-stage ring with
-//    mbarrier transaction counts;
-//  * INT4 weights (`w4` set): warps 2-7 dequantise instead of TMA-loading W:
+// B200 design (one 128 x 256 output tile per CTA, 16 warps):
+//  * warp 0, one lane: TMA producer.  X tiles [128 x 64] (4-stage ring) and
+//    W tiles [256 x 64] (3-stage ring; fp16, K-major, 128-byte swizzle) with
+//    mbarrier transaction counts; the activation ring is deeper so that the
+//    L2 latency of the X tiles does not throttle the MMAs;
+//  * INT4 weights (`w4` set): warps 2-15 dequantise instead of TMA-loading W
+//    (fourteen warps: with six the dequantisation, not the MMA, set the pace):
 //    the nibbles come in by TMA, the (scale, zero) pairs by the producer warp's
-//    cp.async (8 bytes per row and stage, below TMA's 16-byte box minimum) into
-//    the same stage, completing on the same mbarrier; the exact reference value
-//    fp16((q - z) · s) is written into the same swizzled fp16 layout, then
-//    fence.proxy.async makes it visible to the tensor cores;
+//    cp.async (8 bytes per row and stage, below TMA's 16-byte box minimum),
+//    both completing on one mbarrier, in a ring of their own six stages deep
+//    (refilled as soon as the dequantisers have read a slot, so the HBM
+//    latency of the weights hides behind six stages of MMAs); the exact
+//    reference value fp16((q - z) · s) is written into the swizzled fp16 slot
+//    of the MMA ring, then fence.proxy.async makes it visible to the tensor
+//    cores;
 //  * warp 1, one lane: issues tcgen05.mma.cta_group::1.kind::f16 (M = 128,
 //    N = 256, K = 16 per instruction, 4 per stage) from shared-memory matrix
 //    descriptors into a 128 x 256 fp32 accumulator in tensor memory, and
 //    tcgen05.commit releases each stage back to the producer;
-//  * all 8 warps: epilogue, tcgen05.ld of their 32 accumulator lanes (= rows)
-//    and half of the columns, fp16 conversion, stores.
+//  * all 16 warps: epilogue, tcgen05.ld of their 32 accumulator lanes (= rows)
+//    and a quarter of the columns, fp16 conversion, stores.
 // Decode-sized M (few output tiles): the K range is split over gridDim.z so
 // the grid covers the SMs; each split writes an fp32 partial and the tile's
 // last CTA to arrive sums them in split order (deterministic).
@@ -37,12 +42,14 @@ namespace r4q {
 namespace {
 
 constexpr int kBM = 128, kBN = 256, kBK = 64;
-constexpr int kStages = 3;
+constexpr int kStages = 3;                         // W (fp16) ring: TMA-filled, or the dequantisers' target
+constexpr int kXS = 4;                             // activation ring (A operand), deeper than the W ring
+constexpr int kNW = 5;                             // INT4: nibble/pair ring (runs ahead of the MMAs)
 constexpr int kABytes = kBM * kBK * 2;             // 16 KB
 constexpr int kBBytes = kBN * kBK * 2;             // 32 KB
 constexpr int kW4Bytes = kBN * kBK / 2;            // 8 KB of nibbles per stage
 constexpr int kPairBytes = kBN * 8;                // (scale, zero) of 2 blocks per row per stage
-constexpr int kGemmThreads = 256;   // 8 warps
+constexpr int kGemmThreads = 512;   // 16 warps: producer, MMA issuer, 14 dequantisers (INT4)
 constexpr int kDequantThreads = kGemmThreads - 64;
 constexpr long kGemmSpin = 1L << 26;
 
@@ -166,14 +173,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                    const GemmParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sa = smem;                                        // [stage][16 KB]
-  uint8_t* sb = sa + kStages * kABytes;                      // [stage][32 KB] fp16 W
-  uint8_t* sw4 = sb + kStages * kBBytes;                     // [stage][8 KB]  INT4 nibbles
-  uint8_t* spr = sw4 + kStages * kW4Bytes;                   // [stage][2 KB]  INT4 (scale, zero) pairs
-  uint64_t* full = reinterpret_cast<uint64_t*>(spr + kStages * kPairBytes);
-  uint64_t* empty = full + kStages;
-  uint64_t* w4full = empty + kStages;                        // INT4 bytes landed
-  uint64_t* bready = w4full + kStages;                       // dequantised W ready
+  uint8_t* sa = smem;                                        // [kXS][16 KB] activations
+  uint8_t* sb = sa + kXS * kABytes;                          // [kStages][32 KB] fp16 W
+  uint8_t* sw4 = sb + kStages * kBBytes;                     // [kNW][8 KB]  INT4 nibbles
+  uint8_t* spr = sw4 + kNW * kW4Bytes;                       // [kNW][2 KB]  INT4 (scale, zero) pairs
+  uint64_t* xfull = reinterpret_cast<uint64_t*>(spr + kNW * kPairBytes);  // [kXS]
+  uint64_t* xempty = xfull + kXS;                            // [kXS] MMA commit
+  uint64_t* full = xempty + kXS;                             // [kStages] fp16 W landed (TMA)
+  uint64_t* empty = full + kStages;                          // [kStages] MMA commit
+  uint64_t* w4full = empty + kStages;                        // [kNW] INT4 bytes landed
+  uint64_t* w4empty = w4full + kNW;                          // [kNW] INT4 bytes read by the dequantisers
+  uint64_t* bready = w4empty + kNW;                          // [kStages] dequantised W ready
   uint64_t* accum = bready + kStages;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
   int& s_last = *reinterpret_cast<int*>(tmem_slot + 1);      // split-K: this CTA merges
@@ -185,11 +195,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const int kt0 = (int)((long)kz * KTT / p.splits), KT = (int)((long)(kz + 1) * KTT / p.splits) - kt0;
 
   if (tid == 0) {
+    for (int s = 0; s < kXS; ++s) {
+      g_mbar_init(&xfull[s], 1);
+      g_mbar_init(&xempty[s], 1);
+    }
     for (int s = 0; s < kStages; ++s) {
       g_mbar_init(&full[s], 1);
       g_mbar_init(&empty[s], 1);
-      g_mbar_init(&w4full[s], p.w4 ? 33 : 1);    // INT4: TMA arrival + 32 lanes' cp.async
       g_mbar_init(&bready[s], kDequantThreads);
+    }
+    for (int s = 0; s < kNW; ++s) {
+      g_mbar_init(&w4full[s], 33);               // TMA arrival + 32 lanes' cp.async
+      g_mbar_init(&w4empty[s], kDequantThreads / 32);
     }
     g_mbar_init(accum, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -209,60 +226,83 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     //      the stage's (scale, zero) pairs (8 bytes per row, below TMA's
     //      16-byte box minimum) with cp.async, whose completion arrives on
     //      the same mbarrier as the nibbles
+    // Three rings: activations (kXS deep), fp16 W (kStages; TMA-filled, or
+    // written by the dequantisers), and for INT4 the nibbles and (scale,
+    // zero) pairs of stage j in slot j % kNW, kNW stages ahead of the MMAs
+    // (refilled as soon as the dequantisers have read a slot).
+    auto issue_w4 = [&](int j) {
+      const int n = j % kNW, kt = kt0 + j;
+      if (lane == 0) {
+        g_expect_tx(&w4full[n], kW4Bytes);
+        g_tma2d(sw4 + n * kW4Bytes, &tmb, kt * (kBK / 2), n0, &w4full[n]);
+      }
+      for (int r = lane; r < kBN; r += 32) {
+        const bool in = n0 + r < p.N;
+        const uint8_t* src = p.sz + (in ? (long)(n0 + r) * (p.K / 8) + kt * 8 : 0);
+        asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;" ::"r"(sm_u32(spr + n * kPairBytes + r * 8)),
+                     "l"(src), "r"(in ? 8 : 0) : "memory");
+      }
+      asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(sm_u32(&w4full[n])) : "memory");
+    };
     bool ok = true;
+    if (p.w4)
+      for (int j = 0; j < KT && j < kNW; ++j) issue_w4(j);
     for (int i = 0; i < KT && ok; ++i) {                // i: stage of this CTA's K range
-      const int s = i % kStages, kt = kt0 + i;
-      if (i >= kStages) ok = g_wait(&empty[s], ((i / kStages) - 1) & 1, p.status);
+      const int kt = kt0 + i, xs = i % kXS, s = i % kStages;
+      // activations: kXS stages ahead of the MMAs
+      if (i >= kXS) ok = g_wait(&xempty[xs], ((i / kXS) - 1) & 1, p.status);
       if (!ok) break;
+      if (lane == 0) {
+        g_expect_tx(&xfull[xs], kABytes);
+        g_tma2d(sa + xs * kABytes, &tma, kt * kBK, m0, &xfull[xs]);
+      }
       if (p.w4) {
+        // refill the nibble slot stage i - 1 used, for stage i - 1 + kNW
+        const int j = i - 1 + kNW;
+        if (i >= 1 && j < KT) {
+          ok = g_wait(&w4empty[(i - 1) % kNW], ((i - 1) / kNW) & 1, p.status);
+          if (!ok) break;
+          issue_w4(j);
+        }
+      } else {
+        if (i >= kStages) ok = g_wait(&empty[s], ((i / kStages) - 1) & 1, p.status);
+        if (!ok) break;
         if (lane == 0) {
-          g_expect_tx(&full[s], kABytes);
-          g_tma2d(sa + s * kABytes, &tma, kt * kBK, m0, &full[s]);
-          g_expect_tx(&w4full[s], kW4Bytes);
-          g_tma2d(sw4 + s * kW4Bytes, &tmb, kt * (kBK / 2), n0, &w4full[s]);
+          g_expect_tx(&full[s], kBBytes);
+          g_tma2d(sb + s * kBBytes, &tmb, kt * kBK, n0, &full[s]);
         }
-        for (int r = lane; r < kBN; r += 32) {
-          const bool in = n0 + r < p.N;
-          const uint8_t* src = p.sz + (in ? (long)(n0 + r) * (p.K / 8) + kt * 8 : 0);
-          asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;" ::"r"(sm_u32(spr + s * kPairBytes + r * 8)),
-                       "l"(src), "r"(in ? 8 : 0) : "memory");
-        }
-        asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(sm_u32(&w4full[s])) : "memory");
-      } else if (lane == 0) {
-        g_expect_tx(&full[s], kABytes + kBBytes);
-        g_tma2d(sa + s * kABytes, &tma, kt * kBK, m0, &full[s]);
-        g_tma2d(sb + s * kBBytes, &tmb, kt * kBK, n0, &full[s]);
       }
     }
   } else if (warp == 1 && lane == 0) {
     // ---- MMA issuer
     bool ok = true;
     for (int i = 0; i < KT; ++i) {
-      const int s = i % kStages;
-      const unsigned ph = (i / kStages) & 1;
-      if (ok) ok = g_wait(&full[s], ph, p.status);
-      if (ok && p.w4) ok = g_wait(&bready[s], ph, p.status);
+      const int s = i % kStages, xs = i % kXS;
+      if (ok) ok = g_wait(&xfull[xs], (i / kXS) & 1, p.status);
+      if (ok) ok = g_wait(p.w4 ? &bready[s] : &full[s], (i / kStages) & 1, p.status);
       asm volatile("tcgen05.fence::after_thread_sync;");
       if (ok) {
-        const uint32_t a0 = sm_u32(sa + s * kABytes), b0 = sm_u32(sb + s * kBBytes);
+        const uint32_t a0 = sm_u32(sa + xs * kABytes), b0 = sm_u32(sb + s * kBBytes);
 #pragma unroll
         for (int kk = 0; kk < kBK / 16; ++kk)
           umma_f16(tmem, sw128_desc(a0 + kk * 32), sw128_desc(b0 + kk * 32), (i | kk) ? 1u : 0u);
       }
-      umma_commit(&empty[s]);               // the stage is free once these MMAs have read it
+      umma_commit(&xempty[xs]);             // the slots are free once these MMAs have read them
+      umma_commit(&empty[s]);
     }
     umma_commit(accum);
   } else if (warp >= 2 && p.w4) {
-    // ---- INT4 dequantisers (warps 2-7)
+    // ---- INT4 dequantisers (warps 2-15)
     const int t = tid - 64;
     bool ok = true;
     for (int i = 0; i < KT; ++i) {
-      const int s = i % kStages;
-      const unsigned ph = (i / kStages) & 1;
-      if (ok) ok = g_wait(&w4full[s], ph, p.status);
+      const int s = i % kStages, n = i % kNW;
+      if (ok) ok = g_wait(&w4full[n], (i / kNW) & 1, p.status);
       // the fp16 slot was last read by the MMAs of stage i - kStages
       if (ok && i >= kStages) ok = g_wait(&empty[s], ((i / kStages) - 1) & 1, p.status);
-      if (ok) dequant_stage(sw4 + s * kW4Bytes, spr + s * kPairBytes, sb + s * kBBytes, t, kDequantThreads);
+      if (ok) dequant_stage(sw4 + n * kW4Bytes, spr + n * kPairBytes, sb + s * kBBytes, t, kDequantThreads);
+      __syncwarp();
+      if (lane == 0) g_arrive(&w4empty[n]);             // nibble slot n may be refilled
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       g_arrive(&bready[s]);
     }
@@ -273,10 +313,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   __syncwarp();
   const bool ok = g_wait(accum, 0, p.status);
   asm volatile("tcgen05.fence::after_thread_sync;");
+  constexpr int kColGroups = kGemmThreads / 128;             // warps sharing a lane quarter
   const int quarter = warp & 3, half = warp >> 2;
   const int row = m0 + quarter * 32 + lane;
 #pragma unroll 1
-  for (int c0 = half * (kBN / 2); c0 < (half + 1) * (kBN / 2); c0 += 32) {
+  for (int c0 = half * (kBN / kColGroups); c0 < (half + 1) * (kBN / kColGroups); c0 += 32) {
     uint32_t v[32];
     const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)c0;
     asm volatile(
@@ -395,7 +436,8 @@ int map2d(CUtensorMap* m, const void* base, CUtensorMapDataType dt, int esize, l
 }
 
 size_t gemm_smem() {
-  return 1024 + (size_t)kStages * (kABytes + kBBytes + kW4Bytes + kPairBytes) + (4 * kStages + 1) * 8 + 16;
+  return 1024 + (size_t)kXS * kABytes + (size_t)kStages * kBBytes + (size_t)kNW * (kW4Bytes + kPairBytes) +
+         (2 * kXS + 3 * kStages + 2 * kNW + 1) * 8 + 16;
 }
 
 // Workspace: status word at 0, tile counters from byte 256 (split grids have
