@@ -391,7 +391,7 @@ def cpu_set_run(setup):
     return nbytes, time.perf_counter() - t0
 
 
-def cpu_attention_run(B, ctx, reps_s=3.0):
+def cpu_attention_run(B, ctx, reps_s=3.0, heads=None, kv_heads=None):
     """fp32 softmax attention over a dequantised FP8 cache (the reference
     codec's decode as a 256-entry table, int4_decode_step.hip:71-81) for one
     (B, ctx) of config 2, in torch on every intra-op thread.  Returns (cache
@@ -403,7 +403,7 @@ def cpu_attention_run(B, ctx, reps_s=3.0):
     import r4q_oracle as O
     lut = torch.from_numpy(O.fp8_decode(np.arange(256, dtype=np.uint8)))
     g = torch.Generator().manual_seed(1)
-    H, Hk, D = NQ, NKV, HD
+    H, Hk, D = heads or NQ, kv_heads or NKV, HD
     kc = torch.randint(0, 256, (B, Hk, ctx, D), generator=g, dtype=torch.uint8) & 0xF7
     vc = torch.randint(0, 256, (B, Hk, ctx, D), generator=g, dtype=torch.uint8) & 0xF7
     q = torch.randn(B, H, D, generator=g)
@@ -454,7 +454,60 @@ def cpu_baselines(a, B):
     base["decode"] = {"ctx": 2048, "tok_s": round(1e3 / tok_ms, 4), "ms_per_token": round(tok_ms, 1),
                       "kind": "port", "sample": "extrapolated: 40 x (one INT4 layer's GEMV set + attention "
                                                 "at ctx 2048) + fp16 lm_head, batch 1"}
+    base["moe"] = cpu_moe_token()
     return base
+
+
+def cpu_moe_token():
+    """Config 4 on the host, batch 1: one MoE layer (INT4 qkv and o through the
+    reference's dequant math + fp32 matmul, attention at ctx 2048 over the
+    decoded FP8 cache, fp32 router + top-8 softmax, the 8 chosen experts'
+    gate_up / SiLU / down) timed once and extrapolated to 48 layers + the fp16
+    lm_head."""
+    import torch
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import r4q_oracle as O
+    from r4q import moe
+    cfg = moe.qwen3_30b_a3b_config()
+    D, E, Ie, k = cfg['hidden'], cfg['experts'], cfg['expert_inter'], cfg['topk']
+    qkv_n = (cfg['num_heads'] + 2 * cfg['num_kv_heads']) * cfg['head_dim']
+    g = torch.Generator().manual_seed(4)
+
+    def int4(N, K):
+        return (torch.randint(0, 256, (N, K // 2), generator=g, dtype=torch.uint8),
+                (torch.rand(N, K // 32, generator=g) * 0.01 + 1e-3).half(),
+                torch.randint(0, 16, (N, K // 32), generator=g, dtype=torch.uint8))
+
+    qkv, o = int4(qkv_n, D), int4(D, cfg['num_heads'] * cfg['head_dim'])
+    router = torch.randn(E, D, generator=g).half()
+    experts = [(int4(2 * Ie, D), int4(D, Ie)) for _ in range(k)]
+    lm = torch.randn(cfg['vocab'], D, generator=g).half()
+    x = torch.randn(1, D, generator=g).half()
+
+    def lin(w, v):
+        return (v.float() @ O.dequant_int4_torch(*w).float().t()).half()
+
+    t0 = time.perf_counter()
+    lin(qkv, x)
+    lin(o, torch.randn(1, cfg['num_heads'] * cfg['head_dim'], generator=g).half())
+    logits = x.float() @ router.float().t()
+    p = torch.softmax(logits, -1)
+    top = torch.topk(p, k, -1)
+    wts = top.values / top.values.sum(-1, keepdim=True)
+    y = torch.zeros(1, D)
+    for j, (gu, dn) in enumerate(experts):
+        h = lin(gu, x).float()
+        act = (torch.nn.functional.silu(h[:, :Ie]) * h[:, Ie:]).half()
+        y += wts[0, j] * lin(dn, act).float()
+    t_layer = time.perf_counter() - t0
+    _, t_att = cpu_attention_run(1, 2048, heads=cfg['num_heads'], kv_heads=cfg['num_kv_heads'])
+    t0 = time.perf_counter()
+    (x.float() @ lm.float().t()).half()
+    t_lm = time.perf_counter() - t0
+    tok_ms = (cfg['num_layers'] * (t_layer + t_att) + t_lm) * 1e3
+    return {"ctx": 2048, "tok_s": round(1e3 / tok_ms, 4), "ms_per_token": round(tok_ms, 1), "kind": "port",
+            "sample": "extrapolated: 48 x (one MoE layer: INT4 qkv/o, attention at ctx 2048, router + top-8, "
+                      "8 INT4 experts) + fp16 lm_head, batch 1"}
 
 
 def main_ours(a):
