@@ -79,6 +79,8 @@ def parse():
                     help="extra batch sizes of the GEMV set (config 1 names B = 1, 4, 16); '' skips")
     ap.add_argument("--moe-probe", type=int, default=0,
                     help="ncu target: 3 eager MoE decode steps of a 2-layer config-4 model at this batch")
+    ap.add_argument("--gemm-shapes", action="store_true",
+                    help="time the tcgen05 INT4 GEMM on the four layer shapes at M = 512 and 2048 (CUDA events)")
     ap.add_argument("--gemm-probe", action="store_true",
                     help="run the INT4 tcgen05 prefill GEMM (M=512, qkv shape) 4 times and exit (for ncu)")
     ap.add_argument("--kernel-probe", default=None, choices=[n for n, *_ in LAYER_SHAPES],
@@ -1018,9 +1020,40 @@ def gemm_probe(a):
     print("gemm probe ok")
 
 
+def gemm_shapes(a):
+    """TFLOP/s of r4q.ops.gemm (INT4 weights dequantised in the tcgen05 GEMM)
+    for the Qwen3-14B layer shapes at M = 512 and 2048, CUDA events over 10
+    launches after 3 warm-ups; one JSON line."""
+    import torch
+    from r4q import ops, synth
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(0)
+    res = []
+    for M in (512, 2048):
+        for name, N, K, _ in LAYER_SHAPES:
+            _, w, sc = synth.linear_int4(N, K, g, dev)
+            x = torch.randn(M, K, device=dev, generator=g).half()
+            for _ in range(3):
+                ops.gemm(x, w, sc, N)
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(10):
+                ops.gemm(x, w, sc, N)
+            e1.record()
+            torch.cuda.synchronize()
+            ms = e0.elapsed_time(e1) / 10
+            res.append({"M": M, "shape": f"{name}:{K}->{N}", "us": round(ms * 1e3, 1),
+                        "TFLOPs": round(2 * M * N * K / ms / 1e9, 1)})
+            del w, sc, x
+    print(json.dumps({"gemm_shapes": res}))
+
+
 if __name__ == "__main__":
     args = parse()
-    if args.gemm_probe:
+    if args.gemm_shapes:
+        gemm_shapes(args)
+    elif args.gemm_probe:
         gemm_probe(args)
     elif args.decode_probe:
         decode_probe(args)
