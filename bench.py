@@ -46,9 +46,9 @@ LAYER_SHAPES = [  # (name, N, K, prologue)
 ]
 METRIC = "INT4 GEMV HBM GB/s (Qwen3-14B decode-layer GEMV set)"
 # dram__bytes_read.sum + dram__bytes_write.sum of one gate_up launch at B=1
-# (gemv_tma_kernel), from the ncu capture summarised in
-# profiles/gemv_tma_int4_gate_up_b1.md
-TRAFFIC_GATE_UP_B1 = None
+# with the RMSNorm+FWHT prologue (gemv_tma_kernel), from the ncu capture
+# summarised in profiles/gemv_tma_int4_gate_up_b1.md
+TRAFFIC_GATE_UP_B1 = 111495680 + 2992128
 L2_BYTES = 126 * 1024 * 1024
 
 
@@ -85,6 +85,8 @@ def parse():
                     help="run the INT4 tcgen05 prefill GEMM (M=512, qkv shape) 4 times and exit (for ncu)")
     ap.add_argument("--kernel-probe", default=None, choices=[n for n, *_ in LAYER_SHAPES],
                     help="run one GEMV of this shape 4 times and exit (for ncu captures)")
+    ap.add_argument("--probe-pro", default=None, choices=["fwht", "silu_fwht", "rmsnorm_fwht"],
+                    help="prologue of --kernel-probe (default: the shape's own)")
     ap.add_argument("--probe-fmt", default="int4", choices=["int4", "int8"],
                     help="weight format of --kernel-probe")
     ap.add_argument("--attn-probe", default=None,
@@ -950,11 +952,13 @@ def kernel_probe(a):
     g = torch.Generator(device=dev).manual_seed(0)
     mk = synth.linear_int8 if a.probe_fmt == "int8" else synth.linear_int4
     _, w, sc = mk(N, K, g, dev)
+    pro = a.probe_pro or pro
     kin = 2 * K if pro == "silu_fwht" else K
     x = torch.randn(a.batch, kin, device=dev, generator=g).half()
-    prol = Lb.PRO_SILU_FWHT if pro == "silu_fwht" else Lb.PRO_FWHT
+    prol = {"fwht": Lb.PRO_FWHT, "silu_fwht": Lb.PRO_SILU_FWHT, "rmsnorm_fwht": Lb.PRO_RMSNORM_FWHT}[pro]
+    nw = (1 + 0.01 * torch.randn(K, device=dev, generator=g)).half() if pro == "rmsnorm_fwht" else None
     for _ in range(4):
-        ops.gemv(a.probe_fmt, x, w, sc, N, K, prologue=prol)
+        ops.gemv(a.probe_fmt, x, w, sc, N, K, prologue=prol, norm_w=nw)
     torch.cuda.synchronize()
     ops.check_status(dev)
     print(f"probe {name} {a.probe_fmt} N={N} K={K} B={a.batch} ok")
