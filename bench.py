@@ -670,6 +670,9 @@ def main_ours(a):
         del layers
         torch.cuda.empty_cache()
         line["decode"] = decode_tok_s(a, dev, peak, ws, rank)
+        if ws == 1:
+            torch.cuda.empty_cache()
+            line["serve"] = serve_tok_s(a, dev)
     if a.moe_batches and not a.no_extra:
         torch.cuda.empty_cache()
         line["moe"] = moe_tok_s(a, dev, peak, ws, rank)
@@ -711,6 +714,37 @@ def main_reference(a):
             "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
+
+
+def serve_tok_s(a, dev):
+    """Continuous batching (r4q.serve) on the config-3 model: 32 greedy
+    requests (prompts of 128 seeded random ids, 64 new tokens each) through a
+    batch-16 engine; wall time of the whole run on the host (prefills, decode
+    steps, per-step sampling sync), generated tokens per second."""
+    import torch
+    from r4q import decode, serve, synth
+    cfg = synth.qwen3_14b_config()
+    nreq, plen, ntok, batch = 32, 128, 64, 16
+    m = synth.build_decode_model(cfg, dev, seed=3, max_seq=plen + ntok + 8, batch=batch)
+    be = serve.SlotBackend(m, cfg, batch=batch)
+    eng = serve.BatchedEngine(be)
+    g = torch.Generator().manual_seed(9)
+    prompts = [torch.randint(0, cfg['vocab'], (plen,), generator=g).tolist() for _ in range(nreq)]
+    w = eng.submit(prompts[0][:16], max_new_tokens=4)        # warm-up: graph capture, first prefill
+    eng.run()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    reqs = eng.generate(prompts, max_new_tokens=ntok)
+    torch.cuda.synchronize()
+    dt = time.perf_counter() - t0
+    gen = sum(len(r.tokens) for r in reqs)
+    out = {"model": "Qwen3-14B shape, random init", "batch_slots": batch, "requests": nreq, "prompt": plen,
+           "new_tokens": ntok, "steps": eng.steps, "seconds": round(dt, 3), "tok_s": round(gen / dt, 1),
+           "api": "r4q.serve.BatchedEngine (prefill into a free slot, r4q_decode_step_rows per step, "
+                  "argmax per row)", "timing": "host wall clock around the whole run"}
+    del eng, be, m, w
+    decode.clear_contexts()
+    return out
 
 
 def decode_tok_s(a, dev, peak, ws=1, rank=0):
