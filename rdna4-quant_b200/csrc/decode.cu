@@ -224,10 +224,21 @@ static PushSet push_slots(r4q_decode_ctx* c, int parity, bool ll) {
 
 // The consumer GEMV of an exchange reads the slots in its prologue (TMA path);
 // otherwise a reduce kernel materialises r first.
+// The consumer GEMV reads the exchange slots in its prologue (every CTA sums
+// all ranks' partials) up to 4 ranks; with more, every CTA would re-read
+// 8 x hidden tagged words per exchange, so one reduce kernel sums them once
+// and the GEMV takes the materialised residual (measured on 8 x B200:
+// decode fell below the 4-rank rate with the fused form).  R4Q_TP_FUSED=0 / 1
+// forces either form (measurement).
 static bool consumer_fused(r4q_decode_ctx* c, int fmt, const void* w, const void* s, int N) {
   GemvArgs probe{};
   probe.K = c->m.hidden; probe.N = N; probe.B = c->m.batch; probe.w = w; probe.s = s;
-  return gemv_tma_supported(probe, fmt) && !getenv_ldg();
+  static const int forced = [] {
+    const char* e = getenv("R4Q_TP_FUSED");
+    return e ? atoi(e) : -1;
+  }();
+  const bool by_size = forced >= 0 ? forced != 0 : c->m.tp_size <= 4;
+  return by_size && gemv_tma_supported(probe, fmt) && !getenv_ldg();
 }
 
 // A producer whose consumer is fused pushes tagged words (no fence, no flag,
