@@ -30,6 +30,7 @@ import statistics
 import subprocess
 import sys
 import tempfile
+import threading
 import time
 from pathlib import Path
 
@@ -125,7 +126,31 @@ class ClockSampler:
         self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
         self.p = None
 
+    def _poll(self):
+        # NVML read-only queries every 5 ms: a timed region of tens of ms gets
+        # several samples, where nvidia-smi's 200 ms loop may see none under load
+        import pynvml as nv
+        bits = [("hw_slowdown", nv.nvmlClocksEventReasonHwSlowdown),
+                ("hw_thermal_slowdown", nv.nvmlClocksEventReasonHwThermalSlowdown),
+                ("sw_thermal_slowdown", nv.nvmlClocksEventReasonSwThermalSlowdown),
+                ("sw_power_cap", nv.nvmlClocksEventReasonSwPowerCap)]
+        h = nv.nvmlDeviceGetHandleByIndex(self.index)
+        mx = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+        while not self.stop.is_set():
+            sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+            r = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+            self.nvml.append((sm, mx, [n for n, b in bits if r & b]))
+            self.stop.wait(0.005)
+
     def __enter__(self):
+        self.nvml, self.stop, self.thr = [], threading.Event(), None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.thr = threading.Thread(target=self._poll, daemon=True)
+            self.thr.start()
+        except Exception:
+            self.thr = None
         try:
             self.p = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
                                        "--format=csv,noheader,nounits", "-lms", "200"],
@@ -135,6 +160,9 @@ class ClockSampler:
         return self
 
     def __exit__(self, *a):
+        self.stop.set()
+        if self.thr is not None:
+            self.thr.join(timeout=5)
         if self.p is not None:
             self.p.terminate()
             try:
@@ -142,7 +170,16 @@ class ClockSampler:
             except Exception:
                 self.p.kill()
 
+    def begin(self):
+        """Drop the samples taken before the timed region starts."""
+        self.nvml.clear()
+
     def summary(self):
+        if self.nvml:
+            return {"sm_mhz": statistics.median(r[0] for r in self.nvml),
+                    "sm_max_mhz": max(r[1] for r in self.nvml),
+                    "reasons": sorted({n for r in self.nvml for n in r[2]}),
+                    "samples": len(self.nvml), "source": "NVML every 5 ms"}
         try:
             rows = [r.split(",") for r in Path(self.f.name).read_text().strip().splitlines()]
         except Exception:
@@ -550,6 +587,7 @@ def main_ours(a):
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clk:
         time.sleep(0.3)
+        clk.begin()
         with torch.cuda.stream(s):
             e0.record(s)
             for _ in range(a.steps):

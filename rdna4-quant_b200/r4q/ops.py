@@ -14,18 +14,25 @@ _ws_lock = threading.Lock()
 _ws: dict = {}
 
 
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def stream_handle(dev: torch.device) -> int:
+    """cudaStream_t of torch's current stream on dev (the raw-handle query
+    costs a fraction of building a torch.cuda.Stream object per call)."""
+    if _raw_stream is not None:
+        return _raw_stream(dev.index if dev.index is not None else torch.cuda.current_device())
     return torch.cuda.current_stream(dev).cuda_stream
 
 
 def _require_cuda(*ts: torch.Tensor) -> torch.device:
-    dev = ts[0].device
+    idx = ts[0].get_device()
     for t in ts:
         if not t.is_cuda:
             raise ValueError("r4q ops take CUDA tensors only (no CPU fallback)")
-        if t.device != dev:
+        if t.get_device() != idx:
             raise ValueError("all tensors must be on the same device")
-    return dev
+    return ts[0].device
 
 
 # Workspaces replaced by larger ones stay referenced: a CUDA graph captured
@@ -45,11 +52,14 @@ def _grown(cache: dict, key, need: int, minimum: int, dev) -> torch.Tensor:
     return cur
 
 
-def gemv_workspace(dev: torch.device, B: int, N: int, K: int) -> torch.Tensor:
+def gemv_workspace(dev: torch.device, B: int, N: int, K: int, stream: int | None = None) -> torch.Tensor:
     """Zero-filled workspace for GEMV split-K partials, cached per
     (device, stream).  The kernels leave it zeroed after every call."""
     need = int(L.LIB.r4q_gemv_workspace_bytes(B, N, K))
-    key = (dev.index, stream_handle(dev))
+    key = (dev.index, stream_handle(dev) if stream is None else stream)
+    cur = _ws.get(key)          # lock-free hit; replacement happens under the lock
+    if cur is not None and cur.numel() >= need:
+        return cur
     with _ws_lock:
         return _grown(_ws, key, need, 1 << 20, dev)
 
@@ -109,8 +119,8 @@ def gemv(fmt: str, x: torch.Tensor, w: torch.Tensor, s: torch.Tensor | None, N: 
         raise ValueError(f"x has {x2.shape[1]} columns, need {kin}")
     if out is None and out32 is None:
         out = torch.empty(B, N, dtype=torch.float16, device=dev)
-    ws = gemv_workspace(dev, B, N, K)
     st = stream_handle(dev)
+    ws = gemv_workspace(dev, B, N, K, st)
     ldx = x2.stride(0) if B > 1 else kin
     yt = out if out32 is None else out32
     ldy = yt.stride(0) if B > 1 else N
