@@ -466,31 +466,42 @@ static int cache_map(CUtensorMap* m, const void* base, long rows) {
   return R4Q_OK;
 }
 
-// CTAs per cluster: 8 (portable), 4 for short contexts (at most 16 tiles),
-// halved while the grid would exceed one wave (two CTAs per SM): with many
-// (row, kv head) pairs the work already fills the GPU and a wave of
-// clusters costs a whole CTA lifetime.  Measured on B200, B = 1, 8 kv heads,
-// 40 layers in a graph: clusters of 16 (non-portable) schedule badly (15 us
-// at ctx 2048 against 6.9 us for 8).  R4Q_ATTN_CLUSTER forces 1, 2, 4, 8 or
-// 16 (measurement only).
+static size_t attn_smem() {
+  return 1024 + (size_t)kAttnWarps * kAttnSlots * 2 * kTileBytes + (size_t)(kAttnWarps + 1) * 8 * 130 * 4 +
+         (size_t)8 * kAttnD * 2 + kAttnWarps * kAttnSlots * 8;
+}
+
+// CTAs per cluster: no more than gives every warp one 64-position tile (1, 2,
+// 4 or 8: at most 8, portable), then halved while the grid would exceed one
+// wave of resident CTAs (one per SM: the K/V rings take ~155 KB of shared
+// memory).  A second wave of clusters costs a whole CTA lifetime, more than the
+// longer split of a smaller cluster.  Measured on B200 (40 q / 8 kv heads, CUDA
+// graph over cache copies > L2), old rule (4 or 8, halved above two CTAs per SM)
+// -> this one: B = 4 ctx 2048 19.2 -> 9.6 us, B = 8 ctx 128 11.3 -> 5.5 us,
+// B = 16 ctx 128 10.9 -> 5.4 us, B = 16 ctx 2048 22.6 -> 16.7 us, B = 1
+// unchanged at ctx >= 2048; clusters of 16 (non-portable) schedule badly (15 us
+// at B = 1, ctx 2048, against 6.7 us for 8).  R4Q_ATTN_CLUSTER forces 1, 2, 4,
+// 8 or 16 (measurement only).
 static int attn_cluster(int B, int Hk, int max_tiles) {
   static const int forced = [] {
     const char* e = getenv("R4Q_ATTN_CLUSTER");
     return e ? atoi(e) : 0;
   }();
   if (forced == 1 || forced == 2 || forced == 4 || forced == 8 || forced == 16) return forced;
-  int dev = 0, sms = 148;
+  int dev = 0, sms = 148, per_sm = 0;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  int c = max_tiles <= 16 ? 4 : 8;
-  while (c > 1 && (long)B * Hk * c > 2L * sms) c >>= 1;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, attn_kernel, kAttnWarps * 32, attn_smem()) !=
+          cudaSuccess || per_sm < 1) {
+    cudaGetLastError();
+    per_sm = 1;
+  }
+  int c = 8;
+  while (c > 1 && (long)c * kAttnWarps / 2 >= max_tiles) c >>= 1;   // keep >= 1 tile per warp
+  while (c > 1 && (long)B * Hk * c > (long)per_sm * sms) c >>= 1;
   return c;
 }
 
-static size_t attn_smem() {
-  return 1024 + (size_t)kAttnWarps * kAttnSlots * 2 * kTileBytes + (size_t)(kAttnWarps + 1) * 8 * 130 * 4 +
-         (size_t)8 * kAttnD * 2 + kAttnWarps * kAttnSlots * 8;
-}
 
 constexpr size_t kAttnWsBytes = 256;   // status word only
 
