@@ -7,7 +7,7 @@
 // head) the query heads of its GQA group attend over positions [0, seq_len).
 //
 // B200 design:
-//  * one thread-block cluster of C CTAs (4 or 8) per (kv head, batch row),
+//  * one thread-block cluster of C CTAs (1, 2, 4 or 8: see attn_cluster) per (kv head, batch row),
 //    4 warps per CTA; the cluster's 4C warps take consecutive 64-position tiles
 //    round-robin, each streaming its K and V tiles (8 KB each) with TMA
 //    (128-byte swizzle) into a 2-slot ring and keeping an online softmax in
